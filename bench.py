@@ -1,0 +1,393 @@
+"""Benchmark of the CrossDiT attention hot path on B200 (libkd_attn).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kd|reference] [--config 1]
+
+Workload (default): BASELINE config 1 -- full 5 s clip self-attention, B2 (CFG cond +
+uncond) x 31,744 tokens (31x32x32 grid) x 32 heads x d128, RMS-normed Q/K with 3D RoPE
+(theta 1e4, axes 32/48/48), bf16 operands, fp32 accumulation, scale 1/sqrt(128).
+
+A step is one kd_attn_self_attention call on resident f32 Q/K/V projections
+([4096, L, 2] ggml layout, 3 x 1.04 GB > L2): the fused RMSNorm+RoPE+cast prologue
+for Q, K and V, then the tcgen05 flash-attention kernel.  value = dense-equivalent
+TFLOP/s = 4*B*H*L^2*d / step time.  With --gpus N > 1 the 32 heads are sharded
+over the ranks (8 heads x 4 GPUs, ...) and the step ends with kd_attn_allgather_heads
+(one NCCL all-gather + permute) -- strong scaling of the same job.
+
+e2e: the same call through the public API from pinned HOST buffers: H2D of the
+step's Q/K/V projections, the call, D2H of the bf16 output, per step.
+
+--impl reference: the reference's CPU algorithm (the oracle restatement of ggml's
+flash_attn_ext with the RMSNorm/RoPE prologue; ggml itself is not available here)
+on this host's cores, timed on a bounded slice of the same workload and scaled.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "kandinsky.cpp_b200"))
+
+METRIC = "attn TFLOP/s (dense-equiv) at 31744 tok x 32h x d128"
+UNIT = "TFLOP/s"
+
+CONFIGS = {
+    0: dict(name="cfg0 self-attn B1 L1280 (5x16x16) H32 d128, f32 Q / f16 K,V", N=1, grid=(5, 16, 16), H=32,
+            op="f16", out="f32"),
+    1: dict(name="cfg1 self-attn B2 L31744 (31x32x32) H32 d128 bf16", N=2, grid=(31, 32, 32), H=32, op="bf16",
+            out="bf16"),
+    3: dict(name="cfg3 self-attn B2 L71424 (31x48x48) H32 d128 bf16", N=2, grid=(31, 48, 48), H=32, op="bf16",
+            out="bf16"),
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops"), d.get("bf16_tflops_sustained"), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per FA launch from the committed ncu summary (None if absent)."""
+    p = os.path.join(ROOT, "profiles", "fmha_fwd_bf16_cfg1.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.lines:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def sample_rows_for_cpu(L, budget_flop, d=128):
+    """query rows of one (batch, head) pair so the CPU oracle does about budget_flop of work."""
+    per_row = 4.0 * L * d
+    return max(16, min(L, int(budget_flop / per_row)))
+
+
+def cpu_reference(cfg, seconds_target=15.0, threads=None):
+    """Time the CPU oracle (ggml-faithful flash_attn_ext + prologue) on a slice; returns a dict."""
+    import numpy as np
+
+    import oracle
+    threads = threads or os.cpu_count() or 1
+    os.environ["KD_ORACLE_THREADS"] = str(threads)
+    nt, nh, nw = cfg["grid"]
+    L = nt * nh * nw
+    d = 128
+    kv_type = oracle.F16 if cfg["op"] == "f16" else oracle.BF16
+    # calibrate on a small slice, then size the sample for ~seconds_target
+    q = oracle.philox_randn(11, L * d, 0).reshape(1, L, d)
+    k = oracle.philox_randn(11, L * d, 1).reshape(1, L, d)
+    v = oracle.philox_randn(11, L * d, 2).reshape(1, L, d)
+    tab = oracle.visual_rope_table(cfg["grid"])
+
+    def run(rows):
+        t0 = time.perf_counter()
+        qn = oracle.rope_apply(oracle.rms_norm_heads(q[:, :rows], d), 1, d, tab[:rows])
+        kn = oracle.rope_apply(oracle.rms_norm_heads(k, d), 1, d, tab)
+        k4 = oracle.to_type(kn[:, None], kv_type)
+        v4 = oracle.to_type(v[:, None], kv_type)
+        oracle.flash_attn_ext(qn[:, None], k4, v4, mode=oracle.GGML)
+        return time.perf_counter() - t0
+
+    r0 = max(16, min(L, 64))
+    t0 = run(r0)
+    rows = int(min(L, max(r0, r0 * seconds_target / max(t0, 1e-3))))
+    t = run(rows)
+    flop_sample = 4.0 * rows * L * d
+    full_flop = 4.0 * cfg["N"] * cfg["H"] * L * L * d
+    ms_full = t * 1e3 * full_flop / flop_sample
+    return {"value": flop_sample / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 (batch, head) pair x {rows} of {L} query rows (prologue + ggml-faithful flash_attn_ext), "
+                      f"{t:.1f} s; scaled by B*H*L/rows to {ms_full / 1e3:.0f} s per full call",
+            "ms_per_call_scaled": ms_full}
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    steps = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_reference(cfg, seconds_target=args.ref_seconds)
+        if i >= args.warmup:
+            steps.append(cb)
+    vals = [s["value"] for s in steps]
+    val = sum(vals) / len(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": steps[-1]["ms_per_call_scaled"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": cfg["op"],
+            "data": "synthetic (seeded Philox4x32-10 N(0,1), the reference's generator)",
+            "config": {"workload": cfg["name"], "global_batch": cfg["N"], "seq_len": L_of(cfg), "heads": cfg["H"],
+                       "head_dim": 128, "parallelism": "cpu", "l2": "n/a"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def L_of(cfg):
+    nt, nh, nw = cfg["grid"]
+    return nt * nh * nw
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="kd", choices=["kd", "reference"])
+    ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--ref-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import kd_attn
+
+    ws, rank, local = dist_setup()
+    if ws != args.gpus:
+        print(f"note: WORLD_SIZE={ws} but --gpus {args.gpus}; using WORLD_SIZE", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    N, H, d = cfg["N"], cfg["H"], 128
+    L = L_of(cfg)
+    assert H % ws == 0, "heads must divide over the ranks"
+    Hs = H // ws
+    Cs = Hs * d
+    op = kd_attn.BF16 if cfg["op"] == "bf16" else kd_attn.F16
+    out_dt = torch.bfloat16 if cfg["out"] == "bf16" else torch.float32
+
+    nccl_id = None
+    if ws > 1:
+        obj = [kd_attn.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    ctx = kd_attn.Context(device=local, n_ranks=ws, rank=rank, nccl_id=nccl_id)
+    stream = torch.cuda.current_stream()
+
+    # inputs: this rank's column shard (heads [rank*Hs, (rank+1)*Hs)) of the Q/K/V projections
+    def proj(offset):
+        t = torch.empty(N, L, Cs, device=dev)
+        full = torch.empty(N * L * Cs, device=dev)
+        ctx.fill_randn(full, seed=1 + rank, offset=offset)
+        t.copy_(full.view(N, L, Cs))
+        return t
+
+    q, k, v = proj(0), proj(1), proj(2)
+    rope = kd_attn.Rope3D.make(cfg["grid"])
+    out_shard = torch.empty(N, L, Cs, device=dev, dtype=out_dt)
+    out_full = torch.empty(N, L, H * d, device=dev, dtype=out_dt) if ws > 1 else out_shard
+
+    def step():
+        ctx.self_attention(q, k, v, Hs, out_shard, rope=rope, op_type=op, stream=stream)
+        if ws > 1:
+            ctx.allgather_heads(out_shard.view(N, L, Hs, d), out_full.view(N, L, H, d), stream=stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.device_status()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ctx.device_status()
+    t = torch.tensor([ms], device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flop = 4.0 * N * H * L * L * d
+    value = flop / (ms * 1e-3) / 1e12
+
+    # dominant kernel alone: flash attention on the bf16 operands the prologue produced
+    qs = torch.empty(N, Hs, L, d, device=dev, dtype=torch.bfloat16 if op == kd_attn.BF16 else torch.float16)
+    ks, vs = torch.empty_like(qs), torch.empty_like(qs)
+    ctx.prologue(q, Hs, qs, norm=True, rope=rope, stream=stream)
+    ctx.prologue(k, Hs, ks, norm=True, rope=rope, stream=stream)
+    ctx.prologue(v, Hs, vs, norm=False, stream=stream)
+    o4 = out_shard.view(N, L, Hs, d)
+    for _ in range(2):
+        ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream)
+    torch.cuda.synchronize()
+    fa0, fa1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fa0.record(stream)
+    for _ in range(args.steps):
+        ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream)
+    fa1.record(stream)
+    torch.cuda.synchronize()
+    fa_ms = fa0.elapsed_time(fa1) / args.steps
+    # prologue alone (HBM roofline): 3 launches reading f32, writing 16-bit
+    pr0, pr1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pr0.record(stream)
+    for _ in range(args.steps):
+        ctx.prologue(q, Hs, qs, norm=True, rope=rope, stream=stream)
+        ctx.prologue(k, Hs, ks, norm=True, rope=rope, stream=stream)
+        ctx.prologue(v, Hs, vs, norm=False, stream=stream)
+    pr1.record(stream)
+    torch.cuda.synchronize()
+    pro_ms = pr0.elapsed_time(pr1) / args.steps
+    del qs, ks, vs
+
+    # end to end from pinned host buffers through the public API
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(out_full.shape, dtype=out_dt).pin_memory()
+    e2e_steps = max(1, min(args.e2e_steps, args.steps))
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        step()
+        hout.copy_(out_full, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([e2e_ms], device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    h2d = 3 * N * L * Cs * 4
+    d2h = hout.numel() * hout.element_size()
+
+    pk, pk_sus, pk_kind = peaks()
+    fa_flop = 4.0 * N * Hs * L * L * d
+    fa_tflops = fa_flop / (fa_ms * 1e-3) / 1e12
+    traffic = profile_traffic()
+    if traffic is not None and ws > 1:
+        traffic = traffic / ws
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": cfg["op"],
+        "data": "synthetic: seeded Philox4x32-10 N(0,1) projections generated on the device",
+        "config": {"workload": cfg["name"], "global_batch": N, "seq_len": L, "heads": H, "head_dim": d,
+                   "parallelism": f"heads{ws}" if ws > 1 else "single",
+                   "step": "kd_attn_self_attention (RMSNorm+RoPE+cast prologue, tcgen05 flash attention)"
+                           + (" + allgather_heads" if ws > 1 else ""),
+                   "l2": "inputs larger than L2 (3 x f32 projections per rank)"},
+        "roofline": {"bound": "tensor", "achieved": fa_tflops, "peak": pk, "unit": "TFLOP/s",
+                     "frac": fa_tflops / pk if pk else None, "peak_kind": f"{pk_kind} burst bf16",
+                     "frac_of_sustained": fa_tflops / pk_sus if pk_sus else None,
+                     "traffic": traffic, "kernel": "fmha_fwd_kernel<bf16>", "kernel_ms": fa_ms},
+        "prologue": {"ms": pro_ms, "gbs": (3 * N * L * Cs * 4 + 3 * N * L * Cs * 2) / (pro_ms * 1e-3) / 1e9},
+        "e2e": {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps * (4 + (1 if ws > 1 else 0)),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        cb = cpu_reference(cfg, seconds_target=args.ref_seconds)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if ws > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

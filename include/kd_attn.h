@@ -1,0 +1,203 @@
+/*
+ * kd_attn.h -- C ABI of libkd_attn, the B200 (sm_100a) attention library
+ * behind kandinsky.cpp's CrossDiT attention.
+ *
+ * Drop-in boundary.  kandinsky.cpp routes both CrossDiT attention call sites
+ * through ops::attention (src/core/ops.hpp:107-207):
+ *   - DiTSelfAttention::forward  (src/models/crossdit.hpp:117-154; call at :150)
+ *   - DiTCrossAttention::forward (src/models/crossdit.hpp:174-200; call at :198)
+ * whose flash branch builds ggml_flash_attn_ext(q, k, v, mask, scale, 0, 0)
+ * (ops.hpp:176) with Q f32, K/V cast to f16 (ops.hpp:167-169), an optional f16
+ * mask, precision F32 (ops.hpp:177).  The entry points below replace that
+ * operator and the RMSNorm / RoPE graph ops in front of it.
+ *
+ * Conventions (mirroring include/kandinsky.h of the reference):
+ *   - every call returns a kd_attn_status; 0 is success, negative is an error
+ *     (kandinsky.h returns -1 / NULL on error, kandinsky.h:77-89);
+ *   - the caller owns every buffer passed in; the library never frees them;
+ *   - device pointers only in kd_tensor.data (except where noted), work is
+ *     enqueued on the given cudaStream_t (passed as void*), nothing blocks;
+ *   - a context may be used from one host thread at a time;
+ *   - there is no CPU fallback: shapes the kernels do not cover return
+ *     KD_ATTN_ERR_UNSUPPORTED and the caller keeps its own path;
+ *   - kd_tensor mirrors ggml_tensor's {type, ne[4], nb[4], data}, sizes in
+ *     elements with dim 0 fastest and strides in bytes, so a ggml tensor maps
+ *     onto it field by field.
+ */
+#ifndef KD_ATTN_H
+#define KD_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KD_ATTN_VERSION_MAJOR 0
+#define KD_ATTN_VERSION_MINOR 1
+
+typedef enum {
+    KD_ATTN_OK = 0,
+    KD_ATTN_ERR_INVALID_ARGUMENT = -1, /* null pointer, inconsistent shapes or strides */
+    KD_ATTN_ERR_UNSUPPORTED = -2,      /* valid for ggml but not covered here (e.g. head_dim != 128) */
+    KD_ATTN_ERR_CUDA = -3,             /* a CUDA runtime call failed; see kd_attn_last_error */
+    KD_ATTN_ERR_OUT_OF_MEMORY = -4,    /* context scratch could not grow */
+    KD_ATTN_ERR_DEVICE_TIMEOUT = -5,   /* a bounded device-side wait expired (kd_attn_device_status) */
+    KD_ATTN_ERR_NCCL = -6,             /* the head all-gather failed */
+} kd_attn_status;
+
+/* Same values and callback shape as kandinsky.h:12-19 (kd_log_level_t / kd_log_cb_t),
+ * so the host application's logger can be passed through unchanged. */
+typedef enum {
+    KD_ATTN_LOG_DEBUG = 0,
+    KD_ATTN_LOG_INFO = 1,
+    KD_ATTN_LOG_WARN = 2,
+    KD_ATTN_LOG_ERROR = 3,
+} kd_attn_log_level;
+typedef void (*kd_attn_log_cb)(kd_attn_log_level level, const char* text, void* user_data);
+
+/* ggml type ids (ggml.h: GGML_TYPE_F32 = 0, GGML_TYPE_F16 = 1, GGML_TYPE_BF16 = 30) */
+typedef enum {
+    KD_ATTN_TYPE_F32 = 0,
+    KD_ATTN_TYPE_F16 = 1,
+    KD_ATTN_TYPE_BF16 = 30,
+} kd_attn_type;
+
+typedef struct {
+    void* data;     /* device pointer */
+    int32_t type;   /* kd_attn_type */
+    int64_t ne[4];  /* sizes, dim 0 fastest (ggml ne) */
+    size_t nb[4];   /* strides in bytes (ggml nb) */
+} kd_tensor;
+
+/* 3D (t, h, w) rotary embedding of the visual tokens, computed on the fly
+ * (replaces rope::compute_visual_rope, src/rope.hpp:56-102, and the table
+ * upload at crossdit.hpp:562-565,601-602).  Token l of a sequence sits at
+ * t = l / (grid[1]*grid[2]), h = (l / grid[2]) % grid[1], w = l % grid[2]
+ * (rope.hpp:74).  Axis a rotates the pairs of its axes_dim[a] block with
+ * angle = pos_a * theta^(-i/(axes_dim[a]/2)) / scale_factor[a]. */
+typedef struct {
+    int32_t axes_dim[3];    /* {32, 48, 48} for Kandinsky 5 (crossdit.hpp:73) */
+    int32_t grid[3];        /* token grid (frames, height, width) after patching */
+    float scale_factor[3];  /* {1, 2, 2} in the Pro configs (crossdit.hpp:73) */
+    float theta;            /* 10000 (rope.hpp:60) */
+} kd_rope3d;
+
+typedef struct kd_attn_ctx kd_attn_ctx;
+
+typedef struct {
+    int32_t device;              /* CUDA device ordinal */
+    int32_t n_ranks;             /* head-sharding group size (1 = single GPU) */
+    int32_t rank;                /* this process's rank in the group */
+    const void* nccl_unique_id;  /* n_ranks > 1: the 128-byte ncclUniqueId every rank of the group
+                                    received from rank 0's kd_attn_nccl_unique_id; the context then
+                                    owns an NCCL communicator (kd_attn_create is collective) */
+    kd_attn_log_cb log_cb;       /* NULL: messages go to stderr at WARN and above */
+    void* log_user_data;
+} kd_attn_init;
+
+/* Fills out[128] with a fresh ncclUniqueId (rank 0 calls it and shares the
+ * bytes with the group out of band).  NCCL is loaded on demand (libnccl.so.2,
+ * or the path in $KD_ATTN_NCCL_LIB). */
+kd_attn_status kd_attn_nccl_unique_id(void* out128);
+
+/* Replaces: nothing in the reference holds attention state; ggml's backend and
+ * gallocr (src/core/executor.hpp:99-259) play this role.  Creates the per-device
+ * context that owns the operand scratch, the device error word and (for
+ * n_ranks > 1) the NCCL communicator.
+ * Returns KD_ATTN_OK and *out, or an error and *out = NULL. */
+kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out);
+void kd_attn_destroy(kd_attn_ctx* ctx);
+
+/* Text of the last error raised on this context ("" when none). */
+const char* kd_attn_last_error(const kd_attn_ctx* ctx);
+
+/* Synchronises `stream`, then reads and clears the device error word that the
+ * kernels' bounded waits set; KD_ATTN_ERR_DEVICE_TIMEOUT if any wait expired. */
+kd_attn_status kd_attn_device_status(kd_attn_ctx* ctx, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Prologue: RMSNorm per head + 3D RoPE + cast + permute, one HBM pass.
+ * Replaces, per projection x (crossdit.hpp:132-141, :188-193):
+ *   ggml_reshape_4d(x, d, H, L, N)                          crossdit.hpp:132-133
+ *   RMSNorm::forward = ggml_rms_norm(eps) * weight          module.hpp:177, ops.hpp:76-81
+ *   rope::apply(x, table)                                   rope.hpp:109-155
+ *   ggml_cont(ggml_permute(.., 0,2,1,3)) + ggml_cast(F16)   ops.hpp:122-131,167-169
+ * x : [H*d, L, N] f32 (ggml [C, L, N] from to_query/to_key/to_value)
+ * y : [d, L, H, N] of type f16, bf16 or f32 (the flash operand layout)
+ * norm: 0 = no RMSNorm (V), 1 = RMSNorm with `gain` (device [d], NULL = unit gain)
+ * rope: NULL = no rotation (cross-attention, V).  d must be even; with rope,
+ *       axes_dim must sum to d and grid must multiply to L. */
+kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm,
+                                const float* gain, float eps, const kd_rope3d* rope, kd_tensor* y,
+                                void* stream);
+
+/* ---------------------------------------------------------------------------
+ * ggml_flash_attn_ext semantics (called at ops.hpp:176):
+ *   out[:, h, i, n] = softmax_j(scale * q[:, i, h, n] . k[:, j, hk, nk] + mask[j, i, h%mh, n%mn]) v[:, j, hk, nk]
+ * q    : [D, Lq, H, N]      f32 | f16 | bf16 (f32 is rounded to K's type first,
+ *                           as ggml's CPU op rounds Q to the dot type)
+ * k, v : [D, Lk, Hkv, Nkv]  f16 | bf16, same type; H % Hkv == 0 and N % Nkv == 0
+ *                           (GQA broadcast as in ggml)
+ * mask : NULL or f16 [>=Lk, >=Lq, mh, mn], additive, -inf marks a masked key;
+ *        H % mh == 0, N % mn == 0.  Tiles that are entirely -inf are skipped.
+ * kv_len: NULL or device int32 [N]: keys j >= kv_len[n] are masked (the
+ *        variable text length of cross-attention without a dense mask).
+ * out  : [D, H, Lq, N] f32 | bf16 | f16 (ggml's dst permutation; with
+ *        contiguous strides this is [H*D, Lq, N], the ops::attention result)
+ * lse  : NULL or device f32 [N, H, Lq], natural-log softmax denominator
+ *        (ln sum_j exp(scale*q.k_j + mask_j)); -inf for fully masked rows.
+ * max_bias and logit_softcap must be 0 (the only values ops.hpp:176 passes).
+ * Rows whose keys are all masked produce 0.  D must be 128. */
+kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k,
+                                 const kd_tensor* v, const kd_tensor* mask, float scale,
+                                 float max_bias, float logit_softcap, const int32_t* kv_len,
+                                 kd_tensor* out, float* lse, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * The two CrossDiT call sites end to end (prologue + flash), operands staged
+ * in the context's scratch.
+ * Self-attention: DiTSelfAttention::forward between the QKV Linears and the
+ *   out-projection (crossdit.hpp:132-150 + ops.hpp:107-206).
+ * Cross-attention: DiTCrossAttention::forward (crossdit.hpp:186-198 +
+ *   ops.hpp:107-206), no RoPE, optional mask / kv_len.
+ * q_in, k_in, v_in : [C = n_head*128, L, N] f32
+ * op_type          : operand type, KD_ATTN_TYPE_F16 (ggml semantics) or BF16
+ * out              : [C, Lq, N] f32 | bf16 */
+kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                      const kd_tensor* v_in, int32_t n_head, const float* q_gain,
+                                      const float* k_gain, float eps, const kd_rope3d* rope,
+                                      int32_t op_type, kd_tensor* out, float* lse, void* stream);
+
+kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                       const kd_tensor* v_in, int32_t n_head, const float* q_gain,
+                                       const float* k_gain, float eps, const kd_tensor* mask,
+                                       const int32_t* kv_len, int32_t op_type, kd_tensor* out,
+                                       float* lse, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Head sharding.  No reference counterpart (the reference runs on device 0
+ * only, src/pipeline.cpp:214).  Rank r of n owns heads [r*H/n, (r+1)*H/n) and
+ * produces shard = [D, H/n, Lq, N]; this gathers every rank's shard into
+ * full = [D, H, Lq, N] (= [C, Lq, N]) ahead of the out-projection
+ * (crossdit.hpp:153) with one ncclAllGather into scratch plus a permute. */
+kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard, kd_tensor* full,
+                                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Seeded N(0,1) fill on the device: Philox4x32-10 + Box-Muller with the
+ * counter layout of PhiloxRNG::randn (src/rng.hpp:51-69): element i of a call
+ * at counter offset `offset` uses counter (offset, 0, i, 0) and key = seed.
+ * dst: device f32 [n].  Used to build the synthetic benchmark inputs. */
+kd_attn_status kd_attn_fill_randn(kd_attn_ctx* ctx, float* dst, uint64_t n, uint64_t seed,
+                                  uint32_t offset, void* stream);
+
+/* Library version as (major << 16) | minor. */
+int32_t kd_attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KD_ATTN_H */

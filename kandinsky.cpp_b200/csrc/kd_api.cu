@@ -1,0 +1,692 @@
+// kd_api.cu -- the C ABI of libkd_attn (include/kd_attn.h): argument checks,
+// the per-device context (scratch, error words, NCCL), TMA descriptors and
+// the launch sequence of each entry point.  No CPU fallback anywhere: a shape
+// the kernels do not cover is rejected with KD_ATTN_ERR_UNSUPPORTED.
+#include <dlfcn.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "../../include/kd_attn.h"
+#include "kd_internal.h"
+
+using namespace kd;
+
+struct kd_attn_ctx {
+    int device = 0;
+    int n_ranks = 1, rank = 0;
+    kd_attn_log_cb log_cb = nullptr;
+    void* log_user = nullptr;
+    std::string last_error;
+    unsigned* d_words = nullptr;  // [0] sticky error bits, [1] per-launch abort flag
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    int num_sms = 148;
+    void* nccl_comm = nullptr;
+    unsigned long long wait_ns = 2000000000ull;  // bound on a single device-side wait
+};
+
+namespace {
+
+// ------------------------------------------------------------------ errors / logging
+void log_msg(kd_attn_ctx* ctx, kd_attn_log_level lvl, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx && ctx->log_cb) {
+        ctx->log_cb(lvl, buf, ctx->log_user);
+    } else if (lvl >= KD_ATTN_LOG_WARN) {
+        fprintf(stderr, "[kd_attn] %s\n", buf);
+    }
+}
+
+kd_attn_status fail(kd_attn_ctx* ctx, kd_attn_status st, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_error = buf;
+    log_msg(ctx, st == KD_ATTN_ERR_UNSUPPORTED ? KD_ATTN_LOG_WARN : KD_ATTN_LOG_ERROR, "%s", buf);
+    return st;
+}
+
+#define KD_CUDA(ctx, call)                                                                              \
+    do {                                                                                                \
+        cudaError_t _e = (call);                                                                        \
+        if (_e != cudaSuccess)                                                                          \
+            return fail((ctx), KD_ATTN_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(_e));      \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ------------------------------------------------------------------ tensors
+size_t elt_size(int32_t t) {
+    switch (t) {
+        case KD_ATTN_TYPE_F32: return 4;
+        case KD_ATTN_TYPE_F16:
+        case KD_ATTN_TYPE_BF16: return 2;
+        default: return 0;
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ne[i] >= 0, sizes fit int, dim 0 contiguous.
+kd_attn_status check_tensor(kd_attn_ctx* ctx, const kd_tensor* t, const char* name) {
+    if (!t) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    const size_t es = elt_size(t->type);
+    if (!es) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "%s: type %d is not f32/f16/bf16", name, t->type);
+    for (int i = 0; i < 4; ++i)
+        if (t->ne[i] < 0 || t->ne[i] > (int64_t)0x7fffffff)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: ne[%d] = %lld out of range", name, i,
+                        (long long)t->ne[i]);
+    if (t->nb[0] != es) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "%s: dim 0 must be contiguous", name);
+    const int64_t n = t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3];
+    if (n > 0 && !t->data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: data is NULL", name);
+    return KD_ATTN_OK;
+}
+
+// Strides of size-1 dims are irrelevant; give them the packed value so TMA encoding accepts them.
+void packed_strides(const kd_tensor* t, uint64_t nb[4]) {
+    nb[0] = t->nb[0];
+    for (int i = 1; i < 4; ++i) nb[i] = (t->ne[i] == 1) ? nb[i - 1] * (uint64_t)t->ne[i - 1] : t->nb[i];
+}
+
+bool strides16(const uint64_t nb[4]) { return nb[1] % 16 == 0 && nb[2] % 16 == 0 && nb[3] % 16 == 0; }
+
+// ------------------------------------------------------------------ TMA descriptors
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled_t get_encode() {
+    static PFN_encodeTiled_t fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+    }
+    return fn;
+}
+
+// [128, L, heads, seqs] 16-bit operand, {64, 128, 1, 1} box, 128-byte swizzle, zero fill out of range.
+kd_attn_status make_operand_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, bool bf16, int64_t L,
+                                int64_t heads, int64_t seqs, const uint64_t nb[4]) {
+    PFN_encodeTiled_t enc = get_encode();
+    if (!enc) return fail(ctx, KD_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if (!aligned16(data)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "operand base address is not 16-byte aligned");
+    cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)(L > 0 ? L : 1), (cuuint64_t)(heads > 0 ? heads : 1),
+                          (cuuint64_t)(seqs > 0 ? seqs : 1)};
+    cuuint64_t strides[3] = {nb[1], nb[2], nb[3]};
+    cuuint32_t box[4] = {64, (cuuint32_t)kBlockM, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                     const_cast<void*>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled rejected the operand (%d)", (int)r);
+    return KD_ATTN_OK;
+}
+
+// ------------------------------------------------------------------ scratch
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+kd_attn_status ensure_scratch(kd_attn_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->scratch_bytes) return KD_ATTN_OK;
+    // growing happens on the first calls only; make sure no queued work still reads the old buffer
+    KD_CUDA(ctx, cudaDeviceSynchronize());
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    const size_t want = align256(bytes + bytes / 8);
+    if (cudaMalloc(&ctx->scratch, want) != cudaSuccess) {
+        cudaGetLastError();
+        ctx->scratch = nullptr;
+        return fail(ctx, KD_ATTN_ERR_OUT_OF_MEMORY, "could not allocate %zu bytes of scratch", want);
+    }
+    ctx->scratch_bytes = want;
+    return KD_ATTN_OK;
+}
+
+// ------------------------------------------------------------------ NCCL (loaded on demand)
+struct NcclUid {
+    char internal[128];
+};
+struct Nccl {
+    void* so = nullptr;
+    int (*getUniqueId)(NcclUid*) = nullptr;
+    int (*commInitRank)(void**, int, NcclUid, int) = nullptr;
+    int (*allGather)(const void*, void*, size_t, int, void*, cudaStream_t) = nullptr;
+    int (*commDestroy)(void*) = nullptr;
+    const char* (*getErrorString)(int) = nullptr;
+};
+
+Nccl* nccl() {
+    static Nccl n;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        const char* path = getenv("KD_ATTN_NCCL_LIB");
+        n.so = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (n.so) {
+            n.getUniqueId = reinterpret_cast<int (*)(NcclUid*)>(dlsym(n.so, "ncclGetUniqueId"));
+            n.commInitRank = reinterpret_cast<int (*)(void**, int, NcclUid, int)>(dlsym(n.so, "ncclCommInitRank"));
+            n.allGather = reinterpret_cast<int (*)(const void*, void*, size_t, int, void*, cudaStream_t)>(
+                dlsym(n.so, "ncclAllGather"));
+            n.commDestroy = reinterpret_cast<int (*)(void*)>(dlsym(n.so, "ncclCommDestroy"));
+            n.getErrorString = reinterpret_cast<const char* (*)(int)>(dlsym(n.so, "ncclGetErrorString"));
+        }
+    }
+    if (!n.so || !n.getUniqueId || !n.commInitRank || !n.allGather || !n.commDestroy) return nullptr;
+    return &n;
+}
+constexpr int kNcclUint8 = 1;  // ncclDataType_t ncclUint8
+
+const char* nccl_err(Nccl* n, int r) { return (n && n->getErrorString) ? n->getErrorString(r) : "nccl error"; }
+
+OutType out_type_of(int32_t t) {
+    return t == KD_ATTN_TYPE_F32 ? OutType::F32 : (t == KD_ATTN_TYPE_BF16 ? OutType::BF16 : OutType::F16);
+}
+
+// ------------------------------------------------------------------ flash core
+struct FlashArgs {
+    const kd_tensor* q;
+    const kd_tensor* k;
+    const kd_tensor* v;
+    const kd_tensor* mask;
+    float scale;
+    const int32_t* kv_len;
+    kd_tensor* out;
+    float* lse;
+};
+
+kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, a.q, "q")) || (rc = check_tensor(ctx, a.k, "k")) ||
+        (rc = check_tensor(ctx, a.v, "v")) || (rc = check_tensor(ctx, a.out, "out")))
+        return rc;
+    const kd_tensor &q = *a.q, &k = *a.k, &v = *a.v, &o = *a.out;
+    if (q.ne[0] != kHeadDim || k.ne[0] != kHeadDim || v.ne[0] != kHeadDim)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128 (q %lld, k %lld, v %lld)",
+                    (long long)q.ne[0], (long long)k.ne[0], (long long)v.ne[0]);
+    if (k.type != v.type || (k.type != KD_ATTN_TYPE_F16 && k.type != KD_ATTN_TYPE_BF16))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k and v must share type f16 or bf16");
+    const int64_t Lq = q.ne[1], H = q.ne[2], N = q.ne[3];
+    const int64_t Lk = k.ne[1], Hkv = k.ne[2], Nkv = k.ne[3];
+    if (v.ne[1] != Lk || v.ne[2] != Hkv || v.ne[3] != Nkv)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "v shape differs from k");
+    if (Hkv <= 0 || Nkv <= 0 || H % Hkv || N % Nkv)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q heads/sequences (%lld, %lld) are not multiples of k's (%lld, %lld)",
+                    (long long)H, (long long)N, (long long)Hkv, (long long)Nkv);
+    if (o.ne[0] != kHeadDim || o.ne[1] != H || o.ne[2] != Lq || o.ne[3] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [128, H, Lq, N]");
+    if (!(a.scale > 0.f) || !std::isfinite(a.scale))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "scale must be positive and finite");
+    if (Lk > (int64_t)kMaxKvTiles * kBlockN)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "Lk %lld exceeds %d", (long long)Lk, kMaxKvTiles * kBlockN);
+    if (H > 65535 || N > 65535) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than 65535 heads or sequences");
+    uint64_t onb[4];
+    packed_strides(&o, onb);
+    if (!strides16(onb) || !aligned16(o.data))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned");
+    if (Lq == 0 || H == 0 || N == 0) return KD_ATTN_OK;
+
+    const bool bf16 = k.type == KD_ATTN_TYPE_BF16;
+    uint64_t knb[4], vnb[4], qnb[4];
+    packed_strides(&k, knb);
+    packed_strides(&v, vnb);
+    packed_strides(&q, qnb);
+    if (Lk > 0 && (!strides16(knb) || !strides16(vnb)))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k/v strides must be multiples of 16 bytes");
+
+    // scratch: Q rounded to the operand type (when needed) + mask tile classes
+    const bool q_direct = q.type == k.type && strides16(qnb) && aligned16(q.data);
+    const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * kHeadDim * 2);
+    int n_qb = 0, n_kb = 0, mh = 1, mn = 1;
+    size_t cls_bytes = 0;
+    if (a.mask) {
+        if ((rc = check_tensor(ctx, a.mask, "mask"))) return rc;
+        const kd_tensor& m = *a.mask;
+        if (m.type != KD_ATTN_TYPE_F16) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "mask must be f16");
+        if (m.ne[0] < Lk || m.ne[1] < Lq)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "mask [%lld, %lld] smaller than [Lk, Lq] = [%lld, %lld]",
+                        (long long)m.ne[0], (long long)m.ne[1], (long long)Lk, (long long)Lq);
+        if (m.ne[2] <= 0 || m.ne[3] <= 0 || H % m.ne[2] || N % m.ne[3])
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "mask planes must divide heads and sequences");
+        mh = (int)m.ne[2];
+        mn = (int)m.ne[3];
+        n_qb = (int)((Lq + 63) / 64);
+        n_kb = (int)((Lk + 63) / 64);
+        cls_bytes = align256((size_t)mh * mn * n_qb * n_kb);
+    }
+    if ((rc = ensure_scratch(ctx, q_bytes + cls_bytes))) return rc;
+    char* scr = static_cast<char*>(ctx->scratch);
+
+    const void* qdata = q.data;
+    if (!q_direct) {
+        ConvertParams cp{};
+        cp.src = q.data;
+        cp.src_type = q.type;
+        cp.nb1 = (long long)qnb[1];
+        cp.nb2 = (long long)qnb[2];
+        cp.nb3 = (long long)qnb[3];
+        cp.dst = scr;
+        cp.L = (int)Lq;
+        cp.H = (int)H;
+        cp.N = (int)N;
+        KD_CUDA(ctx, launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, ctx->num_sms, st));
+        qdata = scr;
+        qnb[1] = kHeadDim * 2;
+        qnb[2] = qnb[1] * Lq;
+        qnb[3] = qnb[2] * H;
+    }
+    uint8_t* cls = nullptr;
+    if (a.mask) {
+        cls = reinterpret_cast<uint8_t*>(scr + q_bytes);
+        uint64_t mnb[4];
+        packed_strides(a.mask, mnb);
+        MaskClassParams mp{};
+        mp.mask = static_cast<const uint16_t*>(a.mask->data);
+        mp.nb1 = (long long)mnb[1];
+        mp.nb2 = (long long)mnb[2];
+        mp.nb3 = (long long)mnb[3];
+        mp.Lq = (int)Lq;
+        mp.Lk = (int)Lk;
+        mp.mh = mh;
+        mp.mn = mn;
+        mp.cls = cls;
+        mp.n_qb = n_qb;
+        mp.n_kb = n_kb;
+        KD_CUDA(ctx, launch_mask_classify(mp, st));
+    }
+
+    CUtensorMap tmQ, tmK, tmV;
+    if ((rc = make_operand_map(ctx, &tmQ, qdata, bf16, Lq, H, N, qnb))) return rc;
+    if (Lk > 0) {
+        if ((rc = make_operand_map(ctx, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb))) return rc;
+        if ((rc = make_operand_map(ctx, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb))) return rc;
+    } else {
+        tmK = tmQ;  // never dereferenced: no key tiles to visit
+        tmV = tmQ;
+    }
+
+    FmhaParams p{};
+    p.Lq = (int)Lq;
+    p.Lk = (int)Lk;
+    p.H = (int)H;
+    p.N = (int)N;
+    p.rk2 = (int)(H / Hkv);
+    p.rk3 = (int)(N / Nkv);
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.inv_scale = 1.0f / a.scale;
+    p.out = o.data;
+    p.o_nb1 = (long long)onb[1];
+    p.o_nb2 = (long long)onb[2];
+    p.o_nb3 = (long long)onb[3];
+    p.lse = a.lse;
+    p.tile_cls = cls;
+    p.n_qb = n_qb;
+    p.n_kb = n_kb;
+    if (a.mask) {
+        uint64_t mnb[4];
+        packed_strides(a.mask, mnb);
+        p.mask = static_cast<const uint16_t*>(a.mask->data);
+        p.m_nb1 = (long long)mnb[1];
+        p.m_nb2 = (long long)mnb[2];
+        p.m_nb3 = (long long)mnb[3];
+    }
+    p.mh = mh;
+    p.mn = mn;
+    p.kv_len = a.kv_len;
+    p.err = ctx->d_words;
+    p.abort_flag = ctx->d_words + 1;
+    p.wait_ns = ctx->wait_ns;
+    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, sizeof(unsigned), st));
+    KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
+    return KD_ATTN_OK;
+}
+
+// ------------------------------------------------------------------ prologue core
+kd_attn_status fill_rope(kd_attn_ctx* ctx, const kd_rope3d* rope, int64_t L, RopeTab* tab) {
+    const int a0 = rope->axes_dim[0], a1 = rope->axes_dim[1], a2 = rope->axes_dim[2];
+    if (a0 < 0 || a1 < 0 || a2 < 0 || (a0 | a1 | a2) & 1 || a0 + a1 + a2 != kHeadDim)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope axes_dim {%d,%d,%d} must be even and sum to 128", a0, a1, a2);
+    const int64_t g = (int64_t)rope->grid[0] * rope->grid[1] * rope->grid[2];
+    if (rope->grid[0] <= 0 || rope->grid[1] <= 0 || rope->grid[2] <= 0 || g != L)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope grid %dx%dx%d does not cover L = %lld", rope->grid[0],
+                    rope->grid[1], rope->grid[2], (long long)L);
+    for (int a = 0; a < 3; ++a)
+        if (!(rope->scale_factor[a] > 0.f)) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope scale_factor must be > 0");
+    if (!(rope->theta > 0.f)) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope theta must be > 0");
+    const int halves[3] = {a0 / 2, a1 / 2, a2 / 2};
+    int pi = 0;
+    for (int a = 0; a < 3; ++a)
+        for (int i = 0; i < halves[a]; ++i, ++pi) {
+            // rope.hpp:23-29 get_freqs(dim = half): expf(-logf(theta) * i / dim), in float
+            tab->freq[pi] = expf(-logf(rope->theta) * (float)i / (float)halves[a]);
+            tab->div[pi] = rope->scale_factor[a];
+            tab->axis[pi] = (unsigned char)a;
+        }
+    tab->grid_h = rope->grid[1];
+    tab->grid_w = rope->grid[2];
+    return KD_ATTN_OK;
+}
+
+kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm, const float* gain,
+                             float eps, const kd_rope3d* rope, kd_tensor* y, cudaStream_t st) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, x, "x")) || (rc = check_tensor(ctx, y, "y"))) return rc;
+    if (x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "prologue input must be f32");
+    if (n_head <= 0 || x->ne[0] != (int64_t)n_head * kHeadDim)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x.ne[0] = %lld is not n_head * 128", (long long)x->ne[0]);
+    if (x->ne[3] != 1) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x must be [C, L, N] (ne[3] == 1)");
+    const int64_t L = x->ne[1], N = x->ne[2];
+    if (y->ne[0] != kHeadDim || y->ne[1] != L || y->ne[2] != n_head || y->ne[3] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "y must be [128, L, n_head, N]");
+    uint64_t xnb[4], ynb[4];
+    packed_strides(x, xnb);
+    packed_strides(y, ynb);
+    if (!aligned16(x->data) || xnb[1] % 16 || xnb[2] % 16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x rows must be 16-byte aligned");
+    const size_t ye = elt_size(y->type);
+    if ((reinterpret_cast<uintptr_t>(y->data) % (4 * ye)) || ynb[1] % (4 * ye) || ynb[2] % (4 * ye) ||
+        ynb[3] % (4 * ye))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "y rows must be aligned to 4 elements");
+    if (gain && !aligned16(gain)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "gain must be 16-byte aligned");
+    if (L * N == 0) return KD_ATTN_OK;
+    PrologueParams p{};
+    p.x = static_cast<const float*>(x->data);
+    p.x_nb1 = (long long)xnb[1];
+    p.x_nb2 = (long long)xnb[2];
+    p.y = y->data;
+    p.y_nb1 = (long long)ynb[1];
+    p.y_nb2 = (long long)ynb[2];
+    p.y_nb3 = (long long)ynb[3];
+    p.L = (int)L;
+    p.N = (int)N;
+    p.H = n_head;
+    p.norm = norm ? 1 : 0;
+    p.gain = gain;
+    p.eps = eps;
+    p.rope = rope ? 1 : 0;
+    if (rope && (rc = fill_rope(ctx, rope, L, &p.tab))) return rc;
+    KD_CUDA(ctx, launch_prologue(out_type_of(y->type), p, ctx->num_sms, st));
+    return KD_ATTN_OK;
+}
+
+kd_tensor operand_view(void* data, int32_t type, int64_t L, int64_t H, int64_t N) {
+    kd_tensor t{};
+    t.data = data;
+    t.type = type;
+    t.ne[0] = kHeadDim;
+    t.ne[1] = L;
+    t.ne[2] = H;
+    t.ne[3] = N;
+    t.nb[0] = elt_size(type);
+    t.nb[1] = t.nb[0] * kHeadDim;
+    t.nb[2] = t.nb[1] * (size_t)L;
+    t.nb[3] = t.nb[2] * (size_t)H;
+    return t;
+}
+
+// out [C, Lq, N] viewed as the flash dst [128, H, Lq, N]
+kd_attn_status out_view(kd_attn_ctx* ctx, const kd_tensor* out, int32_t n_head, int64_t Lq, int64_t N, kd_tensor* v) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, out, "out"))) return rc;
+    if (out->ne[0] != (int64_t)n_head * kHeadDim || out->ne[1] != Lq || out->ne[2] != N || out->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [n_head*128, Lq, N]");
+    *v = *out;
+    v->ne[0] = kHeadDim;
+    v->ne[1] = n_head;
+    v->ne[2] = Lq;
+    v->ne[3] = N;
+    v->nb[1] = out->nb[0] * kHeadDim;
+    v->nb[2] = out->nb[1];
+    v->nb[3] = out->nb[2];
+    return KD_ATTN_OK;
+}
+
+kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
+                              int32_t n_head, const float* q_gain, const float* k_gain, float eps,
+                              const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
+                              kd_tensor* out, float* lse, cudaStream_t st) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
+        (rc = check_tensor(ctx, v_in, "v_in")))
+        return rc;
+    if (op_type != KD_ATTN_TYPE_F16 && op_type != KD_ATTN_TYPE_BF16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "op_type must be f16 or bf16");
+    const int64_t Lq = q_in->ne[1], N = q_in->ne[2], Lk = k_in->ne[1];
+    if (k_in->ne[2] != N || v_in->ne[1] != Lk || v_in->ne[2] != N || v_in->ne[0] != k_in->ne[0] ||
+        k_in->ne[0] != q_in->ne[0])
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
+    kd_tensor ov;
+    if ((rc = out_view(ctx, out, n_head, Lq, N, &ov))) return rc;
+    const size_t es = 2;
+    const size_t qb = align256((size_t)N * n_head * Lq * kHeadDim * es);
+    const size_t kb = align256((size_t)N * n_head * Lk * kHeadDim * es);
+    // operand scratch sits after the flash core's own scratch needs: reserve them up front
+    const size_t flash_extra =
+        mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
+    if ((rc = ensure_scratch(ctx, flash_extra + qb + 2 * kb))) return rc;
+    // The flash core carves its scratch from the start of the buffer; operands go after it.
+    char* base = static_cast<char*>(ctx->scratch) + flash_extra;
+    kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N);
+    kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_head, N);
+    kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_head, N);
+    if ((rc = prologue_core(ctx, q_in, n_head, 1, q_gain, eps, rope, &Qs, st))) return rc;
+    if ((rc = prologue_core(ctx, k_in, n_head, 1, k_gain, eps, rope, &Ks, st))) return rc;
+    if ((rc = prologue_core(ctx, v_in, n_head, 0, nullptr, eps, nullptr, &Vs, st))) return rc;
+    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, lse};
+    return flash_core(ctx, fa, st);
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int32_t kd_attn_version(void) { return (KD_ATTN_VERSION_MAJOR << 16) | KD_ATTN_VERSION_MINOR; }
+
+kd_attn_status kd_attn_nccl_unique_id(void* out128) {
+    if (!out128) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    Nccl* n = nccl();
+    if (!n) return fail(nullptr, KD_ATTN_ERR_NCCL, "NCCL could not be loaded (libnccl.so.2)");
+    NcclUid id;
+    const int r = n->getUniqueId(&id);
+    if (r != 0) return fail(nullptr, KD_ATTN_ERR_NCCL, "ncclGetUniqueId: %s", nccl_err(n, r));
+    memcpy(out128, id.internal, sizeof id.internal);
+    return KD_ATTN_OK;
+}
+
+kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
+    if (!out) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (!init) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    if (init->n_ranks < 1 || init->rank < 0 || init->rank >= init->n_ranks) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    kd_attn_ctx* ctx = new kd_attn_ctx();
+    ctx->device = init->device;
+    ctx->n_ranks = init->n_ranks;
+    ctx->rank = init->rank;
+    ctx->log_cb = init->log_cb;
+    ctx->log_user = init->log_user_data;
+    if (const char* w = getenv("KD_ATTN_WAIT_MS")) {
+        const long long ms = atoll(w);
+        if (ms > 0) ctx->wait_ns = (unsigned long long)ms * 1000000ull;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || init->device < 0 || init->device >= ndev) {
+        cudaGetLastError();
+        fail(ctx, KD_ATTN_ERR_CUDA, "CUDA device %d is not available", init->device);
+        delete ctx;
+        return KD_ATTN_ERR_CUDA;
+    }
+    DeviceGuard g(ctx->device);
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, ctx->device) != cudaSuccess) {
+        delete ctx;
+        return KD_ATTN_ERR_CUDA;
+    }
+    if (prop.major != 10 || prop.minor != 0) {
+        fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "device %d is sm_%d%d; libkd_attn is built for sm_100a only", ctx->device,
+             prop.major, prop.minor);
+        delete ctx;
+        return KD_ATTN_ERR_UNSUPPORTED;
+    }
+    ctx->num_sms = prop.multiProcessorCount;
+    if (cudaMalloc(&ctx->d_words, 2 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->d_words, 0, 2 * sizeof(unsigned)) != cudaSuccess) {
+        cudaGetLastError();
+        delete ctx;
+        return KD_ATTN_ERR_OUT_OF_MEMORY;
+    }
+    if (ctx->n_ranks > 1) {
+        Nccl* n = nccl();
+        if (!n || !init->nccl_unique_id) {
+            fail(ctx, KD_ATTN_ERR_NCCL, "n_ranks > 1 needs NCCL and an nccl_unique_id");
+            cudaFree(ctx->d_words);
+            delete ctx;
+            return KD_ATTN_ERR_NCCL;
+        }
+        NcclUid id;
+        memcpy(id.internal, init->nccl_unique_id, sizeof id.internal);
+        const int r = n->commInitRank(&ctx->nccl_comm, ctx->n_ranks, id, ctx->rank);
+        if (r != 0) {
+            fail(ctx, KD_ATTN_ERR_NCCL, "ncclCommInitRank: %s", nccl_err(n, r));
+            cudaFree(ctx->d_words);
+            delete ctx;
+            return KD_ATTN_ERR_NCCL;
+        }
+    }
+    *out = ctx;
+    return KD_ATTN_OK;
+}
+
+void kd_attn_destroy(kd_attn_ctx* ctx) {
+    if (!ctx) return;
+    DeviceGuard g(ctx->device);
+    if (ctx->nccl_comm) {
+        if (Nccl* n = nccl()) n->commDestroy(ctx->nccl_comm);
+    }
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->d_words) cudaFree(ctx->d_words);
+    delete ctx;
+}
+
+const char* kd_attn_last_error(const kd_attn_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+kd_attn_status kd_attn_device_status(kd_attn_ctx* ctx, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    KD_CUDA(ctx, cudaStreamSynchronize(st));
+    unsigned words[2] = {0, 0};
+    KD_CUDA(ctx, cudaMemcpy(words, ctx->d_words, sizeof words, cudaMemcpyDeviceToHost));
+    KD_CUDA(ctx, cudaMemset(ctx->d_words, 0, sizeof words));
+    if (words[0])
+        return fail(ctx, KD_ATTN_ERR_DEVICE_TIMEOUT, "device-side wait expired (error bits 0x%x)", words[0]);
+    return KD_ATTN_OK;
+}
+
+kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm, const float* gain,
+                                float eps, const kd_rope3d* rope, kd_tensor* y, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return prologue_core(ctx, x, n_head, norm, gain, eps, rope, y, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
+                                 const kd_tensor* mask, float scale, float max_bias, float logit_softcap,
+                                 const int32_t* kv_len, kd_tensor* out, float* lse, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    if (max_bias != 0.f) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "max_bias (ALiBi) must be 0");
+    if (logit_softcap != 0.f) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "logit_softcap must be 0");
+    DeviceGuard g(ctx->device);
+    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse};
+    return flash_core(ctx, fa, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                      const kd_tensor* v_in, int32_t n_head, const float* q_gain, const float* k_gain,
+                                      float eps, const kd_rope3d* rope, int32_t op_type, kd_tensor* out, float* lse,
+                                      void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    if (q_in && k_in && q_in->ne[1] != k_in->ne[1])
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "self-attention needs Lq == Lk");
+    return attention_core(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type, out, lse,
+                          static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                       const kd_tensor* v_in, int32_t n_head, const float* q_gain, const float* k_gain,
+                                       float eps, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
+                                       kd_tensor* out, float* lse, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return attention_core(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, nullptr, mask, kv_len, op_type, out, lse,
+                          static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard, kd_tensor* full, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, shard, "shard")) || (rc = check_tensor(ctx, full, "full"))) return rc;
+    if (shard->type != full->type) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "shard and full types differ");
+    const int R = ctx->n_ranks;
+    const int64_t D = shard->ne[0], Hs = shard->ne[1], Lq = shard->ne[2], N = shard->ne[3];
+    if (full->ne[0] != D || full->ne[1] != Hs * R || full->ne[2] != Lq || full->ne[3] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "full must be [D, H_shard * n_ranks, Lq, N]");
+    const size_t es = elt_size(shard->type);
+    const size_t row = (size_t)D * Hs * es;
+    auto contiguous = [&](const kd_tensor* t, int64_t heads) {
+        return t->nb[1] == (size_t)D * es && t->nb[2] == (size_t)D * heads * es &&
+               t->nb[3] == (size_t)D * heads * Lq * es;
+    };
+    if (!contiguous(shard, Hs) || !contiguous(full, Hs * R) || row % 16 || !aligned16(full->data))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "allgather_heads needs contiguous, 16-byte aligned rows");
+    const size_t shard_bytes = row * (size_t)Lq * N;
+    if (shard_bytes == 0) return KD_ATTN_OK;
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (R == 1) {
+        KD_CUDA(ctx, cudaMemcpyAsync(full->data, shard->data, shard_bytes, cudaMemcpyDeviceToDevice, st));
+        return KD_ATTN_OK;
+    }
+    Nccl* n = nccl();
+    if (!n || !ctx->nccl_comm) return fail(ctx, KD_ATTN_ERR_NCCL, "context has no NCCL communicator");
+    if ((rc = ensure_scratch(ctx, shard_bytes * R))) return rc;
+    const int r = n->allGather(shard->data, ctx->scratch, shard_bytes, kNcclUint8, ctx->nccl_comm, st);
+    if (r != 0) return fail(ctx, KD_ATTN_ERR_NCCL, "ncclAllGather: %s", nccl_err(n, r));
+    KD_CUDA(ctx, launch_unshard_heads(ctx->scratch, full->data, (long long)Lq * N, R, (long long)row, ctx->num_sms, st));
+    return KD_ATTN_OK;
+}
+
+kd_attn_status kd_attn_fill_randn(kd_attn_ctx* ctx, float* dst, uint64_t n, uint64_t seed, uint32_t offset,
+                                  void* stream) {
+    if (!ctx || (n && !dst)) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    if (n > 0xffffffffull) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "randn counter index is 32-bit (n <= 2^32)");
+    DeviceGuard g(ctx->device);
+    KD_CUDA(ctx, launch_randn(dst, n, seed, offset, ctx->num_sms, static_cast<cudaStream_t>(stream)));
+    return KD_ATTN_OK;
+}
+
+}  // extern "C"

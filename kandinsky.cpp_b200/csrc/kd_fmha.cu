@@ -1,0 +1,521 @@
+// kd_fmha.cu -- flash-attention forward for sm_100a (B200).
+//
+// Computes ggml_flash_attn_ext (called at src/core/ops.hpp:176 of the
+// reference) for head_dim 128:  O = softmax(scale * Q K^T + mask) V per
+// (head, sequence), fp32 accumulation, f16 or bf16 operands.
+//
+// One CTA owns 2 x 128 query rows of one (head, sequence) and streams the K/V
+// tiles of that head through a 4-stage shared-memory ring:
+//
+//   warp 0      TMA producer: Q0, Q1 once, then K_j, V_j (128 x 128 tiles,
+//               two 64-column boxes with 128-byte swizzle each)
+//   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T into TMEM (SS MMA,
+//               both operands K-major), O_i += P_i V_j (TS MMA, P from TMEM,
+//               V MN-major); owns the 512-column TMEM allocation
+//   warp 2      builds the list of K/V tiles this CTA must visit (tiles whose
+//               mask is entirely -inf for all 256 rows are never loaded)
+//   warps 4-7   softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
+//   warps 8-11  the same for Q tile 1
+//
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_i (16-bit,
+// two per column) overwrites the first 64 columns of S_i once S_i has been read.
+//
+// MMA issue order per K/V tile j (FA4-style ping-pong, so one softmax
+// warpgroup works while the tensor core runs the other tile's MMAs):
+//   PV0(j), S0(j+1), PV1(j), S1(j+1)
+// S_i(j+1) is issued after PV_i(j), so the commit that publishes S_i(j+1)
+// also certifies that PV_i(j) finished: the softmax may rescale O_i right
+// after it sees S_i(j+1) without another barrier.
+//
+// Softmax keeps a running max m (log2 domain) and only rescales O and the row
+// sum when the max grows by more than 8 (P values stay <= 256); the final
+// normalisation divides by the row sum, and LSE = (m + log2 l) * ln 2.
+//
+// Every wait is bounded (kd_common.cuh: mbar_wait); on expiry the CTA records
+// an error bit, stops issuing work, drains what it has in flight and frees TMEM.
+#include <type_traits>
+
+#include "kd_common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB: one 128 x 128 16-bit tile
+constexpr int kBoxBytes = kTileBytes / 2;           // one 128-row x 64-column box
+constexpr int kThreads = 384;
+
+constexpr int kSmemQ = 0;
+constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
+constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
+// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], drain
+constexpr int kNumBars = 1 + 2 * kStages + 6 + 1;
+constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
+constexpr int kSmemNKept = kSmemTmemSlot + 4;
+constexpr int kSmemList = (kSmemNKept + 4 + 15) & ~15;
+constexpr int kSmemTotal = kSmemList + kMaxKvTiles * 4;
+constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
+
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8 between rescales
+
+static_assert(kSmemAlloc <= 232448, "shared memory budget");
+
+template <typename TO>
+__device__ __forceinline__ void store_row32(TO* dst, const float (&v)[32]);
+
+template <>
+__device__ __forceinline__ void store_row32<float>(float* dst, const float (&v)[32]) {
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+template <>
+__device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        d[i] = make_uint4(Pack2<__nv_bfloat16>::pack(v[8 * i], v[8 * i + 1]),
+                          Pack2<__nv_bfloat16>::pack(v[8 * i + 2], v[8 * i + 3]),
+                          Pack2<__nv_bfloat16>::pack(v[8 * i + 4], v[8 * i + 5]),
+                          Pack2<__nv_bfloat16>::pack(v[8 * i + 6], v[8 * i + 7]));
+}
+template <>
+__device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        d[i] = make_uint4(Pack2<__half>::pack(v[8 * i], v[8 * i + 1]), Pack2<__half>::pack(v[8 * i + 2], v[8 * i + 3]),
+                          Pack2<__half>::pack(v[8 * i + 4], v[8 * i + 5]),
+                          Pack2<__half>::pack(v[8 * i + 6], v[8 * i + 7]));
+}
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FmhaParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int qblk = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
+    const int hk = h / p.rk2, nk = n / p.rk3;
+    const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;
+    uint64_t* kv_empty = bars + 1 + kStages;
+    uint64_t* s_full = bars + 1 + 2 * kStages;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_full = s_full + 4;
+    uint64_t* drain = s_full + 6;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
+    int* n_kept_slot = reinterpret_cast<int*>(smem + kSmemNKept);
+    uint32_t* list = reinterpret_cast<uint32_t*>(smem + kSmemList);
+
+    int lk_eff = p.Lk;
+    if (p.kv_len) {
+        const int kl = p.kv_len[n];
+        lk_eff = kl < 0 ? 0 : (kl < p.Lk ? kl : p.Lk);
+    }
+    const int n_kv_tiles = (lk_eff + kBlockN - 1) / kBlockN;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], kBlockM);
+            mbar_init(&o_full[i], 1);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 2) {
+        // Kept-tile list: entry = (kv tile index << 16) | 2-bit class per (64-row group g, 64-key half hh)
+        // at bit 4g + 2hh.  Without a mask every tile is FULL; the kv_len / Lk tail is masked by index.
+        int count = 0;
+        const long long plane =
+            p.tile_cls ? ((long long)(n % p.mn) * p.mh + (h % p.mh)) * (long long)p.n_qb * p.n_kb : 0;
+        for (int base = 0; base < n_kv_tiles; base += 32) {
+            const int t = base + lane;
+            uint32_t bits = 0;
+            if (t < n_kv_tiles) {
+                if (p.tile_cls) {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int qb = qblk * 4 + g;
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            const int kb = 2 * t + hh;
+                            uint32_t c = kTileSkip;
+                            if (qb < p.n_qb && kb < p.n_kb) c = p.tile_cls[plane + (long long)qb * p.n_kb + kb];
+                            bits |= (c & 3u) << (4 * g + 2 * hh);
+                        }
+                    }
+                } else {
+                    bits = 0x5555u;
+                }
+            }
+            const bool kept = bits != 0;
+            const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
+            if (kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)t << 16) | bits;
+            count += __popc(ballot);
+        }
+        if (lane == 0) *n_kept_slot = count;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t tmem = *tmem_slot;
+    const int n_iter = *n_kept_slot;
+    const bool skip_all = *reinterpret_cast<volatile unsigned*>(p.abort_flag) != 0;
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+
+    if (skip_all) {
+        // another CTA already gave up: do nothing, just release TMEM below
+    } else if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (n_iter > 0) {
+            if (lane == 0) {
+                tma_prefetch_desc(&tmQ);
+                tma_prefetch_desc(&tmK);
+                tma_prefetch_desc(&tmV);
+                mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
+                const int q0 = qblk * kRowsPerCta;
+#pragma unroll
+                for (int i = 0; i < kQTiles; ++i)
+#pragma unroll
+                    for (int b = 0; b < 2; ++b)
+                        tma_load_4d(smem + kSmemQ + i * kTileBytes + b * kBoxBytes, &tmQ, q_full, b * 64,
+                                    q0 + i * kBlockM, h, n);
+            }
+            __syncwarp();
+            uint32_t it = 0;
+            bool ok = true;
+            for (int j = 0; j < n_iter && ok; ++j) {
+                const int kt = (int)(list[j] >> 16);
+#pragma unroll 1
+                for (int w = 0; w < 2; ++w) {  // w = 0: K tile, w = 1: V tile
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1u;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
+                    if (!ok) break;
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+                        const CUtensorMap* map = w ? &tmV : &tmK;
+#pragma unroll
+                        for (int b = 0; b < 2; ++b)
+                            tma_load_4d(smem + kSmemKV + s * kTileBytes + b * kBoxBytes, map, &kv_full[s], b * 64,
+                                        kt * kBlockN, hk, nk);
+                    }
+                    __syncwarp();
+                    ++it;
+                }
+            }
+            if (!ok) {
+                // Abort path: wait (bounded, ignoring the abort flag) until every copy this warp
+                // issued has landed, so no TMA write targets shared memory after the CTA exits.
+                mbar_wait(q_full, 0, ctl, kErrTimeoutDrain, false);
+                for (uint32_t k = (it > (uint32_t)kStages ? it - kStages : 0u); k < it; ++k)
+                    mbar_wait(&kv_full[k % kStages], (k / kStages) & 1u, ctl, kErrTimeoutDrain, false);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (n_iter > 0) {
+            const uint32_t qa = smem_u32(smem + kSmemQ);
+            const uint32_t kva = smem_u32(smem + kSmemKV);
+            constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
+            constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
+            uint32_t it = 0;
+            bool issued = false;
+
+            auto next_stage = [&](int& s) -> bool {
+                s = it % kStages;
+                const uint32_t ph = (it / kStages) & 1u;
+                ++it;
+                return __all_sync(0xffffffffu, mbar_wait(&kv_full[s], ph, ctl, kErrTimeoutKVFull));
+            };
+            auto issue_s = [&](int i, int s) {
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                        mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
+                               desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
+                    }
+                }
+                __syncwarp();
+            };
+            auto issue_pv = [&](int i, int s, bool acc) {
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < kBlockN / 16; ++kk)
+                        mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
+                               desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
+                               (acc || kk > 0) ? 1u : 0u);
+                }
+                __syncwarp();
+            };
+            auto commit = [&](uint64_t* b) {
+                if (lane == 0) tc_commit(b);
+                __syncwarp();
+            };
+
+            bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, ctl, kErrTimeoutQ));
+            int sK = 0, sV = 0;
+            if (ok) ok = next_stage(sK);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, sK);
+                commit(&s_full[0]);
+                issue_s(1, sK);
+                commit(&s_full[1]);
+                commit(&kv_empty[sK]);
+                issued = true;
+            }
+            for (int j = 0; j < n_iter && ok; ++j) {
+                const bool more = j + 1 < n_iter;
+                if (!(ok = next_stage(sV))) break;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[0], j & 1, ctl, kErrTimeoutP)))) break;
+                tc_fence_after();
+                issue_pv(0, sV, j > 0);
+                if (!more) commit(&o_full[0]);
+                int sK2 = 0;
+                if (more) {
+                    if (!(ok = next_stage(sK2))) break;
+                    issue_s(0, sK2);
+                    commit(&s_full[0]);
+                }
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[1], j & 1, ctl, kErrTimeoutP)))) break;
+                tc_fence_after();
+                issue_pv(1, sV, j > 0);
+                commit(&kv_empty[sV]);
+                if (!more) {
+                    commit(&o_full[1]);
+                } else {
+                    issue_s(1, sK2);
+                    commit(&s_full[1]);
+                    commit(&kv_empty[sK2]);
+                }
+            }
+            if (issued) {
+                // every MMA issued above must retire before the TMEM is released
+                commit(drain);
+                mbar_wait(drain, 0, ctl, kErrTimeoutDrain, false);
+            }
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ softmax / correction / epilogue
+        const int wg = (warp - 4) >> 2;
+        const int r = ((warp & 3) << 5) + lane;          // TMEM lane = row within the Q tile
+        const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
+        const bool row_valid = qrow < p.Lq;
+        const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lane_addr + wg * 128;
+        const uint32_t tO = tmem + lane_addr + 256 + wg * 128;
+        const int g = wg * 2 + (r >> 6);                 // 64-row group of this row within the CTA
+        const uint16_t* mrow = nullptr;
+        if (p.mask && row_valid)
+            mrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const char*>(p.mask) +
+                                                     (long long)(n % p.mn) * p.m_nb3 +
+                                                     (long long)(h % p.mh) * p.m_nb2 + (long long)qrow * p.m_nb1);
+        const float sl2 = p.scale_log2;
+
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_iter; ++j) {
+            const uint32_t e = list[j];
+            const int kbase = (int)(e >> 16) * kBlockN;
+            const uint32_t c0 = (e >> (4 * g)) & 3u, c1 = (e >> (4 * g + 2)) & 3u;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], j & 1, ctl, kErrTimeoutS)))) break;
+            tc_fence_after();
+
+            // Mixed tiles: add the additive mask (divided by scale, so that scale*(s + m/scale) =
+            // scale*s + m) into S in TMEM, 32 columns at a time.  c0/c1 are warp-uniform (a warp's
+            // 32 rows lie in one 64-row group).
+            if (c0 == kTileMixed || c1 == kTileMixed) {
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    if ((c < 2 ? c0 : c1) != kTileMixed) continue;
+                    uint32_t x[32];
+                    tmem_ld32_sync(tS + c * 32, x);
+                    if (mrow) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int key = kbase + c * 32 + i;
+                            if (key < lk_eff) {
+                                const float mv = __half2float(__ushort_as_half(__ldg(mrow + key)));
+                                x[i] = __float_as_uint(fmaf(mv, p.inv_scale, __uint_as_float(x[i])));
+                            }
+                        }
+                    }
+                    tmem_st32(tS + c * 32, x);
+                }
+                tmem_wait_st();
+            }
+            uint32_t su[128];
+            tmem_ld128_sync(tS, su);
+            // Skipped halves and keys past the valid length become -inf.
+            {
+                const int lim = lk_eff - kbase;
+                const int lim0 = c0 == kTileSkip ? 0 : lim;
+                const int lim1 = c1 == kTileSkip ? 0 : lim;
+                if (lim0 < 64 || lim1 < 128) {
+#pragma unroll
+                    for (int c = 0; c < 128; ++c)
+                        if (c >= (c < 64 ? lim0 : lim1)) su[c] = __float_as_uint(-INFINITY);
+                }
+            }
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 128; c += 4) {
+                mx0 = fmaxf(mx0, __uint_as_float(su[c]));
+                mx1 = fmaxf(mx1, __uint_as_float(su[c + 1]));
+                mx2 = fmaxf(mx2, __uint_as_float(su[c + 2]));
+                mx3 = fmaxf(mx3, __uint_as_float(su[c + 3]));
+            }
+            const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+            const float m_new = fmaxf(m, m_tile);
+            const bool resc = m_new > m + kRescaleThreshold;
+            const bool warp_resc = __any_sync(0xffffffffu, resc);
+            float alpha = 1.0f;
+            if (resc) {
+                alpha = ex2_approx(m - m_new);
+                l *= alpha;
+                m = m_new;
+            }
+            const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+            float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float a = ex2_approx(fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu));
+                    const float b = ex2_approx(fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu));
+                    rs0 += a;
+                    rs1 += b;
+                    pk[i] = Pack2<T>::pack(a, b);
+                }
+                tmem_st16(tS + c * 16, pk);
+            }
+            // Rescale O_i (PV_i(j-1) is complete: its commit preceded S_i(j)'s).  Done after P so
+            // the 128 score registers are dead; it only has to precede the p_full arrive.
+            if (warp_resc && j > 0) {
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32_sync(tO + c * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
+            tmem_wait_st();
+            l += rs0 + rs1;
+            tc_fence_before();
+            mbar_arrive(&p_full[wg]);
+        }
+
+        if (ok) {
+            TO* orow = nullptr;
+            if (row_valid)
+                orow = reinterpret_cast<TO*>(reinterpret_cast<char*>(p.out) + (long long)n * p.o_nb3 +
+                                             (long long)qrow * p.o_nb2 + (long long)h * p.o_nb1);
+            if (n_iter > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&o_full[wg], 0, ctl, kErrTimeoutO));
+                if (ok) {
+                    tc_fence_after();
+                    const float inv = l > 0.f ? 1.0f / l : 0.f;
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32_sync(tO + c * 32, o);
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
+                        if (orow) store_row32<TO>(orow + c * 32, v);
+                    }
+                }
+            } else if (orow) {
+                float z[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) z[i] = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) store_row32<TO>(orow + c * 32, z);
+            }
+            if (ok && row_valid && p.lse)
+                p.lse[((long long)n * p.H + h) * p.Lq + qrow] = (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <typename T, typename TO>
+cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const FmhaParams& p,
+                     cudaStream_t st) {
+    auto kern = fmha_fwd_kernel<T, TO>;
+    // set on every launch: the attribute belongs to the current device, and the call is cheap
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+    if (e != cudaSuccess) return e;
+    dim3 grid((p.Lq + kRowsPerCta - 1) / kRowsPerCta, p.H, p.N);
+    kern<<<grid, kThreads, kSmemAlloc, st>>>(tmQ, tmK, tmV, p);
+    return cudaGetLastError();
+}
+
+template <typename T, typename TO>
+int regs_t() {
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO>) != cudaSuccess) return -1;
+    return a.numRegs;
+}
+
+}  // namespace
+
+int fmha_smem_bytes() { return kSmemAlloc; }
+
+cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                        const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st) {
+    if (op == OpType::BF16) {
+        if (ot == OutType::F32) return launch_t<__nv_bfloat16, float>(tmQ, tmK, tmV, p, st);
+        if (ot == OutType::BF16) return launch_t<__nv_bfloat16, __nv_bfloat16>(tmQ, tmK, tmV, p, st);
+        return launch_t<__nv_bfloat16, __half>(tmQ, tmK, tmV, p, st);
+    }
+    if (ot == OutType::F32) return launch_t<__half, float>(tmQ, tmK, tmV, p, st);
+    if (ot == OutType::BF16) return launch_t<__half, __nv_bfloat16>(tmQ, tmK, tmV, p, st);
+    return launch_t<__half, __half>(tmQ, tmK, tmV, p, st);
+}
+
+int fmha_num_regs(OpType op, OutType ot) {
+    if (op == OpType::BF16) {
+        if (ot == OutType::F32) return regs_t<__nv_bfloat16, float>();
+        if (ot == OutType::BF16) return regs_t<__nv_bfloat16, __nv_bfloat16>();
+        return regs_t<__nv_bfloat16, __half>();
+    }
+    if (ot == OutType::F32) return regs_t<__half, float>();
+    if (ot == OutType::BF16) return regs_t<__half, __nv_bfloat16>();
+    return regs_t<__half, __half>();
+}
+
+}  // namespace kd

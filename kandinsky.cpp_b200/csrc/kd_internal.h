@@ -1,0 +1,101 @@
+// kd_internal.h -- declarations shared between the host API (kd_api.cu) and
+// the kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kd {
+
+// Tile classes of the additive mask, per 64 x 64 (query x key) tile.
+enum : uint8_t { kTileSkip = 0, kTileFull = 1, kTileMixed = 2 };
+
+// Flash-attention forward geometry (sm_100a kernel in kd_fmha.cu).
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;   // query rows per Q tile = one M=128 tcgen05 MMA
+constexpr int kQTiles = 2;     // Q tiles per CTA, one softmax warpgroup each
+constexpr int kRowsPerCta = kBlockM * kQTiles;
+constexpr int kBlockN = 128;   // keys per K/V tile
+constexpr int kMaxKvTiles = 4096;  // per-CTA kept-tile list capacity (Lk <= 524288)
+
+struct FmhaParams {
+    int Lq, Lk, H, N;        // query rows, keys, heads, sequences
+    int rk2, rk3;            // H / Hkv, N / Nkv (ggml broadcast ratios)
+    float scale_log2;        // scale * log2(e)
+    float inv_scale;         // 1 / scale (mask values are folded into raw scores)
+    void* out;               // [D, H, Lq, N]
+    long long o_nb1, o_nb2, o_nb3;  // byte strides of out (head, row, sequence)
+    float* lse;              // [N, H, Lq] or null
+    const uint8_t* tile_cls; // [mn][mh][n_qb][n_kb] or null
+    int n_qb, n_kb;
+    const uint16_t* mask;    // f16 bits [.., Lk] rows, or null
+    long long m_nb1, m_nb2, m_nb3;
+    int mh, mn;
+    const int32_t* kv_len;   // [N] or null
+    unsigned* err;           // sticky device error word
+    unsigned* abort_flag;    // per-launch abort flag (cleared by the host before each launch)
+    unsigned long long wait_ns;
+};
+
+enum class OpType { F16, BF16 };
+enum class OutType { F32, F16, BF16 };
+
+// Launches the tcgen05 flash-attention forward.  tmQ/tmK/tmV are 4-D tiled
+// tensor maps over [128, L, heads, seqs] with a {64, 128, 1, 1} box and
+// 128-byte swizzle.
+cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                        const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st);
+int fmha_smem_bytes();
+// Register count the compiler gave the kernel (the host refuses to launch if it is not the expected one).
+int fmha_num_regs(OpType op, OutType ot);
+
+// ---------------------------------------------------------------- prologue
+struct RopeTab {
+    float freq[64];          // per rotary pair: theta^(-i/half_axis), computed like rope.hpp:23-29
+    float div[64];           // scale_factor of the pair's axis
+    unsigned char axis[64];  // 0 = t, 1 = h, 2 = w
+    int grid_h, grid_w;      // token -> (t,h,w): t = l/(gh*gw), h = (l/gw)%gh, w = l%gw
+};
+
+struct PrologueParams {
+    const float* x;          // [C, L, N] f32
+    long long x_nb1, x_nb2;  // byte strides of x (token, sequence); dim 0 contiguous
+    void* y;                 // [128, L, H, N]
+    long long y_nb1, y_nb2, y_nb3;  // byte strides (row, head, sequence)
+    int L, N, H;
+    int norm;                // 1: RMSNorm
+    const float* gain;       // [128] or null (unit gain)
+    float eps;
+    int rope;                // 1: apply RoPE with `tab`
+    RopeTab tab;
+};
+cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st);
+
+// Rounds a strided [128, L, H, N] f32/f16/bf16 tensor to the operand type, contiguous.
+struct ConvertParams {
+    const void* src; int src_type;   // kd_attn_type id
+    long long nb1, nb2, nb3;
+    void* dst;                       // contiguous [128, L, H, N]
+    int L, H, N;
+};
+cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st);
+
+// Classifies each 64x64 tile of an f16 additive mask as skip / full / mixed.
+struct MaskClassParams {
+    const uint16_t* mask;
+    long long nb1, nb2, nb3;         // byte strides (query row, head plane, sequence plane)
+    int Lq, Lk, mh, mn;
+    uint8_t* cls;                    // [mn][mh][n_qb][n_kb]
+    int n_qb, n_kb;
+};
+cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st);
+
+cudaError_t launch_randn(float* dst, unsigned long long n, unsigned long long seed, unsigned offset, int num_sms,
+                         cudaStream_t st);
+
+// Rank-major gathered shards [R][N*Lq][Hs*128] -> [N*Lq][R*Hs*128] (elt bytes 2 or 4).
+cudaError_t launch_unshard_heads(const void* src, void* dst, long long rows, int ranks, long long shard_row_bytes,
+                                 int num_sms, cudaStream_t st);
+
+}  // namespace kd

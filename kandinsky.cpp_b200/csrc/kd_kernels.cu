@@ -1,0 +1,271 @@
+// kd_kernels.cu -- the HBM-bound kernels around the attention core:
+//   - prologue: RMSNorm per head + 3D RoPE + cast + permute in one pass
+//     (replaces crossdit.hpp:132-141 and ops.hpp:122-131,167-169);
+//   - Q rounding to the operand type (ggml rounds f32 Q to K's dot type);
+//   - classification of an f16 additive mask into 64 x 64 skip/full/mixed tiles;
+//   - Philox4x32-10 + Box-Muller fill (src/rng.hpp:51-69 counter layout);
+//   - the permute that follows the head all-gather.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kd_common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+
+namespace {
+
+template <typename TO>
+__device__ __forceinline__ void store4(void* dst, float a, float b, float c, float d);
+template <>
+__device__ __forceinline__ void store4<float>(void* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(void* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(Pack2<__nv_bfloat16>::pack(a, b), Pack2<__nv_bfloat16>::pack(c, d));
+}
+template <>
+__device__ __forceinline__ void store4<__half>(void* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(Pack2<__half>::pack(a, b), Pack2<__half>::pack(c, d));
+}
+
+// One warp per (sequence n, token l, head h) row of 128 values; lane owns
+// elements 4*lane .. 4*lane+3, i.e. rotary pairs 2*lane and 2*lane+1.
+// RMSNorm follows ggml's CPU rms_norm: squares formed in float, summed in
+// double, mean rounded to float, scale = 1/sqrtf(mean + eps), y = x*scale*g.
+// RoPE follows rope::apply (rope.hpp:140-141): x0' = x0*c - x1*s,
+// x1' = x0*s + x1*c, each product rounded separately (no contraction).
+template <typename TO>
+__global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    const long long rows = (long long)p.N * p.L * p.H;
+    for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
+         row += warps) {
+        const int h = (int)(row % p.H);
+        const long long nl = row / p.H;
+        const int l = (int)(nl % p.L);
+        const int n = (int)(nl / p.L);
+        const float* src = reinterpret_cast<const float*>(reinterpret_cast<const char*>(p.x) + (long long)n * p.x_nb2 +
+                                                          (long long)l * p.x_nb1) +
+                           h * kHeadDim;
+        float4 v = __ldg(reinterpret_cast<const float4*>(src) + lane);
+        if (p.norm) {
+            double ss = (double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y) + (double)__fmul_rn(v.z, v.z) +
+                        (double)__fmul_rn(v.w, v.w);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float mean = (float)(ss / (double)kHeadDim);
+            const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, p.eps)));
+            v.x = __fmul_rn(v.x, scale);
+            v.y = __fmul_rn(v.y, scale);
+            v.z = __fmul_rn(v.z, scale);
+            v.w = __fmul_rn(v.w, scale);
+            if (p.gain) {
+                const float4 g = __ldg(reinterpret_cast<const float4*>(p.gain) + lane);
+                v.x = __fmul_rn(v.x, g.x);
+                v.y = __fmul_rn(v.y, g.y);
+                v.z = __fmul_rn(v.z, g.z);
+                v.w = __fmul_rn(v.w, g.w);
+            }
+        }
+        if (p.rope) {
+            const int hw = p.tab.grid_h * p.tab.grid_w;
+            const int pos[3] = {l / hw, (l / p.tab.grid_w) % p.tab.grid_h, l % p.tab.grid_w};
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int pi = 2 * lane + k;
+                const float ang = __fdiv_rn(__fmul_rn((float)pos[p.tab.axis[pi]], p.tab.freq[pi]), p.tab.div[pi]);
+                float s, c;
+                sincosf(ang, &s, &c);
+                const float x0 = k ? v.z : v.x, x1 = k ? v.w : v.y;
+                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+                if (k) { v.z = y0; v.w = y1; } else { v.x = y0; v.y = y1; }
+            }
+        }
+        char* dst = reinterpret_cast<char*>(p.y) + (long long)n * p.y_nb3 + (long long)h * p.y_nb2 +
+                    (long long)l * p.y_nb1 + (long long)lane * 4 * sizeof(TO);
+        store4<TO>(dst, v.x, v.y, v.z, v.w);
+    }
+}
+
+__device__ __forceinline__ float load_elt(const void* base, long long idx, int type) {
+    if (type == 0) return __ldg(reinterpret_cast<const float*>(base) + idx);
+    const unsigned short b = __ldg(reinterpret_cast<const unsigned short*>(base) + idx);
+    if (type == 1) return __half2float(__ushort_as_half(b));
+    return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// One warp per 128-element row; the source row is contiguous (nb0 = element size).
+template <typename TD>
+__global__ void __launch_bounds__(256) convert_q_kernel(const ConvertParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    const long long rows = (long long)p.N * p.H * p.L;
+    const int esz = p.src_type == 0 ? 4 : 2;
+    for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
+         row += warps) {
+        const int l = (int)(row % p.L);
+        const long long nh = row / p.L;
+        const int h = (int)(nh % p.H);
+        const int n = (int)(nh / p.H);
+        const char* src = reinterpret_cast<const char*>(p.src) + (long long)n * p.nb3 + (long long)h * p.nb2 +
+                          (long long)l * p.nb1;
+        float a = load_elt(src, 4 * lane + 0, p.src_type), b = load_elt(src, 4 * lane + 1, p.src_type);
+        float c = load_elt(src, 4 * lane + 2, p.src_type), d = load_elt(src, 4 * lane + 3, p.src_type);
+        (void)esz;
+        char* dst = reinterpret_cast<char*>(p.dst) + (row * kHeadDim + 4 * lane) * (long long)sizeof(TD);
+        store4<TD>(dst, a, b, c, d);
+    }
+}
+
+// grid (n_qb, mh*mn); 8 warps per block.  Each warp scans 8 of the 64 rows of
+// the query block; per 64-key tile the block records whether every in-range
+// element is -inf (skip) or +-0 (full).  Elements outside [0,Lq) x [0,Lk) are
+// ignored; a tile with no in-range element is a skip tile.
+__global__ void __launch_bounds__(256) mask_classify_kernel(const MaskClassParams p) {
+    extern __shared__ unsigned flags[];  // per key tile: bit0 all -inf, bit1 all zero
+    const int qb = blockIdx.x;
+    const int plane = blockIdx.y;
+    const int mhi = plane % p.mh, mni = plane / p.mh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int kb = threadIdx.x; kb < p.n_kb; kb += blockDim.x) flags[kb] = 3u;
+    __syncthreads();
+    const char* base = reinterpret_cast<const char*>(p.mask) + (long long)mni * p.nb3 + (long long)mhi * p.nb2;
+    for (int kb = 0; kb < p.n_kb; ++kb) {
+        bool all_inf = true, all_zero = true;
+        for (int rr = warp; rr < 64; rr += 8) {
+            const int q = qb * 64 + rr;
+            if (q >= p.Lq) break;
+            const uint16_t* row = reinterpret_cast<const uint16_t*>(base + (long long)q * p.nb1);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = kb * 64 + 2 * lane + e;
+                if (key < p.Lk) {
+                    const uint16_t b = __ldg(row + key);
+                    all_inf &= (b == 0xFC00u);
+                    all_zero &= ((b & 0x7FFFu) == 0u);
+                }
+            }
+        }
+        const unsigned wi = __all_sync(0xffffffffu, all_inf) ? 1u : 0u;
+        const unsigned wz = __all_sync(0xffffffffu, all_zero) ? 2u : 0u;
+        if (lane == 0 && (wi | wz) != 3u) atomicAnd(&flags[kb], wi | wz);
+    }
+    __syncthreads();
+    uint8_t* out = p.cls + ((long long)plane * p.n_qb + qb) * p.n_kb;
+    for (int kb = threadIdx.x; kb < p.n_kb; kb += blockDim.x) {
+        const unsigned f = flags[kb];
+        out[kb] = (f & 1u) ? kTileSkip : ((f & 2u) ? kTileFull : kTileMixed);
+    }
+}
+
+// Philox4x32-10 (Salmon et al. 2011) with the counter/key layout of
+// PhiloxRNG::randn (rng.hpp:51-69) and Box-Muller (rng.hpp:130-134).
+__global__ void randn_kernel(float* dst, unsigned long long n, unsigned long long seed, unsigned offset) {
+    const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+    for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        unsigned c0 = offset, c1 = 0, c2 = (unsigned)i, c3 = 0;
+        unsigned k0 = (unsigned)(seed & 0xffffffffull), k1 = (unsigned)(seed >> 32);
+#pragma unroll
+        for (int r = 0; r < 10; ++r) {
+            const unsigned long long p0 = (unsigned long long)c0 * 0xD2511F53ull;
+            const unsigned long long p1 = (unsigned long long)c2 * 0xCD9E8D57ull;
+            const unsigned n0 = (unsigned)(p1 >> 32) ^ c1 ^ k0;
+            const unsigned n1 = (unsigned)p1;
+            const unsigned n2 = (unsigned)(p0 >> 32) ^ c3 ^ k1;
+            const unsigned n3 = (unsigned)p0;
+            c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+            if (r < 9) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+        }
+        const float inv32 = 2.3283064e-10f;
+        const float inv32_2pi = 2.3283064e-10f * 6.2831855f;
+        const float u = __fadd_rn(__fmul_rn((float)c0, inv32), inv32 / 2);
+        const float v = __fadd_rn(__fmul_rn((float)c1, inv32_2pi), inv32_2pi / 2);
+        dst[i] = __fmul_rn(sqrtf(-2.0f * logf(u)), sinf(v));
+    }
+}
+
+// dst row r = concat over ranks k of src[k][r] (each shard_row_bytes long, 16-byte multiple).
+__global__ void unshard_kernel(const uint4* src, uint4* dst, long long rows, int ranks, long long shard_u4) {
+    const long long total = rows * ranks * shard_u4;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const long long w = i % shard_u4;
+        const long long rk = i / shard_u4;
+        const int k = (int)(rk % ranks);
+        const long long r = rk / ranks;
+        dst[i] = src[((long long)k * rows + r) * shard_u4 + w];
+    }
+}
+
+int grid_for(long long warps_needed, int num_sms) {
+    long long blocks = (warps_needed + 7) / 8;
+    long long cap = (long long)num_sms * 16;
+    if (blocks > cap) blocks = cap;
+    return (int)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace
+
+cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st) {
+    const long long rows = (long long)p.N * p.L * p.H;
+    if (rows == 0) return cudaSuccess;
+    const int grid = grid_for(rows, num_sms);
+    if (yt == OutType::BF16)
+        prologue_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else if (yt == OutType::F16)
+        prologue_kernel<__half><<<grid, 256, 0, st>>>(p);
+    else
+        prologue_kernel<float><<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st) {
+    const long long rows = (long long)p.N * p.H * p.L;
+    if (rows == 0) return cudaSuccess;
+    const int grid = grid_for(rows, num_sms);
+    if (dt == OpType::BF16)
+        convert_q_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else
+        convert_q_kernel<__half><<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st) {
+    if (p.n_qb == 0 || p.n_kb == 0) return cudaSuccess;
+    const size_t smem = (size_t)p.n_kb * sizeof(unsigned);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(mask_classify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid(p.n_qb, p.mh * p.mn);
+    mask_classify_kernel<<<grid, 256, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_randn(float* dst, unsigned long long n, unsigned long long seed, unsigned offset, int num_sms,
+                         cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    long long blocks = (long long)((n + 255) / 256);
+    if (blocks > (long long)num_sms * 32) blocks = (long long)num_sms * 32;
+    randn_kernel<<<(int)blocks, 256, 0, st>>>(dst, n, seed, offset);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_unshard_heads(const void* src, void* dst, long long rows, int ranks, long long shard_row_bytes,
+                                 int num_sms, cudaStream_t st) {
+    const long long shard_u4 = shard_row_bytes / 16;
+    const long long total = rows * ranks * shard_u4;
+    if (total == 0) return cudaSuccess;
+    long long blocks = (total + 255) / 256;
+    if (blocks > (long long)num_sms * 32) blocks = (long long)num_sms * 32;
+    unshard_kernel<<<(int)blocks, 256, 0, st>>>(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst),
+                                                rows, ranks, shard_u4);
+    return cudaGetLastError();
+}
+
+}  // namespace kd

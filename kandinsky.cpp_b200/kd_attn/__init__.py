@@ -1,0 +1,294 @@
+"""kd_attn -- Python host side of libkd_attn (include/kd_attn.h) over ctypes.
+
+Mirrors the operator interface of kandinsky.cpp's attention path:
+  - ``attention(...)``       ops::attention flash branch (src/core/ops.hpp:107-207)
+  - ``self_attention(...)``  DiTSelfAttention::forward core (src/models/crossdit.hpp:117-154)
+  - ``cross_attention(...)`` DiTCrossAttention::forward core (src/models/crossdit.hpp:174-200)
+  - ``flash_attn_ext(...)``  ggml_flash_attn_ext operator semantics (called at ops.hpp:176)
+  - ``prologue(...)``        RMSNorm + RoPE + cast + permute (crossdit.hpp:132-141, rope.hpp:109-155)
+with torch tensors as device buffers (PyTorch is only the allocator and the
+stream provider here).  The compute always runs in libkd_attn.so; if that
+library is missing this module raises at import -- there is no fallback.
+
+Layout convention: a ggml tensor with sizes ne = (ne0, ne1, ne2, ne3) is the
+torch tensor of shape (ne3, ne2, ne1, ne0); ``KdTensor.of`` converts shape and
+strides accordingly (dim 0 = the last torch dim).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkd_attn.so")
+
+# status codes (kd_attn_status)
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED = -2
+ERR_CUDA = -3
+ERR_OUT_OF_MEMORY = -4
+ERR_DEVICE_TIMEOUT = -5
+ERR_NCCL = -6
+
+# ggml type ids (kd_attn_type)
+F32, F16, BF16 = 0, 1, 30
+
+EXPORTED = [
+    "kd_attn_create", "kd_attn_destroy", "kd_attn_last_error", "kd_attn_device_status",
+    "kd_attn_prologue", "kd_attn_flash_ext", "kd_attn_self_attention", "kd_attn_cross_attention",
+    "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
+]
+
+
+class KdAttnError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"kd_attn status {status}: {msg}")
+        self.status = status
+
+
+class KdTensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("type", ctypes.c_int32),
+                ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4)]
+
+    @staticmethod
+    def of(t):
+        """kd_tensor view of a torch tensor (ggml ne/nb from torch shape/strides, reversed)."""
+        import torch
+        types = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+        if t.dtype not in types:
+            raise TypeError(f"unsupported dtype {t.dtype}")
+        if t.dim() > 4:
+            raise ValueError("at most 4 dims")
+        es = t.element_size()
+        shape = list(reversed(t.shape))      # ggml order: dim 0 fastest
+        strides = list(reversed(t.stride()))
+        k = KdTensor()
+        k.data = t.data_ptr() if t.numel() else None
+        k.type = types[t.dtype]
+        for i in range(4):
+            if i < t.dim():
+                k.ne[i] = shape[i]
+                k.nb[i] = strides[i] * es
+            else:  # missing outer dims: size 1 with the packed stride
+                k.ne[i] = 1
+                k.nb[i] = k.nb[i - 1] * k.ne[i - 1] if i > 0 else es
+        return k
+
+
+class Rope3D(ctypes.Structure):
+    """kd_rope3d: 3D (t,h,w) RoPE of rope.hpp:56-102, computed on the fly."""
+    _fields_ = [("axes_dim", ctypes.c_int32 * 3), ("grid", ctypes.c_int32 * 3),
+                ("scale_factor", ctypes.c_float * 3), ("theta", ctypes.c_float)]
+
+    @staticmethod
+    def make(grid, axes=(32, 48, 48), scale=(1.0, 1.0, 1.0), theta=10000.0):
+        r = Rope3D()
+        for i in range(3):
+            r.axes_dim[i] = int(axes[i])
+            r.grid[i] = int(grid[i])
+            r.scale_factor[i] = float(scale[i])
+        r.theta = float(theta)
+        return r
+
+
+LOG_CB = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_char_p, ctypes.c_void_p)
+
+
+class _Init(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("nccl_unique_id", ctypes.c_void_p), ("log_cb", LOG_CB), ("log_user_data", ctypes.c_void_p)]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with kandinsky.cpp_b200/build.py "
+                          "(libkd_attn has no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, T = ctypes.c_void_p, ctypes.POINTER(KdTensor)
+    st = ctypes.c_int
+    L.kd_attn_create.argtypes = [ctypes.POINTER(_Init), ctypes.POINTER(ctypes.c_void_p)]
+    L.kd_attn_create.restype = st
+    L.kd_attn_destroy.argtypes = [P]
+    L.kd_attn_destroy.restype = None
+    L.kd_attn_last_error.argtypes = [P]
+    L.kd_attn_last_error.restype = ctypes.c_char_p
+    L.kd_attn_device_status.argtypes = [P, P]
+    L.kd_attn_device_status.restype = st
+    L.kd_attn_prologue.argtypes = [P, T, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_float,
+                                   ctypes.POINTER(Rope3D), T, P]
+    L.kd_attn_prologue.restype = st
+    L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, T, P, P]
+    L.kd_attn_flash_ext.restype = st
+    L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
+                                         ctypes.POINTER(Rope3D), ctypes.c_int32, T, P, P]
+    L.kd_attn_self_attention.restype = st
+    L.kd_attn_cross_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float, T, P,
+                                          ctypes.c_int32, T, P, P]
+    L.kd_attn_cross_attention.restype = st
+    L.kd_attn_allgather_heads.argtypes = [P, T, T, P]
+    L.kd_attn_allgather_heads.restype = st
+    L.kd_attn_fill_randn.argtypes = [P, P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32, P]
+    L.kd_attn_fill_randn.restype = st
+    L.kd_attn_nccl_unique_id.argtypes = [P]
+    L.kd_attn_nccl_unique_id.restype = st
+    L.kd_attn_version.argtypes = []
+    L.kd_attn_version.restype = ctypes.c_int32
+    return L
+
+
+lib = _load()
+
+
+def version():
+    v = lib.kd_attn_version()
+    return (v >> 16, v & 0xFFFF)
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    rc = lib.kd_attn_nccl_unique_id(buf)
+    if rc != OK:
+        raise KdAttnError(rc, "ncclGetUniqueId failed")
+    return buf.raw
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _ref(t):
+    return None if t is None else ctypes.byref(KdTensor.of(t))
+
+
+class Context:
+    """kd_attn_ctx: per-device state (operand scratch, error words, NCCL communicator)."""
+
+    def __init__(self, device=0, n_ranks=1, rank=0, nccl_id: bytes | None = None, log=None):
+        init = _Init()
+        init.device, init.n_ranks, init.rank = int(device), int(n_ranks), int(rank)
+        self._id_buf = None
+        if nccl_id is not None:
+            self._id_buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            init.nccl_unique_id = ctypes.cast(self._id_buf, ctypes.c_void_p)
+        self._cb = LOG_CB(lambda lvl, txt, _u: log(lvl, txt.decode())) if log else LOG_CB()
+        init.log_cb = self._cb
+        h = ctypes.c_void_p()
+        rc = lib.kd_attn_create(ctypes.byref(init), ctypes.byref(h))
+        if rc != OK:
+            raise KdAttnError(rc, f"kd_attn_create(device={device}) failed")
+        self.handle = h
+        self.device = int(device)
+        self.n_ranks = int(n_ranks)
+        self.rank = int(rank)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.kd_attn_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def check(self, rc):
+        if rc != OK:
+            raise KdAttnError(rc, lib.kd_attn_last_error(self.handle).decode())
+
+    def device_status(self, stream=None):
+        """Synchronise and read/clear the device error word (bounded-wait timeouts)."""
+        self.check(lib.kd_attn_device_status(self.handle, _stream_ptr(stream)))
+
+    # -------------------------------------------------------------- entry points
+    def prologue(self, x, n_head, y, norm=True, gain=None, eps=1e-6, rope=None, stream=None):
+        """x: (N, L, C) f32 -> y: (N, n_head, L, 128) f32/f16/bf16 (ggml [128, L, H, N])."""
+        self.check(lib.kd_attn_prologue(self.handle, _ref(x), int(n_head), 1 if norm else 0, _ptr(gain),
+                                        float(eps), None if rope is None else ctypes.byref(rope), _ref(y),
+                                        _stream_ptr(stream)))
+        return y
+
+    def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
+                       logit_softcap=0.0, stream=None):
+        """ggml_flash_attn_ext.  q: (N, H, Lq, 128); k, v: (Nkv, Hkv, Lk, 128);
+        mask: (mn, mh, >=Lq, >=Lk) f16 or None; out: (N, Lq, H, 128); lse: (N, H, Lq) f32 or None."""
+        if scale is None:
+            scale = 1.0 / (q.shape[-1] ** 0.5)
+        self.check(lib.kd_attn_flash_ext(self.handle, _ref(q), _ref(k), _ref(v), _ref(mask), float(scale),
+                                         float(max_bias), float(logit_softcap), _ptr(kv_len), _ref(out), _ptr(lse),
+                                         _stream_ptr(stream)))
+        return out
+
+    def self_attention(self, q_in, k_in, v_in, n_head, out, rope=None, q_gain=None, k_gain=None, eps=1e-6,
+                       op_type=BF16, lse=None, stream=None):
+        """q_in/k_in/v_in: (N, L, C) f32 -> out (N, L, C) f32/bf16."""
+        self.check(lib.kd_attn_self_attention(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), int(n_head),
+                                              _ptr(q_gain), _ptr(k_gain), float(eps),
+                                              None if rope is None else ctypes.byref(rope), int(op_type), _ref(out),
+                                              _ptr(lse), _stream_ptr(stream)))
+        return out
+
+    def cross_attention(self, q_in, k_in, v_in, n_head, out, mask=None, kv_len=None, q_gain=None, k_gain=None,
+                        eps=1e-6, op_type=BF16, lse=None, stream=None):
+        self.check(lib.kd_attn_cross_attention(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), int(n_head),
+                                               _ptr(q_gain), _ptr(k_gain), float(eps), _ref(mask), _ptr(kv_len),
+                                               int(op_type), _ref(out), _ptr(lse), _stream_ptr(stream)))
+        return out
+
+    def allgather_heads(self, shard, full, stream=None):
+        """shard: (N, Lq, H/n, 128) -> full: (N, Lq, H, 128), one NCCL all-gather + permute."""
+        self.check(lib.kd_attn_allgather_heads(self.handle, _ref(shard), _ref(full), _stream_ptr(stream)))
+        return full
+
+    def fill_randn(self, dst, seed, offset=0, stream=None):
+        """Philox4x32-10 + Box-Muller N(0,1) into a contiguous f32 tensor (rng.hpp:51-69 layout)."""
+        self.check(lib.kd_attn_fill_randn(self.handle, _ptr(dst), dst.numel(), int(seed), int(offset),
+                                          _stream_ptr(stream)))
+        return dst
+
+
+def attention(ctx: Context, q, k, v, n_head, mask=None, flash=True, op_type=F16, out_dtype=None, stream=None):
+    """ops::attention (src/core/ops.hpp:107-207), flash branch, on device tensors.
+
+    q: (N, Lq, C) f32, k, v: (N, Lk, C_kv) f32 -- the [C, L, N] ggml tensors of the reference.
+    Permutes to [d, L, H, N] (ops.hpp:122-131), casts K/V to op_type (ops.hpp:167-169, f16 in the
+    reference), runs flash_attn_ext with scale 1/sqrt(d) (ops.hpp:161,176) and returns (N, Lq, C)
+    (ops.hpp:204-206).  GQA (C_kv < C) is broadcast by the kernel instead of repeated
+    (ops.hpp:135-157).  The causal / non-flash branch is not covered (UNSUPPORTED).
+    """
+    import torch
+    if not flash:
+        raise KdAttnError(ERR_UNSUPPORTED, "only the flash branch of ops::attention is implemented")
+    N, Lq, C = q.shape
+    Lk = k.shape[1]
+    d = C // n_head
+    n_kv = k.shape[2] // d
+    dt = torch.float16 if op_type == F16 else torch.bfloat16
+    qh = q.view(N, Lq, n_head, d).permute(0, 2, 1, 3)           # strided view, rounded by the library
+    # K/V permute + cast (ops.hpp:127-131,167-169) in the library's prologue kernel, no norm/RoPE
+    kh = torch.empty(N, n_kv, Lk, d, device=q.device, dtype=dt)
+    vh = torch.empty(N, n_kv, Lk, d, device=q.device, dtype=dt)
+    ctx.prologue(k, n_kv, kh, norm=False, stream=stream)
+    ctx.prologue(v, n_kv, vh, norm=False, stream=stream)
+    out = torch.empty(N, Lq, n_head, d, device=q.device, dtype=out_dtype or torch.float32)
+    m = None
+    if mask is not None:
+        m = mask.to(torch.float16)
+        while m.dim() < 4:
+            m = m.unsqueeze(0)
+    ctx.flash_attn_ext(qh, kh, vh, out, mask=m, scale=1.0 / d ** 0.5, stream=stream)
+    return out.view(N, Lq, C)

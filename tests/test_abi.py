@@ -1,0 +1,68 @@
+"""The C-ABI library loads and exports every entry point include/kd_attn.h declares (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kd_attn.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:kd_attn_status|void|const char\s*\*|int32_t)\s+(kd_attn_\w+)\s*\(", src,
+                                 flags=re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("kd_attn_create", "kd_attn_destroy", "kd_attn_flash_ext", "kd_attn_prologue",
+                 "kd_attn_self_attention", "kd_attn_cross_attention", "kd_attn_allgather_heads"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(kd):
+    lib = ctypes.CDLL(kd.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert sorted(kd.EXPORTED) == declared_functions()
+
+
+def test_version(kd):
+    assert kd.version() == (0, 1)
+
+
+def test_create_without_gpu_fails_cleanly(kd):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    init = kd._Init()
+    init.device, init.n_ranks, init.rank = 0, 1, 0
+    h = ctypes.c_void_p(1234)
+    rc = kd.lib.kd_attn_create(ctypes.byref(init), ctypes.byref(h))
+    assert rc == kd.ERR_CUDA and not h.value
+
+
+def test_create_rejects_bad_arguments(kd):
+    init = kd._Init()
+    init.device, init.n_ranks, init.rank = 0, 2, 5
+    h = ctypes.c_void_p()
+    assert kd.lib.kd_attn_create(ctypes.byref(init), ctypes.byref(h)) == kd.ERR_INVALID_ARGUMENT
+    assert kd.lib.kd_attn_create(None, ctypes.byref(h)) == kd.ERR_INVALID_ARGUMENT
+    assert kd.lib.kd_attn_flash_ext(None, None, None, None, None, 1.0, 0.0, 0.0, None, None, None, None) == \
+        kd.ERR_INVALID_ARGUMENT
+
+
+def test_kd_tensor_maps_torch_layout_to_ggml(kd):
+    import torch
+    t = torch.empty(2, 32, 100, 128, dtype=torch.bfloat16)      # ggml [128, 100, 32, 2]
+    k = kd.KdTensor.of(t)
+    assert list(k.ne) == [128, 100, 32, 2]
+    assert list(k.nb) == [2, 256, 256 * 100, 256 * 100 * 32]
+    v = t.permute(0, 2, 1, 3)                                   # ggml [128, 32, 100, 2] strided
+    k = kd.KdTensor.of(v)
+    assert list(k.ne) == [128, 32, 100, 2] and list(k.nb) == [2, 256 * 100, 256, 256 * 100 * 32]
+    k = kd.KdTensor.of(torch.empty(5, 7, dtype=torch.float32))
+    assert list(k.ne) == [7, 5, 1, 1] and list(k.nb) == [4, 28, 140, 140]

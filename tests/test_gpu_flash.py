@@ -1,0 +1,233 @@
+"""GPU parity: libkd_attn (through its C ABI) against the CPU oracle on identical seeded inputs."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_gates, lse_err, seeded
+
+pytestmark = pytest.mark.gpu
+
+TT = {oracle.F16: torch.float16, oracle.BF16: torch.bfloat16}
+
+
+def dev(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def op_tensor(a_np, t):
+    """numpy f32 -> device tensor of operand type t, rounded exactly like the oracle (RNE)."""
+    bits = oracle.to_type(a_np, t)
+    if t == oracle.F16:
+        return torch.from_numpy(bits).cuda()
+    return torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+
+
+# ------------------------------------------------------------------ config 0: the tiny self-attention block
+@pytest.mark.parametrize("kv_type", [oracle.F16, oracle.BF16])
+@pytest.mark.parametrize("scale", [(1, 1, 1), (1, 2, 2)])
+def test_config0_self_attention(ctx, kd, kv_type, scale):
+    """1,280 tokens (5x16x16), 32 heads, d128, RMSNorm + 3D RoPE, K/V cast."""
+    N, L, H, d = 1, 1280, 32, 128
+    C = H * d
+    q = seeded((N, L, C), 2024, 0)
+    k = seeded((N, L, C), 2024, 1)
+    v = seeded((N, L, C), 2024, 2)
+    tab = oracle.visual_rope_table((5, 16, 16), scale=scale)
+    exact, lse_ref = oracle.self_attention(q, k, v, H, rope_table=tab, kv_type=kv_type, mode=oracle.EXACT, lse=True)
+    ggml = oracle.self_attention(q, k, v, H, rope_table=tab, kv_type=kv_type, mode=oracle.GGML)
+    out = torch.empty(N, L, C, device="cuda")
+    lse = torch.empty(N, H, L, device="cuda")
+    rope = kd.Rope3D.make((5, 16, 16), scale=scale)
+    ctx.self_attention(dev(q), dev(k), dev(v), H, out, rope=rope, op_type=kv_type, lse=lse)
+    ctx.device_status()
+    assert_gates(out.cpu().numpy(), exact, ggml, lse.cpu().numpy(), lse_ref, label=f"cfg0 {kv_type} {scale}")
+
+
+# ------------------------------------------------------------------ flash_attn_ext on edge shapes
+SHAPES = [  # N, H, Hkv, Lq, Lk
+    (1, 1, 1, 1, 1), (1, 2, 2, 63, 40), (1, 2, 1, 64, 127), (2, 2, 2, 65, 128), (1, 1, 1, 127, 129),
+    (1, 2, 2, 129, 255), (2, 4, 2, 255, 256), (1, 1, 1, 257, 300), (1, 2, 2, 256, 1), (1, 1, 1, 513, 640),
+]
+
+
+@pytest.mark.parametrize("N,H,Hkv,Lq,Lk", SHAPES)
+@pytest.mark.parametrize("kv_type", [oracle.F16, oracle.BF16])
+def test_flash_ext_shapes(ctx, N, H, Hkv, Lq, Lk, kv_type):
+    D = 128
+    qf = seeded((N, H, Lq, D), 7 + Lq, 0)
+    kf = seeded((N, Hkv, Lk, D), 7 + Lq, 1)
+    vf = seeded((N, Hkv, Lk, D), 7 + Lq, 2)
+    kb, vb = oracle.to_type(kf, kv_type), oracle.to_type(vf, kv_type)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, mode=oracle.EXACT, lse=True)
+    out = torch.empty(N, Lq, H, D, device="cuda")
+    lse = torch.empty(N, H, Lq, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, kv_type), op_tensor(vf, kv_type), out, lse=lse)
+    ctx.device_status()
+    assert_gates(out.cpu().numpy(), exact, lse=lse.cpu().numpy(), lse_ref=lse_ref, label=f"{N,H,Hkv,Lq,Lk}")
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_flash_ext_output_types_and_strided_q(ctx, out_dtype):
+    """Q given as the strided f32 view ops::attention builds (permute of [C, L, N]); out in 3 types."""
+    N, L, H, D = 2, 300, 4, 128
+    q_in = seeded((N, L, H * D), 99, 0)
+    kf = seeded((N, H, L, D), 99, 1)
+    vf = seeded((N, H, L, D), 99, 2)
+    kb, vb = oracle.to_type(kf, oracle.BF16), oracle.to_type(vf, oracle.BF16)
+    qf = np.ascontiguousarray(q_in.reshape(N, L, H, D).transpose(0, 2, 1, 3))
+    exact = oracle.flash_attn_ext(qf, kb, vb, mode=oracle.EXACT)
+    qd = dev(q_in).view(N, L, H, D).permute(0, 2, 1, 3)          # strided: ggml [D, L, H, N] view
+    out = torch.empty(N, L, H, D, device="cuda", dtype=out_dtype)
+    ctx.flash_attn_ext(qd, op_tensor(kf, oracle.BF16), op_tensor(vf, oracle.BF16), out)
+    ctx.device_status()
+    assert_gates(out.float().cpu().numpy(), exact, label=str(out_dtype))
+
+
+# ------------------------------------------------------------------ masks, kv_len, fully masked rows
+def _mask_case(kind, N, Lq, Lk, seed):
+    rng = np.random.default_rng(seed)
+    if kind == "random":          # per-element -inf plus finite additive values: mixed tiles
+        m = (rng.normal(size=(N, 1, Lq, Lk)) * 0.5).astype(np.float16)
+        m[rng.random(m.shape) < 0.25] = -np.inf
+    elif kind == "block":         # 64x64 block-sparse with a kept diagonal
+        nb_q, nb_k = (Lq + 63) // 64, (Lk + 63) // 64
+        keep = rng.random((nb_q, nb_k)) < 0.3
+        for i in range(min(nb_q, nb_k)):
+            keep[i, i] = True
+        m = np.where(np.kron(keep, np.ones((64, 64)))[:Lq, :Lk], 0, -np.inf).astype(np.float16)[None, None]
+        m = np.repeat(m, N, axis=0)
+    elif kind == "rows":          # some fully masked rows and a masked head block
+        m = np.zeros((N, 1, Lq, Lk), np.float16)
+        m[:, :, ::7, :] = -np.inf
+        m[:, :, :64, 128:] = -np.inf
+    else:
+        raise ValueError(kind)
+    return m
+
+
+@pytest.mark.parametrize("kind", ["random", "block", "rows"])
+def test_flash_ext_masks(ctx, kind):
+    N, H, Lq, Lk, D = 2, 2, 320, 384, 128
+    qf = seeded((N, H, Lq, D), 31, 0)
+    kf = seeded((N, H, Lk, D), 31, 1)
+    vf = seeded((N, H, Lk, D), 31, 2)
+    kb, vb = oracle.to_type(kf, oracle.F16), oracle.to_type(vf, oracle.F16)
+    mask = _mask_case(kind, N, Lq, Lk, 5)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, mask=mask, mode=oracle.EXACT, lse=True)
+    out = torch.empty(N, Lq, H, D, device="cuda")
+    lse = torch.empty(N, H, Lq, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, oracle.F16), op_tensor(vf, oracle.F16), out,
+                       mask=torch.from_numpy(mask).cuda(), lse=lse)
+    ctx.device_status()
+    got = out.cpu().numpy()
+    assert_gates(got, exact, lse=lse.cpu().numpy(), lse_ref=lse_ref, label=kind)
+    dead = np.isneginf(lse_ref).transpose(0, 2, 1)                   # (N, Lq, H)
+    assert np.all(got[dead] == 0)
+
+
+def test_flash_ext_kv_len(ctx):
+    N, H, Lq, Lk, D = 3, 2, 200, 256, 128
+    qf = seeded((N, H, Lq, D), 41, 0)
+    kf = seeded((N, H, Lk, D), 41, 1)
+    vf = seeded((N, H, Lk, D), 41, 2)
+    kv_len = np.array([40, 256, 0], np.int32)
+    kb, vb = oracle.to_type(kf, oracle.BF16), oracle.to_type(vf, oracle.BF16)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, kv_len=kv_len, mode=oracle.EXACT, lse=True)
+    out = torch.full((N, Lq, H, D), 7.0, device="cuda")
+    lse = torch.empty(N, H, Lq, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, oracle.BF16), op_tensor(vf, oracle.BF16), out,
+                       kv_len=torch.from_numpy(kv_len).cuda(), lse=lse)
+    ctx.device_status()
+    got = out.cpu().numpy()
+    assert np.all(got[2] == 0) and np.all(np.isneginf(lse.cpu().numpy()[2]))
+    assert_gates(got[:2], exact[:2], lse=lse.cpu().numpy()[:2], lse_ref=lse_ref[:2], label="kv_len")
+
+
+def test_mask_broadcast_over_heads_and_sequences(ctx):
+    """mask planes (mh, mn) broadcast as h % mh, n % mn (ggml's rule)."""
+    N, H, Lq, Lk, D = 2, 4, 130, 200, 128
+    qf = seeded((N, H, Lq, D), 51, 0)
+    kf = seeded((N, H, Lk, D), 51, 1)
+    vf = seeded((N, H, Lk, D), 51, 2)
+    rng = np.random.default_rng(1)
+    mask = (rng.normal(size=(1, 2, Lq, Lk))).astype(np.float16)
+    mask[rng.random(mask.shape) < 0.5] = -np.inf
+    kb, vb = oracle.to_type(kf, oracle.F16), oracle.to_type(vf, oracle.F16)
+    exact = oracle.flash_attn_ext(qf, kb, vb, mask=mask, mode=oracle.EXACT)
+    out = torch.empty(N, Lq, H, D, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, oracle.F16), op_tensor(vf, oracle.F16), out,
+                       mask=torch.from_numpy(mask).cuda())
+    ctx.device_status()
+    assert_gates(out.cpu().numpy(), exact, label="broadcast")
+
+
+# ------------------------------------------------------------------ prologue and generator
+@pytest.mark.parametrize("scale", [(1, 1, 1), (1, 2, 2)])
+def test_prologue_matches_oracle(ctx, kd, scale):
+    N, L, H, d = 2, 60, 3, 128
+    x = seeded((N, L, H * d), 61, 0) * 3.0
+    gain = (1.0 + 0.1 * seeded((d,), 61, 1)).astype(np.float32)
+    tab = oracle.visual_rope_table((3, 4, 5), scale=scale)
+    ref = oracle.prologue(x, H, gain=gain, rope_table=tab)                 # (N, H, L, d) f32
+    y = torch.empty(N, H, L, d, device="cuda")
+    ctx.prologue(dev(x), H, y, norm=True, gain=dev(gain), rope=kd.Rope3D.make((3, 4, 5), scale=scale))
+    ctx.device_status()
+    got = y.cpu().numpy()
+    # float ops replicate the reference's; sin/cos may differ by an ulp from the host libm
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-6)
+    yb = torch.empty(N, H, L, d, device="cuda", dtype=torch.bfloat16)
+    ctx.prologue(dev(x), H, yb, norm=True, gain=dev(gain), rope=kd.Rope3D.make((3, 4, 5), scale=scale))
+    rb = oracle.to_f32(oracle.to_type(ref, oracle.BF16), oracle.BF16)
+    diff = np.abs(yb.float().cpu().numpy() - rb)
+    assert np.mean(diff == 0) > 0.999 and np.all(diff <= np.abs(rb) * 2 ** -7 + 1e-30)
+    # V path: no norm, no RoPE: an exact cast + permute
+    yv = torch.empty(N, H, L, d, device="cuda", dtype=torch.float16)
+    ctx.prologue(dev(x), H, yv, norm=False)
+    np.testing.assert_array_equal(yv.cpu().numpy(), x.reshape(N, L, H, d).transpose(0, 2, 1, 3).astype(np.float16))
+
+
+def test_fill_randn_matches_oracle(ctx):
+    n = 1 << 20
+    t = torch.empty(n, device="cuda")
+    ctx.fill_randn(t, seed=42, offset=3)
+    ref = oracle.philox_randn(42, n, 3)
+    got = t.cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)     # libm sin/log/sqrt ulp differences only
+
+
+# ------------------------------------------------------------------ ops::attention mirror
+def test_ops_attention_mirror(ctx, kd):
+    """kd_attn.attention = ops::attention flash branch: [C, L, N] f32 in, f16 K/V, [C, Lq, N] f32 out."""
+    N, Lq, Lk, H, d = 1, 200, 77, 4, 128
+    q = seeded((N, Lq, H * d), 71, 0)
+    k = seeded((N, Lk, H * d), 71, 1)
+    v = seeded((N, Lk, H * d), 71, 2)
+    q4 = np.ascontiguousarray(q.reshape(N, Lq, H, d).transpose(0, 2, 1, 3))
+    k4 = oracle.to_type(np.ascontiguousarray(k.reshape(N, Lk, H, d).transpose(0, 2, 1, 3)), oracle.F16)
+    v4 = oracle.to_type(np.ascontiguousarray(v.reshape(N, Lk, H, d).transpose(0, 2, 1, 3)), oracle.F16)
+    exact = oracle.flash_attn_ext(q4, k4, v4, mode=oracle.EXACT).reshape(N, Lq, H * d)
+    got = kd.attention(ctx, dev(q), dev(k), dev(v), H)
+    ctx.device_status()
+    assert_gates(got.cpu().numpy(), exact, label="ops::attention")
+
+
+# ------------------------------------------------------------------ argument errors come back as statuses
+def test_rejects_unsupported_and_invalid(ctx, kd):
+    q = torch.zeros(1, 2, 16, 64, device="cuda", dtype=torch.float16)
+    out = torch.empty(1, 16, 2, 64, device="cuda")
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.flash_attn_ext(q, q, q, out)
+    assert e.value.status == kd.ERR_UNSUPPORTED
+    q = torch.zeros(1, 2, 16, 128, device="cuda", dtype=torch.float16)
+    bad_out = torch.empty(1, 16, 3, 128, device="cuda")
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.flash_attn_ext(q, q, q, bad_out)
+    assert e.value.status == kd.ERR_INVALID_ARGUMENT
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.flash_attn_ext(q, q, q, torch.empty(1, 16, 2, 128, device="cuda"), max_bias=1.0)
+    assert e.value.status == kd.ERR_UNSUPPORTED
+    ctx.device_status()
