@@ -215,8 +215,18 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override the config's batch (profiling runs)")
+    ap.add_argument("--heads", type=int, default=None, help="override the config's head count (profiling runs)")
+    ap.add_argument("--fa-only", action="store_true",
+                    help="time only the flash-attention kernel on prologue-made operands (profiling runs)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["N"] = args.batch
+    if args.heads:
+        cfg["H"] = args.heads
+    if args.batch or args.heads:
+        cfg["name"] += f" [override B{cfg['N']} H{cfg['H']}]"
 
     if args.impl == "reference":
         run_reference(args, cfg)
@@ -274,6 +284,30 @@ def main():
         if ws > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
+
+    if args.fa_only:
+        qs = torch.empty(N, Hs, L, d, device=dev, dtype=torch.bfloat16 if op == kd_attn.BF16 else torch.float16)
+        ks, vs = torch.empty_like(qs), torch.empty_like(qs)
+        ctx.prologue(q, Hs, qs, norm=True, rope=rope, stream=stream)
+        ctx.prologue(k, Hs, ks, norm=True, rope=rope, stream=stream)
+        ctx.prologue(v, Hs, vs, norm=False, stream=stream)
+        o4 = out_shard.view(N, L, Hs, d)
+        for _ in range(max(args.warmup, 3)):
+            ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream)
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ctx.device_status()
+        fms = a.elapsed_time(b) / args.steps
+        if rank == 0:
+            print(json.dumps({"fa_only": True, "workload": cfg["name"], "ms": fms,
+                              "tflops": 4.0 * N * Hs * L * L * d / (fms * 1e-3) / 1e12}), flush=True)
+        ctx.close()
+        return
 
     for _ in range(max(args.warmup, 3)):
         step()

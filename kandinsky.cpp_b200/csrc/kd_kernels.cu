@@ -30,64 +30,86 @@ __device__ __forceinline__ void store4<__half>(void* dst, float a, float b, floa
     *reinterpret_cast<uint2*>(dst) = make_uint2(Pack2<__half>::pack(a, b), Pack2<__half>::pack(c, d));
 }
 
-// One warp per (sequence n, token l, head h) row of 128 values; lane owns
-// elements 4*lane .. 4*lane+3, i.e. rotary pairs 2*lane and 2*lane+1.
+constexpr int kPrologueHeads = 4;  // heads per warp work item: 4 row loads in flight, one sin/cos per token
+
+__device__ __forceinline__ float pick_pos(int axis, int t, int h, int w) { return (float)(axis == 0 ? t : (axis == 1 ? h : w)); }
+
+// One warp per (sequence n, token l, group of 4 heads); lane owns elements
+// 4*lane .. 4*lane+3 of each 128-wide head row, i.e. rotary pairs 2*lane and
+// 2*lane+1, whose angle depends only on the token: sin/cos are computed once
+// per token and reused for the group's heads.
 // RMSNorm follows ggml's CPU rms_norm: squares formed in float, summed in
 // double, mean rounded to float, scale = 1/sqrtf(mean + eps), y = x*scale*g.
 // RoPE follows rope::apply (rope.hpp:140-141): x0' = x0*c - x1*s,
-// x1' = x0*s + x1*c, each product rounded separately (no contraction).
+// x1' = x0*s + x1*c, each product rounded separately (no contraction), with
+// angle = pos * freq / scale_factor as rope.hpp:78-95 computes it.
 template <typename TO>
 __global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
     const int lane = threadIdx.x & 31;
+    // per-lane RoPE constants, read from the parameter bank once (not per row)
+    float fr0 = 0.f, fr1 = 0.f, dv0 = 1.f, dv1 = 1.f;
+    int ax0 = 0, ax1 = 0;
+    if (p.rope) {
+        fr0 = p.tab.freq[2 * lane];
+        fr1 = p.tab.freq[2 * lane + 1];
+        dv0 = p.tab.div[2 * lane];
+        dv1 = p.tab.div[2 * lane + 1];
+        ax0 = p.tab.axis[2 * lane];
+        ax1 = p.tab.axis[2 * lane + 1];
+    }
+    float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (p.norm && p.gain) g = __ldg(reinterpret_cast<const float4*>(p.gain) + lane);
+    const int hgroups = (p.H + kPrologueHeads - 1) / kPrologueHeads;
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    const long long rows = (long long)p.N * p.L * p.H;
-    for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
-         row += warps) {
-        const int h = (int)(row % p.H);
-        const long long nl = row / p.H;
+    const long long items = (long long)p.N * p.L * hgroups;
+    for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
+        const int hg = (int)(it % hgroups);
+        const long long nl = it / hgroups;
         const int l = (int)(nl % p.L);
         const int n = (int)(nl / p.L);
-        const float* src = reinterpret_cast<const float*>(reinterpret_cast<const char*>(p.x) + (long long)n * p.x_nb2 +
-                                                          (long long)l * p.x_nb1) +
-                           h * kHeadDim;
-        float4 v = __ldg(reinterpret_cast<const float4*>(src) + lane);
-        if (p.norm) {
-            double ss = (double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y) + (double)__fmul_rn(v.z, v.z) +
-                        (double)__fmul_rn(v.w, v.w);
+        const int h0 = hg * kPrologueHeads;
+        const int nh = min(kPrologueHeads, p.H - h0);
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(p.x) +
+                                                            (long long)n * p.x_nb2 + (long long)l * p.x_nb1) +
+                            (h0 * kHeadDim) / 4 + lane;
+        float4 v[kPrologueHeads];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float mean = (float)(ss / (double)kHeadDim);
-            const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, p.eps)));
-            v.x = __fmul_rn(v.x, scale);
-            v.y = __fmul_rn(v.y, scale);
-            v.z = __fmul_rn(v.z, scale);
-            v.w = __fmul_rn(v.w, scale);
-            if (p.gain) {
-                const float4 g = __ldg(reinterpret_cast<const float4*>(p.gain) + lane);
-                v.x = __fmul_rn(v.x, g.x);
-                v.y = __fmul_rn(v.y, g.y);
-                v.z = __fmul_rn(v.z, g.z);
-                v.w = __fmul_rn(v.w, g.w);
-            }
-        }
+        for (int j = 0; j < kPrologueHeads; ++j)
+            if (j < nh) v[j] = __ldcs(src + j * (kHeadDim / 4));
+        float s0 = 0.f, c0 = 1.f, s1 = 0.f, c1 = 1.f;
         if (p.rope) {
             const int hw = p.tab.grid_h * p.tab.grid_w;
-            const int pos[3] = {l / hw, (l / p.tab.grid_w) % p.tab.grid_h, l % p.tab.grid_w};
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const int pi = 2 * lane + k;
-                const float ang = __fdiv_rn(__fmul_rn((float)pos[p.tab.axis[pi]], p.tab.freq[pi]), p.tab.div[pi]);
-                float s, c;
-                sincosf(ang, &s, &c);
-                const float x0 = k ? v.z : v.x, x1 = k ? v.w : v.y;
-                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-                const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-                if (k) { v.z = y0; v.w = y1; } else { v.x = y0; v.y = y1; }
-            }
+            const int t = l / hw, hh = (l / p.tab.grid_w) % p.tab.grid_h, w = l % p.tab.grid_w;
+            sincosf(__fdiv_rn(__fmul_rn(pick_pos(ax0, t, hh, w), fr0), dv0), &s0, &c0);
+            sincosf(__fdiv_rn(__fmul_rn(pick_pos(ax1, t, hh, w), fr1), dv1), &s1, &c1);
         }
-        char* dst = reinterpret_cast<char*>(p.y) + (long long)n * p.y_nb3 + (long long)h * p.y_nb2 +
-                    (long long)l * p.y_nb1 + (long long)lane * 4 * sizeof(TO);
-        store4<TO>(dst, v.x, v.y, v.z, v.w);
+#pragma unroll
+        for (int j = 0; j < kPrologueHeads; ++j) {
+            if (j >= nh) break;
+            float4 x = v[j];
+            if (p.norm) {
+                double ss = (double)__fmul_rn(x.x, x.x) + (double)__fmul_rn(x.y, x.y) + (double)__fmul_rn(x.z, x.z) +
+                            (double)__fmul_rn(x.w, x.w);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                const float mean = (float)(ss * (1.0 / kHeadDim));
+                const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, p.eps)));
+                x.x = __fmul_rn(__fmul_rn(x.x, scale), g.x);
+                x.y = __fmul_rn(__fmul_rn(x.y, scale), g.y);
+                x.z = __fmul_rn(__fmul_rn(x.z, scale), g.z);
+                x.w = __fmul_rn(__fmul_rn(x.w, scale), g.w);
+            }
+            if (p.rope) {
+                const float a0 = __fsub_rn(__fmul_rn(x.x, c0), __fmul_rn(x.y, s0));
+                const float a1 = __fadd_rn(__fmul_rn(x.x, s0), __fmul_rn(x.y, c0));
+                const float b0 = __fsub_rn(__fmul_rn(x.z, c1), __fmul_rn(x.w, s1));
+                const float b1 = __fadd_rn(__fmul_rn(x.z, s1), __fmul_rn(x.w, c1));
+                x = make_float4(a0, a1, b0, b1);
+            }
+            char* dst = reinterpret_cast<char*>(p.y) + (long long)n * p.y_nb3 + (long long)(h0 + j) * p.y_nb2 +
+                        (long long)l * p.y_nb1 + (long long)lane * 4 * sizeof(TO);
+            store4<TO>(dst, x.x, x.y, x.z, x.w);
+        }
     }
 }
 
@@ -211,9 +233,9 @@ int grid_for(long long warps_needed, int num_sms) {
 }  // namespace
 
 cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st) {
-    const long long rows = (long long)p.N * p.L * p.H;
-    if (rows == 0) return cudaSuccess;
-    const int grid = grid_for(rows, num_sms);
+    const long long items = (long long)p.N * p.L * ((p.H + kPrologueHeads - 1) / kPrologueHeads);
+    if (items == 0) return cudaSuccess;
+    const int grid = grid_for(items, num_sms);
     if (yt == OutType::BF16)
         prologue_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
     else if (yt == OutType::F16)

@@ -84,7 +84,8 @@ def test_flash_ext_output_types_and_strided_q(ctx, out_dtype):
     out = torch.empty(N, L, H, D, device="cuda", dtype=out_dtype)
     ctx.flash_attn_ext(qd, op_tensor(kf, oracle.BF16), op_tensor(vf, oracle.BF16), out)
     ctx.device_status()
-    assert_gates(out.float().cpu().numpy(), exact, label=str(out_dtype))
+    ot = {torch.float32: None, torch.bfloat16: "bf16", torch.float16: "f16"}[out_dtype]
+    assert_gates(out.float().cpu().numpy(), exact, label=str(out_dtype), out_type=ot)
 
 
 # ------------------------------------------------------------------ masks, kv_len, fully masked rows

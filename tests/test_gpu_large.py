@@ -62,7 +62,7 @@ def test_config1_full_size_self_attention(ctx, kd):
         rows = _sample_rows(L, 96, seed=n * 100 + h)
         ref, lref = _oracle_head_rows(q, k, v, n, h, rows, table, oracle.BF16)
         got = o[n, rows, h * d:(h + 1) * d]
-        assert_gates(got, ref, lse=ls[n, h, rows], lse_ref=lref, label=f"cfg1 n{n} h{h}")
+        assert_gates(got, ref, lse=ls[n, h, rows], lse_ref=lref, label=f"cfg1 n{n} h{h}", out_type="bf16")
 
 
 @pytest.mark.parametrize("use_mask", [False, True])
@@ -98,4 +98,4 @@ def test_config2_full_size_cross_attention(ctx, kd, use_mask):
         rows = _sample_rows(Lq, 128, seed=7 + n)
         ref, lref = _oracle_head_rows(q, k, v, n, h, rows, None, oracle.BF16, kv_len=int(kv_len[n]))
         got = o[n, rows, h * d:(h + 1) * d]
-        assert_gates(got, ref, lse=ls[n, h, rows], lse_ref=lref, label=f"cfg2 n{n} h{h} mask={use_mask}")
+        assert_gates(got, ref, lse=ls[n, h, rows], lse_ref=lref, label=f"cfg2 n{n} h{h} mask={use_mask}", out_type="bf16")
