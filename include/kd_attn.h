@@ -156,6 +156,34 @@ kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_
                                  kd_tensor* out, float* lse, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Allocation-free variant of kd_attn_flash_ext.  It has no counterpart in the
+ * reference: it exists for callers that cannot allocate device memory at all
+ * -- code running while a CUDA graph is being captured, or embedders whose
+ * device memory is owned by another allocator (a ggml backend buffer, a
+ * serving runtime's arena) and who may not call cudaMalloc behind its back.
+ * It needs no kd_attn_ctx (whose creation allocates) and calls no cudaMalloc,
+ * cudaFree or allocating library routine.
+ *
+ * Same arguments and semantics as kd_attn_flash_ext; it runs on the calling
+ * thread's current CUDA device.  Its scratch (Q rounded to the operand type
+ * when Q is f32 or strided, plus the mask's tile classes) lives in one
+ * statically sized device array of KD_ATTN_NOALLOC_SCRATCH_BYTES per device,
+ * held from the first call until the process exits.  Problems that need more
+ * scratch than that are rejected with KD_ATTN_ERR_UNSUPPORTED before anything
+ * is launched (Q already in K's type with 16-byte-aligned rows needs none).
+ *   - The first call on a device looks up that array's device address; make
+ *     that first call before any stream capture begins.
+ *   - Every call on a device shares the one array: calls that may overlap on
+ *     the GPU (different streams without ordering) race and must not be issued.
+ *   - Device-side wait timeouts are bounded as in the context path, but this
+ *     entry point has no context to report them through. */
+#define KD_ATTN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
+                                         const kd_tensor* mask, float scale, float max_bias,
+                                         float logit_softcap, const int32_t* kv_len, kd_tensor* out,
+                                         float* lse, void* stream);
+
+/* ---------------------------------------------------------------------------
  * The two CrossDiT call sites end to end (prologue + flash), operands staged
  * in the context's scratch.
  * Self-attention: DiTSelfAttention::forward between the QKV Linears and the

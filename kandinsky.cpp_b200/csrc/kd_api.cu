@@ -690,3 +690,223 @@ kd_attn_status kd_attn_fill_randn(kd_attn_ctx* ctx, float* dst, uint64_t n, uint
 }
 
 }  // extern "C"
+
+// ====================================================================== allocation-free flash entry
+// kd_attn_flash_ext_noalloc: the flash_attn_ext sequence (Q rounding, mask tile
+// classes, tcgen05 kernel) with every piece of scratch taken from statically
+// sized device arrays defined in this file, for callers that cannot allocate.
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = KD_ATTN_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+
+// One copy per device, created when the module loads and kept until the process exits.
+// Host code must not use these names as addresses: it asks cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) unsigned g_noalloc_words[2];  // [0] sticky error bits, [1] abort flag
+
+struct NoAllocDevice {
+    bool ready = false;
+    char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+    unsigned* words = nullptr; // device address of g_noalloc_words on this device
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// Once per device, with that device current: resolve the arrays' device addresses.
+kd_attn_status noalloc_setup(NoAllocDevice** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "device %d attributes unavailable", dev);
+        if (major != 10 || minor != 0)
+            return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device %d is sm_%d%d; built for sm_100a only", dev, major,
+                        minor);
+        void* s = nullptr;
+        void* w = nullptr;
+        e = cudaGetSymbolAddress(&s, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+        e = cudaGetSymbolAddress(&w, g_noalloc_words);
+        if (e != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(words) failed: %s", cudaGetErrorString(e));
+        d.scratch = static_cast<char*>(s);
+        d.words = static_cast<unsigned*>(w);
+        d.num_sms = sms;
+        d.ready = true;
+    }
+    *out = &d;
+    return KD_ATTN_OK;
+}
+
+kd_attn_status flash_noalloc(const FlashArgs& a, cudaStream_t st) {
+    kd_attn_ctx* const nc = nullptr;  // no context: messages go to stderr
+    kd_attn_status rc;
+    if ((rc = check_tensor(nc, a.q, "q")) || (rc = check_tensor(nc, a.k, "k")) || (rc = check_tensor(nc, a.v, "v")) ||
+        (rc = check_tensor(nc, a.out, "out")))
+        return rc;
+    const kd_tensor &q = *a.q, &k = *a.k, &v = *a.v, &o = *a.out;
+    if (q.ne[0] != kHeadDim || k.ne[0] != kHeadDim || v.ne[0] != kHeadDim)
+        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (k.type != v.type || (k.type != KD_ATTN_TYPE_F16 && k.type != KD_ATTN_TYPE_BF16))
+        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "k and v must share type f16 or bf16");
+    const int64_t Lq = q.ne[1], H = q.ne[2], N = q.ne[3];
+    const int64_t Lk = k.ne[1], Hkv = k.ne[2], Nkv = k.ne[3];
+    if (v.ne[1] != Lk || v.ne[2] != Hkv || v.ne[3] != Nkv)
+        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "v shape differs from k");
+    if (Hkv <= 0 || Nkv <= 0 || H % Hkv || N % Nkv)
+        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "q heads/sequences are not multiples of k's");
+    if (o.ne[0] != kHeadDim || o.ne[1] != H || o.ne[2] != Lq || o.ne[3] != N)
+        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [128, H, Lq, N]");
+    if (!(a.scale > 0.f) || !std::isfinite(a.scale))
+        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "scale must be positive and finite");
+    if (Lk > (int64_t)kMaxKvTiles * kBlockN) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "Lk too large");
+    if (H > 65535 || N > 65535) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "more than 65535 heads or sequences");
+    uint64_t onb[4], knb[4], vnb[4], qnb[4];
+    packed_strides(&o, onb);
+    packed_strides(&k, knb);
+    packed_strides(&v, vnb);
+    packed_strides(&q, qnb);
+    if (!strides16(onb) || !aligned16(o.data)) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned");
+    if (Lk > 0 && (!strides16(knb) || !strides16(vnb)))
+        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "k/v strides must be multiples of 16 bytes");
+    if (Lq == 0 || H == 0 || N == 0) return KD_ATTN_OK;
+    const bool bf16 = k.type == KD_ATTN_TYPE_BF16;
+
+    // scratch plan: [Q rounded to the operand type][mask tile classes], both inside the static array
+    const bool q_direct = q.type == k.type && strides16(qnb) && aligned16(q.data);
+    const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * kHeadDim * 2);
+    int n_qb = 0, n_kb = 0, mh = 1, mn = 1;
+    size_t cls_bytes = 0;
+    uint64_t mnb[4] = {0, 0, 0, 0};
+    if (a.mask) {
+        if ((rc = check_tensor(nc, a.mask, "mask"))) return rc;
+        const kd_tensor& m = *a.mask;
+        if (m.type != KD_ATTN_TYPE_F16) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "mask must be f16");
+        if (m.ne[0] < Lk || m.ne[1] < Lq) return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "mask smaller than [Lk, Lq]");
+        if (m.ne[2] <= 0 || m.ne[3] <= 0 || H % m.ne[2] || N % m.ne[3])
+            return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "mask planes must divide heads and sequences");
+        mh = (int)m.ne[2];
+        mn = (int)m.ne[3];
+        n_qb = (int)((Lq + 63) / 64);
+        n_kb = (int)((Lk + 63) / 64);
+        cls_bytes = align256((size_t)mh * mn * n_qb * n_kb);
+        packed_strides(a.mask, mnb);
+    }
+    if (q_bytes + cls_bytes > kNoAllocScratchBytes)
+        return fail(nc, KD_ATTN_ERR_UNSUPPORTED,
+                    "kd_attn_flash_ext_noalloc needs %zu bytes of scratch but holds %zu (KD_ATTN_NOALLOC_SCRATCH_BYTES); "
+                    "pass Q in K's type with 16-byte-aligned rows, or use kd_attn_flash_ext",
+                    q_bytes + cls_bytes, kNoAllocScratchBytes);
+
+    NoAllocDevice* d = nullptr;
+    if ((rc = noalloc_setup(&d))) return rc;
+#define KD_CUDA_NC(call)                                                                                 \
+    do {                                                                                                 \
+        cudaError_t _e = (call);                                                                         \
+        if (_e != cudaSuccess) return fail(nc, KD_ATTN_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(_e)); \
+    } while (0)
+
+    const void* qdata = q.data;
+    if (!q_direct) {
+        ConvertParams cp{};
+        cp.src = q.data;
+        cp.src_type = q.type;
+        cp.nb1 = (long long)qnb[1];
+        cp.nb2 = (long long)qnb[2];
+        cp.nb3 = (long long)qnb[3];
+        cp.dst = d->scratch;
+        cp.L = (int)Lq;
+        cp.H = (int)H;
+        cp.N = (int)N;
+        KD_CUDA_NC(launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, d->num_sms, st));
+        qdata = d->scratch;
+        qnb[1] = kHeadDim * 2;
+        qnb[2] = qnb[1] * Lq;
+        qnb[3] = qnb[2] * H;
+    }
+    uint8_t* cls = nullptr;
+    if (a.mask) {
+        cls = reinterpret_cast<uint8_t*>(d->scratch + q_bytes);
+        MaskClassParams mp{};
+        mp.mask = static_cast<const uint16_t*>(a.mask->data);
+        mp.nb1 = (long long)mnb[1];
+        mp.nb2 = (long long)mnb[2];
+        mp.nb3 = (long long)mnb[3];
+        mp.Lq = (int)Lq;
+        mp.Lk = (int)Lk;
+        mp.mh = mh;
+        mp.mn = mn;
+        mp.cls = cls;
+        mp.n_qb = n_qb;
+        mp.n_kb = n_kb;
+        KD_CUDA_NC(launch_mask_classify(mp, st));  // overwrites every class byte it covers
+    }
+    CUtensorMap tmQ, tmK, tmV;
+    if ((rc = make_operand_map(nc, &tmQ, qdata, bf16, Lq, H, N, qnb))) return rc;
+    if (Lk > 0) {
+        if ((rc = make_operand_map(nc, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb))) return rc;
+        if ((rc = make_operand_map(nc, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb))) return rc;
+    } else {
+        tmK = tmQ;
+        tmV = tmQ;
+    }
+    FmhaParams p{};
+    p.Lq = (int)Lq;
+    p.Lk = (int)Lk;
+    p.H = (int)H;
+    p.N = (int)N;
+    p.rk2 = (int)(H / Hkv);
+    p.rk3 = (int)(N / Nkv);
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.inv_scale = 1.0f / a.scale;
+    p.out = o.data;
+    p.o_nb1 = (long long)onb[1];
+    p.o_nb2 = (long long)onb[2];
+    p.o_nb3 = (long long)onb[3];
+    p.lse = a.lse;
+    p.tile_cls = cls;
+    p.n_qb = n_qb;
+    p.n_kb = n_kb;
+    if (a.mask) {
+        p.mask = static_cast<const uint16_t*>(a.mask->data);
+        p.m_nb1 = (long long)mnb[1];
+        p.m_nb2 = (long long)mnb[2];
+        p.m_nb3 = (long long)mnb[3];
+    }
+    p.mh = mh;
+    p.mn = mn;
+    p.kv_len = a.kv_len;
+    p.err = d->words;
+    p.abort_flag = d->words + 1;
+    p.wait_ns = 2000000000ull;
+    // the abort flag must start at zero for every launch (the array keeps the last call's contents)
+    KD_CUDA_NC(cudaMemsetAsync(d->words + 1, 0, sizeof(unsigned), st));
+    KD_CUDA_NC(launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
+#undef KD_CUDA_NC
+    return KD_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
+                                                    const kd_tensor* mask, float scale, float max_bias,
+                                                    float logit_softcap, const int32_t* kv_len, kd_tensor* out,
+                                                    float* lse, void* stream) {
+    if (max_bias != 0.f) return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "max_bias (ALiBi) must be 0");
+    if (logit_softcap != 0.f) return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "logit_softcap must be 0");
+    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse};
+    return flash_noalloc(fa, static_cast<cudaStream_t>(stream));
+}

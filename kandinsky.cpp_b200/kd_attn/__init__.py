@@ -38,7 +38,11 @@ EXPORTED = [
     "kd_attn_create", "kd_attn_destroy", "kd_attn_last_error", "kd_attn_device_status",
     "kd_attn_prologue", "kd_attn_flash_ext", "kd_attn_self_attention", "kd_attn_cross_attention",
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
+    "kd_attn_flash_ext_noalloc",
 ]
+
+# scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
+NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 
 class KdAttnError(RuntimeError):
@@ -132,6 +136,8 @@ def _load():
     L.kd_attn_fill_randn.restype = st
     L.kd_attn_nccl_unique_id.argtypes = [P]
     L.kd_attn_nccl_unique_id.restype = st
+    L.kd_attn_flash_ext_noalloc.argtypes = [T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, T, P, P]
+    L.kd_attn_flash_ext_noalloc.restype = st
     L.kd_attn_version.argtypes = []
     L.kd_attn_version.restype = ctypes.c_int32
     return L
@@ -259,6 +265,24 @@ class Context:
         self.check(lib.kd_attn_fill_randn(self.handle, _ptr(dst), dst.numel(), int(seed), int(offset),
                                           _stream_ptr(stream)))
         return dst
+
+
+def flash_attn_ext_noalloc(q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
+                           logit_softcap=0.0, stream=None):
+    """kd_attn_flash_ext_noalloc: flash_attn_ext without a Context and without any device allocation.
+
+    For callers that may not allocate (graph capture, foreign memory arenas).  Runs on the current
+    CUDA device; its scratch is a fixed NOALLOC_SCRATCH_BYTES device array shared by every call on
+    that device, so calls must not overlap on the GPU.  Make the first call before any stream capture.
+    Problems needing more scratch are rejected with ERR_UNSUPPORTED.
+    """
+    if scale is None:
+        scale = 1.0 / (q.shape[-1] ** 0.5)
+    rc = lib.kd_attn_flash_ext_noalloc(_ref(q), _ref(k), _ref(v), _ref(mask), float(scale), float(max_bias),
+                                       float(logit_softcap), _ptr(kv_len), _ref(out), _ptr(lse), _stream_ptr(stream))
+    if rc != OK:
+        raise KdAttnError(rc, "kd_attn_flash_ext_noalloc failed (details on stderr)")
+    return out
 
 
 def attention(ctx: Context, q, k, v, n_head, mask=None, flash=True, op_type=F16, out_dtype=None, stream=None):
