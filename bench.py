@@ -164,16 +164,27 @@ def cpu_reference(cfg, seconds_target=15.0, threads=None):
         oracle.flash_attn_ext(qn[:, None], k4, v4, mode=oracle.GGML)
         return time.perf_counter() - t0
 
-    r0 = max(16, min(L, 64))
-    t0 = run(r0)
-    rows = int(min(L, max(r0, r0 * seconds_target / max(t0, 1e-3))))
-    t = run(rows)
-    flop_sample = 4.0 * rows * L * d
+    # per-row cost from two small runs (each run also pays the fixed K-side prologue and casts)
+    r_a, r_b = min(L, 64), min(L, 512)
+    t_a, t_b = run(r_a), run(r_b)
+    slope = max((t_b - t_a) / max(r_b - r_a, 1), 1e-6)
+    rows = int(min(L, max(r_b, r_b + (seconds_target - t_b) / slope)))
+    planes, t = 0, 0.0
+    if rows < L:
+        t, planes = run(rows), 1
+        flop_sample = 4.0 * rows * L * d
+        what = f"1 (batch, head) plane x {rows} of {L} query rows"
+    else:  # a whole plane is quicker than the target: repeat whole planes (same work each)
+        while planes == 0 or (t < seconds_target and planes < cfg["N"] * cfg["H"]):
+            t += run(L)
+            planes += 1
+        flop_sample = planes * 4.0 * L * L * d
+        what = f"{planes} whole (batch, head) planes of {cfg['N'] * cfg['H']}"
     full_flop = 4.0 * cfg["N"] * cfg["H"] * L * L * d
     ms_full = t * 1e3 * full_flop / flop_sample
     return {"value": flop_sample / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"1 (batch, head) pair x {rows} of {L} query rows (prologue + ggml-faithful flash_attn_ext), "
-                      f"{t:.1f} s; scaled by B*H*L/rows to {ms_full / 1e3:.0f} s per full call",
+            "sample": f"{what} (prologue + ggml-faithful flash_attn_ext), {t:.1f} s on {threads} threads; "
+                      f"scaled by the FLOP ratio to {ms_full / 1e3:.0f} s per full call",
             "ms_per_call_scaled": ms_full}
 
 

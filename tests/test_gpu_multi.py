@@ -1,0 +1,72 @@
+"""Head-sharded self-attention on 2 GPUs through the C ABI (skipped with fewer than 2 GPUs).
+
+Rank r runs kd_attn_self_attention on its column shard of the config-1-like projections and
+kd_attn_allgather_heads (one ncclAllGather + permute) rebuilds [C, L, N]; the result must equal
+the single-GPU call on the full projections bit for bit (heads are independent and the kernels
+are deterministic).  Child processes, one per GPU, 127.0.0.1 rendezvous, NVLS off.
+"""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "kandinsky.cpp_b200"))
+    import kd_attn
+    from kd_attn.sharding import column_shard
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank), timeout=datetime.timedelta(seconds=60))
+    obj = [kd_attn.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    N, H, d, grid = 2, 8, 128, (4, 16, 16)
+    L, C = grid[0] * grid[1] * grid[2], H * d
+    rope = kd_attn.Rope3D.make(grid, scale=(1, 2, 2))
+    with kd_attn.Context(device=rank, n_ranks=world, rank=rank, nccl_id=obj[0]) as ctx:
+        full_in = []
+        for off in range(3):
+            t = torch.empty(N * L * C, device="cuda")
+            ctx.fill_randn(t, seed=77, offset=off)            # same full projections on every rank
+            full_in.append(t.view(N, L, C))
+        shard_in = [column_shard(x, rank, world, H).contiguous() for x in full_in]
+        Hs = H // world
+        shard_out = torch.empty(N, L, Hs * d, device="cuda", dtype=torch.bfloat16)
+        ctx.self_attention(*shard_in, Hs, shard_out, rope=rope, op_type=kd_attn.BF16)
+        gathered = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+        ctx.allgather_heads(shard_out.view(N, L, Hs, d), gathered.view(N, L, H, d))
+        ctx.device_status()
+        if rank == 0:
+            with kd_attn.Context(device=0) as single:
+                ref = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+                single.self_attention(*full_in, H, ref, rope=rope, op_type=kd_attn.BF16)
+                single.device_status()
+            torch.save({"got": gathered.cpu(), "ref": ref.cpu()}, os.path.join(out_dir, "r0.pt"))
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+def test_two_gpu_head_sharding_matches_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    r = torch.load(os.path.join(str(tmp_path), "r0.pt"))
+    assert torch.equal(r["got"], r["ref"])
