@@ -258,6 +258,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// 2^x on the FMA/ALU pipes, used for part of the softmax exponentials so the MUFU
+// unit is not the only exp2 engine.  Range split 2^x = 2^n * 2^f with n = rint(x)
+// (add/subtract 1.5*2^23, which also leaves n in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted
+// for this library by a Remez exchange minimising the maximum relative error on
+// [-0.5, 0.5] (7.5e-5 = 2^-13.7, far below the 2^-9 half-ulp of the bf16 P it
+// feeds); n is added to the exponent field.  The argument is clamped at -126 so
+// the exponent field cannot underflow (p in [0.70, 1.42] has field 126 or 127),
+// and anything at or below -126 (including -inf scores) returns exactly 0.
+__device__ __forceinline__ float exp2_poly(float x) {
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    constexpr float c0 = 0.999928057f, c1 = 0.693260968f, c2 = 0.242611125f, c3 = 0.0551716685f;
+    const float xc = fmaxf(x, -126.0f);
+    const float t = xc + kShift;
+    const float f = xc - (t - kShift);
+    const float p = fmaf(fmaf(fmaf(c3, f, c2), f, c1), f, c0);
+    const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+    return x > -126.0f ? r : 0.0f;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 template <typename T>
 struct Pack2;
 template <>

@@ -40,6 +40,25 @@
 
 namespace kd {
 
+// Optional pipeline-event trace for studies of the schedule.  Only a build with
+// -DKD_FMHA_TRACE=<x> has it (the shipped library does not): lane 0 of the
+// producer, the MMA warp and the first warp of each softmax warpgroup of CTA
+// (x, 0, 0) store clock64() at named events, per K/V iteration (< 512), into
+// kd_fmha_trace[role][event][iteration]; kd_fmha_trace_read copies it out.
+#ifdef KD_FMHA_TRACE
+__device__ unsigned long long kd_fmha_trace[4][8][512];
+#define KD_TRACE(role, ev, it)                                                                   \
+    do {                                                                                         \
+        if (blockIdx.x == (KD_FMHA_TRACE) && blockIdx.y == 0 && blockIdx.z == 0 && lane == 0 && \
+            (it) < 512)                                                                          \
+            kd_fmha_trace[(role)][(ev)][(it)] = clock64();                                       \
+    } while (0)
+#else
+#define KD_TRACE(role, ev, it) \
+    do {                       \
+    } while (0)
+#endif
+
 namespace {
 
 constexpr int kStages = 4;
@@ -50,8 +69,8 @@ constexpr int kThreads = 384;
 constexpr int kSmemQ = 0;
 constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
 constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
-// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], drain
-constexpr int kNumBars = 1 + 2 * kStages + 6 + 1;
+// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], drain, p_half[2]
+constexpr int kNumBars = 1 + 2 * kStages + 6 + 1 + 2;
 constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
 constexpr int kSmemNKept = kSmemTmemSlot + 4;
 constexpr int kSmemList = (kSmemNKept + 4 + 15) & ~15;
@@ -61,6 +80,23 @@ constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 10
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8 between rescales
+// Tuning knobs (compile-time):
+//   KD_FMHA_POLY_PAIRS: bit i set = score pair i of each 32-key chunk takes exp2 from the
+//                       FMA pipe (exp2_poly) instead of MUFU ex2 (0 = all MUFU).
+//   KD_FMHA_SPLIT_P:    1 = hand P to the MMA in two 64-key halves (PV starts on the first
+//                       half while the second is exponentiated), 0 = one hand-off.
+//   KD_FMHA_MAX3:       1 = three-input max.f32 for the row maximum.
+#ifndef KD_FMHA_POLY_PAIRS
+#define KD_FMHA_POLY_PAIRS 0x0000u
+#endif
+#ifndef KD_FMHA_SPLIT_P
+#define KD_FMHA_SPLIT_P 0
+#endif
+#ifndef KD_FMHA_MAX3
+#define KD_FMHA_MAX3 1
+#endif
+constexpr uint32_t kPolyPairs = KD_FMHA_POLY_PAIRS;
+constexpr bool kSplitP = KD_FMHA_SPLIT_P != 0;
 
 static_assert(kSmemAlloc <= 232448, "shared memory budget");
 
@@ -114,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* p_full = s_full + 2;
     uint64_t* o_full = s_full + 4;
     uint64_t* drain = s_full + 6;
+    uint64_t* p_half = s_full + 7;   // first 64 keys of P_i written (PV may start on them)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
     int* n_kept_slot = reinterpret_cast<int*>(smem + kSmemNKept);
     uint32_t* list = reinterpret_cast<uint32_t*>(smem + kSmemList);
@@ -134,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], kBlockM);
+            mbar_init(&p_half[i], kBlockM);
             mbar_init(&o_full[i], 1);
         }
         mbar_init(drain, 1);
@@ -214,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ph = (it / kStages) & 1u;
                     ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
                     if (!ok) break;
+                    KD_TRACE(0, w, j);
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
                         const CUtensorMap* map = w ? &tmV : &tmK;
@@ -261,15 +300,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 __syncwarp();
             };
-            auto issue_pv = [&](int i, int s, bool acc) {
+            // O_i += P_i V for keys [64*half, 64*half + 64): P columns 32*half.., V rows 64*half..
+            auto issue_pv = [&](int i, int s, bool acc, int half) {
                 if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < kBlockN / 16; ++kk)
+                    for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+                        const int kk = half * (kBlockN / 32) + k4;
                         mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
                                desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
                                (acc || kk > 0) ? 1u : 0u);
+                    }
                 }
                 __syncwarp();
+            };
+            // wait for one half of P_i (phase j), then issue that half of PV
+            auto pv_half = [&](int i, int s, int j, int half) -> bool {
+                if (!kSplitP) {  // one hand-off: wait for all of P, then issue both halves
+                    if (half) return true;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], j & 1, ctl, kErrTimeoutP))) return false;
+                    tc_fence_after();
+                    issue_pv(i, s, j > 0, 0);
+                    issue_pv(i, s, j > 0, 1);
+                    return true;
+                }
+                uint64_t* bar = half ? &p_full[i] : &p_half[i];
+                if (!__all_sync(0xffffffffu, mbar_wait(bar, j & 1, ctl, kErrTimeoutP))) return false;
+                tc_fence_after();
+                issue_pv(i, s, j > 0, half);
+                return true;
             };
             auto commit = [&](uint64_t* b) {
                 if (lane == 0) tc_commit(b);
@@ -291,24 +349,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < n_iter && ok; ++j) {
                 const bool more = j + 1 < n_iter;
                 if (!(ok = next_stage(sV))) break;
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[0], j & 1, ctl, kErrTimeoutP)))) break;
-                tc_fence_after();
-                issue_pv(0, sV, j > 0);
+                KD_TRACE(1, 0, j);
+                if (!(ok = pv_half(0, sV, j, 0))) break;
+                if (!(ok = pv_half(0, sV, j, 1))) break;
+                KD_TRACE(1, 1, j);
                 if (!more) commit(&o_full[0]);
                 int sK2 = 0;
                 if (more) {
                     if (!(ok = next_stage(sK2))) break;
                     issue_s(0, sK2);
+                    KD_TRACE(1, 2, j);
                     commit(&s_full[0]);
                 }
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[1], j & 1, ctl, kErrTimeoutP)))) break;
-                tc_fence_after();
-                issue_pv(1, sV, j > 0);
+                if (!(ok = pv_half(1, sV, j, 0))) break;
+                if (!(ok = pv_half(1, sV, j, 1))) break;
+                KD_TRACE(1, 3, j);
                 commit(&kv_empty[sV]);
                 if (!more) {
                     commit(&o_full[1]);
                 } else {
                     issue_s(1, sK2);
+                    KD_TRACE(1, 4, j);
                     commit(&s_full[1]);
                     commit(&kv_empty[sK2]);
                 }
@@ -343,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kbase = (int)(e >> 16) * kBlockN;
             const uint32_t c0 = (e >> (4 * g)) & 3u, c1 = (e >> (4 * g + 2)) & 3u;
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], j & 1, ctl, kErrTimeoutS)))) break;
+            if ((warp & 3) == 0) KD_TRACE(2 + wg, 0, j);
             tc_fence_after();
 
             // Mixed tiles: add the additive mask (divided by scale, so that scale*(s + m/scale) =
@@ -370,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint32_t su[128];
             tmem_ld128_sync(tS, su);
+            if ((warp & 3) == 0) KD_TRACE(2 + wg, 1, j);
             // Skipped halves and keys past the valid length become -inf.
             {
                 const int lim = lk_eff - kbase;
@@ -382,6 +445,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#if KD_FMHA_MAX3
+#pragma unroll
+            for (int c = 0; c < 128; c += 8) {
+                mx0 = fmax3(mx0, __uint_as_float(su[c]), __uint_as_float(su[c + 1]));
+                mx1 = fmax3(mx1, __uint_as_float(su[c + 2]), __uint_as_float(su[c + 3]));
+                mx2 = fmax3(mx2, __uint_as_float(su[c + 4]), __uint_as_float(su[c + 5]));
+                mx3 = fmax3(mx3, __uint_as_float(su[c + 6]), __uint_as_float(su[c + 7]));
+            }
+#else
 #pragma unroll
             for (int c = 0; c < 128; c += 4) {
                 mx0 = fmaxf(mx0, __uint_as_float(su[c]));
@@ -389,7 +461,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mx2 = fmaxf(mx2, __uint_as_float(su[c + 2]));
                 mx3 = fmaxf(mx3, __uint_as_float(su[c + 3]));
             }
-            const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+#endif
+            const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+            if ((warp & 3) == 0) KD_TRACE(2 + wg, 2, j);
             const float m_new = fmaxf(m, m_tile);
             const bool resc = m_new > m + kRescaleThreshold;
             const bool warp_resc = __any_sync(0xffffffffu, resc);
@@ -401,21 +475,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float neg_mu = (m == -INFINITY) ? 0.f : -m;
             float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            // P for 32 keys -> 16 packed columns of S_i's TMEM
+            auto p_chunk = [&](int c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float a = ex2_approx(fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu));
-                    const float b = ex2_approx(fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu));
+                    const float xa = fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu);
+                    const float xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
+                    float a, b;
+                    if ((kPolyPairs >> i) & 1u) {
+                        a = exp2_poly(xa);
+                        b = exp2_poly(xb);
+                    } else {
+                        a = ex2_approx(xa);
+                        b = ex2_approx(xb);
+                    }
                     rs0 += a;
                     rs1 += b;
                     pk[i] = Pack2<T>::pack(a, b);
                 }
                 tmem_st16(tS + c * 16, pk);
-            }
-            // Rescale O_i (PV_i(j-1) is complete: its commit preceded S_i(j)'s).  Done after P so
-            // the 128 score registers are dead; it only has to precede the p_full arrive.
+            };
+            p_chunk(0);
+            p_chunk(1);
+            if ((warp & 3) == 0) KD_TRACE(2 + wg, 3, j);
+            // Rescale O_i (PV_i(j-1) is complete: its commit preceded S_i(j)'s).  It only has to
+            // precede the first PV_i(j) MMA, i.e. the p_half arrive; the first 64 scores are dead here.
             if (warp_resc && j > 0) {
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
@@ -426,10 +511,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(tO + c * 32, o);
                 }
             }
+            if (kSplitP) {
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&p_half[wg]);
+            }
+            p_chunk(2);
+            p_chunk(3);
             tmem_wait_st();
             l += rs0 + rs1;
             tc_fence_before();
             mbar_arrive(&p_full[wg]);
+            if ((warp & 3) == 0) KD_TRACE(2 + wg, 4, j);
         }
 
         if (ok) {
@@ -494,6 +587,13 @@ int regs_t() {
 }  // namespace
 
 int fmha_smem_bytes() { return kSmemAlloc; }
+
+#ifdef KD_FMHA_TRACE
+extern "C" int kd_fmha_trace_read(unsigned long long* host, unsigned long long n) {
+    if (n > sizeof(kd_fmha_trace) / sizeof(unsigned long long)) n = sizeof(kd_fmha_trace) / sizeof(unsigned long long);
+    return (int)cudaMemcpyFromSymbol(host, kd_fmha_trace, n * sizeof(unsigned long long));
+}
+#endif
 
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                         const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st) {

@@ -20,7 +20,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libkd_attn.so")
+# $KD_ATTN_LIBRARY selects another build of the library (e.g. one compiled with other tuning knobs)
+LIB_PATH = os.environ.get("KD_ATTN_LIBRARY") or os.path.join(_HERE, "libkd_attn.so")
 
 # status codes (kd_attn_status)
 OK = 0
