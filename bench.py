@@ -40,9 +40,29 @@ CONFIGS = {
             op="f16", out="f32"),
     1: dict(name="cfg1 self-attn B2 L31744 (31x32x32) H32 d128 bf16", N=2, grid=(31, 32, 32), H=32, op="bf16",
             out="bf16"),
+    2: dict(name="cfg2 cross-attn B2 Lq31744 (31x32x32) x Lk256 (valid U[40,256]) H32 d128 bf16", kind="cross",
+            N=2, grid=(31, 32, 32), Lk=256, H=32, op="bf16", out="bf16"),
     3: dict(name="cfg3 self-attn B2 L71424 (31x48x48) H32 d128 bf16", N=2, grid=(31, 48, 48), H=32, op="bf16",
             out="bf16"),
+    4: dict(name="cfg4 block-sparse self-attn B1 L62464 (61x32x32) H32 d128 bf16, 64x64 tiles", kind="sparse",
+            N=1, grid=(61, 32, 32), H=32, op="bf16", out="bf16", p_random=0.14),
 }
+
+
+def block_sparse_tiles(grid, p_random, seed=4):
+    """Kept 64x64 tiles of config 4 (numpy bool [nt, nt]): tile i = (frame i//16, strip i%16) of a
+    32x32-token frame (1024 tokens = 16 tiles of 2 latent rows); kept = diagonal, |df| <= 1 and
+    |ds| <= 1 (temporal window over spatially adjacent tiles), plus seeded random tiles at p_random."""
+    import numpy as np
+    nt_tok = grid[0] * grid[1] * grid[2]
+    nt = nt_tok // 64
+    per_frame = grid[1] * grid[2] // 64
+    i = np.arange(nt)
+    f, s = i // per_frame, i % per_frame
+    keep = (np.abs(f[:, None] - f[None, :]) <= 1) & (np.abs(s[:, None] - s[None, :]) <= 1)
+    keep |= np.eye(nt, dtype=bool)
+    keep |= np.random.default_rng(seed).random((nt, nt)) < p_random
+    return keep
 
 
 def peaks():
@@ -216,6 +236,101 @@ def L_of(cfg):
     return nt * nh * nw
 
 
+def _timed(torch, stream, fn, steps, warmup):
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_other(args, cfg, ctx, kd_attn, torch, q, k, v, rope, op, out_dt, stream):
+    """Configs 2 (cross-attention, variable text length) and 4 (64x64 block-sparse self-attention)."""
+    import numpy as np
+    N, H, d, L = cfg["N"], cfg["H"], 128, L_of(cfg)
+    dev = q.device
+    opdt = torch.bfloat16 if op == kd_attn.BF16 else torch.float16
+    pk, _, pk_kind = peaks()
+    if cfg["kind"] == "cross":
+        Lk = cfg["Lk"]
+        kv_len = torch.from_numpy(np.random.default_rng(2).integers(40, Lk + 1, size=N).astype(np.int32)).to(dev)
+        kt = torch.empty(N * Lk * H * d, device=dev)
+        vt = torch.empty_like(kt)
+        ctx.fill_randn(kt, seed=3, offset=1)
+        ctx.fill_randn(vt, seed=3, offset=2)
+        kt, vt = (kt * 0.5).view(N, Lk, H * d), (vt * 0.5).view(N, Lk, H * d)
+        out = torch.empty(N, L, H * d, device=dev, dtype=out_dt)
+        ms = _timed(torch, stream, lambda: ctx.cross_attention(q, kt, vt, H, out, kv_len=kv_len, op_type=op,
+                                                                stream=stream), args.steps, args.warmup)
+        qs = torch.empty(N, H, L, d, device=dev, dtype=opdt)
+        ks = torch.empty(N, H, Lk, d, device=dev, dtype=opdt)
+        vs = torch.empty_like(ks)
+        ctx.prologue(q, H, qs, norm=True, stream=stream)
+        ctx.prologue(kt, H, ks, norm=True, stream=stream)
+        ctx.prologue(vt, H, vs, norm=False, stream=stream)
+        o4 = out.view(N, L, H, d)
+        fa_ms = _timed(torch, stream, lambda: ctx.flash_attn_ext(qs, ks, vs, o4, kv_len=kv_len, stream=stream),
+                       args.steps, args.warmup)
+        ctx.device_status()
+        flop = 4.0 * N * H * L * Lk * d
+        flop_valid = 4.0 * H * L * d * float(kv_len.sum().item())
+        fa_bytes = (N * H * L * d * 2) * 2 + N * H * Lk * d * 2 * 2     # Q + O (bf16) + K + V
+        call_bytes = N * L * H * d * 4 + 2 * N * Lk * H * d * 4 + N * H * (L + 2 * Lk) * d * 2 + fa_bytes
+        return {"metric": "cross-attn TFLOP/s (dense-equiv) and HBM GB/s", "config": {"workload": cfg["name"],
+                "kv_len": kv_len.tolist()}, "ms_per_step": ms, "value": flop / (ms * 1e-3) / 1e12, "unit": UNIT,
+                "tflops_valid_keys": flop_valid / (ms * 1e-3) / 1e12,
+                "call_gbs": call_bytes / (ms * 1e-3) / 1e9,
+                "flash_kernel": {"ms": fa_ms, "gbs": fa_bytes / (fa_ms * 1e-3) / 1e9,
+                                 "frac_of_hbm": fa_bytes / (fa_ms * 1e-3) / 1e9 / hbm_peak(),
+                                 "algorithmic_bytes": fa_bytes}}
+    # block-sparse
+    keep = block_sparse_tiles(cfg["grid"], cfg["p_random"])
+    nt = keep.shape[0]
+    density = float(keep.mean())
+    cta = keep.reshape(nt // 4, 4, nt // 2, 2).any(axis=(1, 3))             # 256-row x 128-key blocks visited
+    keep_t = torch.from_numpy(keep).to(dev)
+    cond = keep_t.repeat_interleave(64, 0).repeat_interleave(64, 1)
+    mask = torch.zeros(1, 1, L, L, device=dev, dtype=torch.float16)
+    mask.view(L, L).masked_fill_(~cond, float("-inf"))
+    del cond, keep_t
+    qs = torch.empty(N, H, L, d, device=dev, dtype=opdt)
+    ks, vs = torch.empty_like(qs), torch.empty_like(qs)
+    out = torch.empty(N, L, H, d, device=dev, dtype=out_dt)
+
+    def step():
+        ctx.prologue(q, H, qs, norm=True, rope=rope, stream=stream)
+        ctx.prologue(k, H, ks, norm=True, rope=rope, stream=stream)
+        ctx.prologue(v, H, vs, norm=False, stream=stream)
+        ctx.flash_attn_ext(qs, ks, vs, out, mask=mask, stream=stream)
+
+    ms = _timed(torch, stream, step, args.steps, args.warmup)
+    fa_ms = _timed(torch, stream, lambda: ctx.flash_attn_ext(qs, ks, vs, out, mask=mask, stream=stream),
+                   args.steps, args.warmup)
+    ctx.device_status()
+    dense = 4.0 * N * H * L * L * d
+    actual = dense * density
+    return {"metric": "block-sparse attn TFLOP/s (dense-equiv and kept-tile)", "config": {"workload": cfg["name"],
+            "tile_density": density, "visited_fraction_256x128": float(cta.mean())},
+            "ms_per_step": ms, "value": dense / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "tflops_kept_tiles": actual / (ms * 1e-3) / 1e12,
+            "flash_kernel_with_mask": {"ms": fa_ms, "dense_equiv_tflops": dense / (fa_ms * 1e-3) / 1e12,
+                                       "kept_tile_tflops": actual / (fa_ms * 1e-3) / 1e12,
+                                       "kernel_tflops_on_visited": dense * float(cta.mean()) / (fa_ms * 1e-3) / 1e12,
+                                       "peak": pk, "peak_kind": pk_kind}}
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get("hbm_gbs", 6650.0)
+    return 6650.0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -295,6 +410,14 @@ def main():
         if ws > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
+
+    if cfg.get("kind") in ("cross", "sparse"):
+        if ws > 1:
+            raise SystemExit("configs 2 and 4 are single-GPU measurements")
+        line = run_other(args, cfg, ctx, kd_attn, torch, q, k, v, rope, op, out_dt, stream)
+        print(json.dumps(line), flush=True)
+        ctx.close()
+        return
 
     if args.fa_only:
         qs = torch.empty(N, Hs, L, d, device=dev, dtype=torch.bfloat16 if op == kd_attn.BF16 else torch.float16)

@@ -143,44 +143,48 @@ __global__ void __launch_bounds__(256) convert_q_kernel(const ConvertParams p) {
     }
 }
 
-// grid (n_qb, mh*mn); 8 warps per block.  Each warp scans 8 of the 64 rows of
-// the query block; per 64-key tile the block records whether every in-range
-// element is -inf (skip) or +-0 (full).  Elements outside [0,Lq) x [0,Lk) are
-// ignored; a tile with no in-range element is a skip tile.
+// One warp per 64 x 64 (query x key) tile, grid-strided over all tiles of all
+// mask planes: lane l reads keys 2l, 2l+1 of the tile's 64 rows, 8 rows in
+// flight at a time, and the warp votes whether every in-range element is -inf
+// (skip) or +-0 (full); anything else is mixed.  Elements outside
+// [0,Lq) x [0,Lk) are ignored; a tile with no in-range element is a skip tile.
 __global__ void __launch_bounds__(256) mask_classify_kernel(const MaskClassParams p) {
-    extern __shared__ unsigned flags[];  // per key tile: bit0 all -inf, bit1 all zero
-    const int qb = blockIdx.x;
-    const int plane = blockIdx.y;
-    const int mhi = plane % p.mh, mni = plane / p.mh;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int kb = threadIdx.x; kb < p.n_kb; kb += blockDim.x) flags[kb] = 3u;
-    __syncthreads();
-    const char* base = reinterpret_cast<const char*>(p.mask) + (long long)mni * p.nb3 + (long long)mhi * p.nb2;
-    for (int kb = 0; kb < p.n_kb; ++kb) {
+    const int lane = threadIdx.x & 31;
+    const long long tiles_per_plane = (long long)p.n_qb * p.n_kb;
+    const long long tiles = tiles_per_plane * p.mh * p.mn;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long t = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tiles; t += warps) {
+        const int plane = (int)(t / tiles_per_plane);
+        const long long r = t % tiles_per_plane;
+        const int qb = (int)(r / p.n_kb), kb = (int)(r % p.n_kb);
+        const int mhi = plane % p.mh, mni = plane / p.mh;
+        const char* base = reinterpret_cast<const char*>(p.mask) + (long long)mni * p.nb3 + (long long)mhi * p.nb2;
+        const int key = kb * 64 + 2 * lane;
+        const int rows = min(64, p.Lq - qb * 64);
         bool all_inf = true, all_zero = true;
-        for (int rr = warp; rr < 64; rr += 8) {
-            const int q = qb * 64 + rr;
-            if (q >= p.Lq) break;
-            const uint16_t* row = reinterpret_cast<const uint16_t*>(base + (long long)q * p.nb1);
+        for (int r0 = 0; r0 < rows; r0 += 8) {
+            uint16_t v[8][2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int key = kb * 64 + 2 * lane + e;
-                if (key < p.Lk) {
-                    const uint16_t b = __ldg(row + key);
-                    all_inf &= (b == 0xFC00u);
-                    all_zero &= ((b & 0x7FFFu) == 0u);
-                }
+            for (int i = 0; i < 8; ++i) {
+                const uint16_t* row = reinterpret_cast<const uint16_t*>(base + (long long)(qb * 64 + r0 + i) * p.nb1);
+                const bool in_row = r0 + i < rows;
+                v[i][0] = (in_row && key < p.Lk) ? __ldg(row + key) : (uint16_t)0xFC00u;
+                v[i][1] = (in_row && key + 1 < p.Lk) ? __ldg(row + key + 1) : (uint16_t)0xFC00u;
             }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const bool in = r0 + i < rows && key + e < p.Lk;
+                    if (in) {
+                        all_inf &= (v[i][e] == 0xFC00u);
+                        all_zero &= ((v[i][e] & 0x7FFFu) == 0u);
+                    }
+                }
         }
-        const unsigned wi = __all_sync(0xffffffffu, all_inf) ? 1u : 0u;
-        const unsigned wz = __all_sync(0xffffffffu, all_zero) ? 2u : 0u;
-        if (lane == 0 && (wi | wz) != 3u) atomicAnd(&flags[kb], wi | wz);
-    }
-    __syncthreads();
-    uint8_t* out = p.cls + ((long long)plane * p.n_qb + qb) * p.n_kb;
-    for (int kb = threadIdx.x; kb < p.n_kb; kb += blockDim.x) {
-        const unsigned f = flags[kb];
-        out[kb] = (f & 1u) ? kTileSkip : ((f & 2u) ? kTileFull : kTileMixed);
+        const bool wi = __all_sync(0xffffffffu, all_inf);
+        const bool wz = __all_sync(0xffffffffu, all_zero);
+        if (lane == 0) p.cls[t] = wi ? kTileSkip : (wz ? kTileFull : kTileMixed);
     }
 }
 
@@ -258,14 +262,10 @@ cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cud
 
 cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st) {
     if (p.n_qb == 0 || p.n_kb == 0) return cudaSuccess;
-    const size_t smem = (size_t)p.n_kb * sizeof(unsigned);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(mask_classify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    dim3 grid(p.n_qb, p.mh * p.mn);
-    mask_classify_kernel<<<grid, 256, smem, st>>>(p);
+    const long long tiles = (long long)p.n_qb * p.n_kb * p.mh * p.mn;
+    long long blocks = (tiles + 7) / 8;
+    if (blocks > 148LL * 64) blocks = 148LL * 64;
+    mask_classify_kernel<<<(int)blocks, 256, 0, st>>>(p);
     return cudaGetLastError();
 }
 
