@@ -22,7 +22,7 @@ struct kd_attn_ctx {
     kd_attn_log_cb log_cb = nullptr;
     void* log_user = nullptr;
     std::string last_error;
-    unsigned* d_words = nullptr;  // [0] sticky error bits, [1] per-launch abort flag
+    unsigned* d_words = nullptr;  // [0] sticky error bits, [1] per-launch abort flag, [2] work counter
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     int num_sms = 148;
@@ -358,8 +358,11 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
     p.kv_len = a.kv_len;
     p.err = ctx->d_words;
     p.abort_flag = ctx->d_words + 1;
+    p.work_counter = ctx->d_words + 2;
+    p.num_ctas = ctx->num_sms;
     p.wait_ns = ctx->wait_ns;
-    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, sizeof(unsigned), st));
+    // abort flag and work counter start at zero for every launch
+    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, 2 * sizeof(unsigned), st));
     KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
     return KD_ATTN_OK;
 }
@@ -552,8 +555,8 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
         return KD_ATTN_ERR_UNSUPPORTED;
     }
     ctx->num_sms = prop.multiProcessorCount;
-    if (cudaMalloc(&ctx->d_words, 2 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(ctx->d_words, 0, 2 * sizeof(unsigned)) != cudaSuccess) {
+    if (cudaMalloc(&ctx->d_words, 4 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->d_words, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
         return KD_ATTN_ERR_OUT_OF_MEMORY;
@@ -705,7 +708,7 @@ constexpr int kNoAllocMaxDevices = 64;
 // One copy per device, created when the module loads and kept until the process exits.
 // Host code must not use these names as addresses: it asks cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static __device__ __align__(256) unsigned g_noalloc_words[2];  // [0] sticky error bits, [1] abort flag
+static __device__ __align__(256) unsigned g_noalloc_words[4];  // [0] sticky error bits, [1] abort flag, [2] work counter
 
 struct NoAllocDevice {
     bool ready = false;
@@ -891,9 +894,11 @@ kd_attn_status flash_noalloc(const FlashArgs& a, cudaStream_t st) {
     p.kv_len = a.kv_len;
     p.err = d->words;
     p.abort_flag = d->words + 1;
+    p.work_counter = d->words + 2;
+    p.num_ctas = d->num_sms;
     p.wait_ns = 2000000000ull;
-    // the abort flag must start at zero for every launch (the array keeps the last call's contents)
-    KD_CUDA_NC(cudaMemsetAsync(d->words + 1, 0, sizeof(unsigned), st));
+    // abort flag and work counter must start at zero for every launch (the array keeps the last call's contents)
+    KD_CUDA_NC(cudaMemsetAsync(d->words + 1, 0, 2 * sizeof(unsigned), st));
     KD_CUDA_NC(launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
 #undef KD_CUDA_NC
     return KD_ATTN_OK;

@@ -26,6 +26,7 @@ enum : unsigned {
     kErrTimeoutO = 1u << 5,      // O accumulator never completed
     kErrBadLaunch = 1u << 6,     // launch geometry the kernel does not support
     kErrTimeoutDrain = 1u << 7,  // in-flight copies / MMAs did not drain on the abort path
+    kErrTimeoutList = 1u << 8,   // a unit's K/V tile list was never published / released
 };
 
 struct DevCtl {
@@ -75,11 +76,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // records `code` in the device error word and returns false; the caller then
 // unwinds its role without issuing further work.
 // With honor_abort = false (the drain path) only the time bound ends the wait.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const DevCtl& ctl, unsigned code,
-                                          bool honor_abort = true) {
-    if (mbar_try_wait(bar, parity)) return true;
+// sleep_ns > 0 backs off between polls, for waiters that are off the critical
+// path and should not take issue slots from the warps that are on it.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, const DevCtl ctl, unsigned code, bool honor_abort,
+                    unsigned sleep_ns) {
     const unsigned long long t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 700
+        if (sleep_ns) __nanosleep(sleep_ns);
+#endif
         if (mbar_try_wait(bar, parity)) return true;
         if ((n & 63u) == 0) {
             if (honor_abort && *reinterpret_cast<volatile unsigned*>(ctl.abort_flag)) return false;
@@ -90,6 +95,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
             }
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const DevCtl& ctl, unsigned code,
+                                          bool honor_abort = true, unsigned sleep_ns = 0) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_poll(bar, parity, ctl, code, honor_abort, sleep_ns);
 }
 
 // ------------------------------------------------------------------ TMA

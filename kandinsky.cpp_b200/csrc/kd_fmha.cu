@@ -4,18 +4,25 @@
 // reference) for head_dim 128:  O = softmax(scale * Q K^T + mask) V per
 // (head, sequence), fp32 accumulation, f16 or bf16 operands.
 //
-// One CTA owns 2 x 128 query rows of one (head, sequence) and streams the K/V
-// tiles of that head through a 4-stage shared-memory ring:
+// Persistent: one CTA per SM takes "units" -- 2 x 128 query rows of one
+// (head, sequence) -- from a global counter in increasing order and streams
+// the K/V tiles of each unit's head through a 4-stage shared-memory ring:
 //
-//   warp 0      TMA producer: Q0, Q1 once, then K_j, V_j (128 x 128 tiles,
+//   warp 0      TMA producer: Q0, Q1 per unit (as soon as the previous unit's
+//               last S MMA frees the Q buffer), then K_j, V_j (128 x 128 tiles,
 //               two 64-column boxes with 128-byte swizzle each)
 //   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T into TMEM (SS MMA,
 //               both operands K-major), O_i += P_i V_j (TS MMA, P from TMEM,
 //               V MN-major); owns the 512-column TMEM allocation
-//   warp 2      builds the list of K/V tiles this CTA must visit (tiles whose
-//               mask is entirely -inf for all 256 rows are never loaded)
+//   warp 2      scheduler: takes the next unit and publishes it with the list
+//               of K/V tiles it must visit (tiles whose mask is entirely -inf
+//               for all 256 rows are never loaded), one unit ahead
 //   warps 4-7   softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
 //   warps 8-11  the same for Q tile 1
+//
+// A unit's epilogue (O out of TMEM, normalise, store) overlaps the next
+// unit's Q load and first S MMAs; the next unit's first PV_i waits only for
+// the epilogue to have read O_i (o_free).
 //
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_i (16-bit,
 // two per column) overwrites the first 64 columns of S_i once S_i has been read.
@@ -69,13 +76,16 @@ constexpr int kThreads = 384;
 constexpr int kSmemQ = 0;
 constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
 constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
-// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], drain, p_half[2]
-constexpr int kNumBars = 1 + 2 * kStages + 6 + 1 + 2;
+// q_full, q_empty, kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full, o_free,
+// list_full, list_empty, and drain
+constexpr int kNumBars = 2 + 2 * kStages + 14 + 1;
 constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
-constexpr int kSmemNKept = kSmemTmemSlot + 4;
-constexpr int kSmemList = (kSmemNKept + 4 + 15) & ~15;
-constexpr int kSmemTotal = kSmemList + kMaxKvTiles * 4;
+constexpr int kSmemUnit = kSmemTmemSlot + 16;              // unit, n_kept, lk_eff per list buffer (6 ints)
+constexpr int kSmemList = (kSmemUnit + 6 * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
+constexpr int kSmemTotal = kSmemList + 2 * kMaxKvTiles * 4;
 constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
+// threads that release a list buffer: producer warp, MMA warp, both softmax warpgroups
+constexpr int kListConsumers = 32 + 32 + 2 * kBlockM;
 
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -138,32 +148,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int qblk = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
-    const int hk = h / p.rk2, nk = n / p.rk3;
     const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
+    const int n_qblk = (p.Lq + kRowsPerCta - 1) / kRowsPerCta;
+    const int n_units = n_qblk * p.H * p.N;
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
-    uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = bars + 1 + kStages;
-    uint64_t* s_full = bars + 1 + 2 * kStages;
-    uint64_t* p_full = s_full + 2;
-    uint64_t* o_full = s_full + 4;
-    uint64_t* drain = s_full + 6;
-    uint64_t* p_half = s_full + 7;   // first 64 keys of P_i written (PV may start on them)
+    uint64_t* q_full = bars + 0;
+    uint64_t* q_empty = bars + 1;
+    uint64_t* kv_full = bars + 2;
+    uint64_t* kv_empty = kv_full + kStages;
+    uint64_t* s_full = kv_empty + kStages;   // [2]
+    uint64_t* p_full = s_full + 2;           // [2]
+    uint64_t* p_half = s_full + 4;           // [2] first 64 keys of P_i written (split hand-off only)
+    uint64_t* o_full = s_full + 6;           // [2] last PV_i of a unit complete
+    uint64_t* o_free = s_full + 8;           // [2] epilogue has read O_i out of TMEM
+    uint64_t* list_full = s_full + 10;       // [2] unit descriptor + kept-tile list published
+    uint64_t* list_empty = s_full + 12;      // [2] every consumer is done with that list buffer
+    uint64_t* drain = s_full + 14;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
-    int* n_kept_slot = reinterpret_cast<int*>(smem + kSmemNKept);
-    uint32_t* list = reinterpret_cast<uint32_t*>(smem + kSmemList);
-
-    int lk_eff = p.Lk;
-    if (p.kv_len) {
-        const int kl = p.kv_len[n];
-        lk_eff = kl < 0 ? 0 : (kl < p.Lk ? kl : p.Lk);
-    }
-    const int n_kv_tiles = (lk_eff + kBlockN - 1) / kBlockN;
+    int* s_unit = reinterpret_cast<int*>(smem + kSmemUnit);     // [2] unit index, -1 = no more work
+    int* s_nkept = s_unit + 2;                                   // [2] kept K/V tiles of the unit
+    int* s_lkeff = s_unit + 4;                                   // [2] valid keys of the unit's sequence
+    uint32_t* lists = reinterpret_cast<uint32_t*>(smem + kSmemList);  // [2][kMaxKvTiles]
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
@@ -173,6 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&p_full[i], kBlockM);
             mbar_init(&p_half[i], kBlockM);
             mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], kBlockM);
+            mbar_init(&list_full[i], 32);
+            mbar_init(&list_empty[i], kListConsumers);
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -181,368 +194,448 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 2) {
-        // Kept-tile list: entry = (kv tile index << 16) | 2-bit class per (64-row group g, 64-key half hh)
-        // at bit 4g + 2hh.  Without a mask every tile is FULL; the kv_len / Lk tail is masked by index.
-        int count = 0;
-        const long long plane =
-            p.tile_cls ? ((long long)(n % p.mn) * p.mh + (h % p.mh)) * (long long)p.n_qb * p.n_kb : 0;
-        for (int base = 0; base < n_kv_tiles; base += 32) {
-            const int t = base + lane;
-            uint32_t bits = 0;
-            if (t < n_kv_tiles) {
-                if (p.tile_cls) {
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const int qb = qblk * 4 + g;
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            const int kb = 2 * t + hh;
-                            uint32_t c = kTileSkip;
-                            if (qb < p.n_qb && kb < p.n_kb) c = p.tile_cls[plane + (long long)qb * p.n_kb + kb];
-                            bits |= (c & 3u) << (4 * g + 2 * hh);
-                        }
-                    }
-                } else {
-                    bits = 0x5555u;
-                }
-            }
-            const bool kept = bits != 0;
-            const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
-            if (kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)t << 16) | bits;
-            count += __popc(ballot);
-        }
-        if (lane == 0) *n_kept_slot = count;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
     const uint32_t tmem = *tmem_slot;
-    const int n_iter = *n_kept_slot;
-    const bool skip_all = *reinterpret_cast<volatile unsigned*>(p.abort_flag) != 0;
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
 
-    if (skip_all) {
-        // another CTA already gave up: do nothing, just release TMEM below
-    } else if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
-        if (n_iter > 0) {
+    if (warp == 2) {
+        // ------------------------------------------------------------ work scheduler + list builder
+        // Takes units (256 query rows of one head and sequence) from the global counter in increasing
+        // order, so CTAs working at the same time share heads and their K/V stay in L2.  For each unit
+        // it publishes the list of K/V tiles to visit: entry = (tile << 16) | 2-bit class per
+        // (64-row group g, 64-key half hh) at bit 4g + 2hh; without a mask every tile is FULL and the
+        // kv_len / Lk tail is masked by index.  Double-buffered: unit t+1's list is built while unit t runs.
+        for (int t = 0;; ++t) {
+            const int b = t & 1;
+            // one unit ahead of the consumers: poll slowly so the softmax warps keep the issue slots
+            if (t >= 2 && !__all_sync(0xffffffffu, mbar_wait(&list_empty[b], ((t >> 1) - 1) & 1, ctl,
+                                                               kErrTimeoutList, true, 2000)))
+                break;
+            int u = 0;
+            if (lane == 0) u = (int)atomicAdd(p.work_counter, 1u);
+            u = __shfl_sync(0xffffffffu, u, 0);
+            if (u >= n_units || *reinterpret_cast<volatile unsigned*>(p.abort_flag)) {
+                if (lane == 0) s_unit[b] = -1;
+                __syncwarp();
+                mbar_arrive(&list_full[b]);
+                break;
+            }
+            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+            int lk_eff = p.Lk;
+            if (p.kv_len) {
+                const int kl = p.kv_len[n];
+                lk_eff = kl < 0 ? 0 : (kl < p.Lk ? kl : p.Lk);
+            }
+            const int n_kv_tiles = (lk_eff + kBlockN - 1) / kBlockN;
+            uint32_t* list = lists + b * kMaxKvTiles;
+            int count = 0;
+            const long long plane =
+                p.tile_cls ? ((long long)(n % p.mn) * p.mh + (h % p.mh)) * (long long)p.n_qb * p.n_kb : 0;
+            for (int base = 0; base < n_kv_tiles; base += 32) {
+                const int kt = base + lane;
+                uint32_t bits = 0;
+                if (kt < n_kv_tiles) {
+                    if (p.tile_cls) {
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            const int qb = qblk * 4 + g;
+#pragma unroll
+                            for (int hh = 0; hh < 2; ++hh) {
+                                const int kb = 2 * kt + hh;
+                                uint32_t c = kTileSkip;
+                                if (qb < p.n_qb && kb < p.n_kb) c = p.tile_cls[plane + (long long)qb * p.n_kb + kb];
+                                bits |= (c & 3u) << (4 * g + 2 * hh);
+                            }
+                        }
+                    } else {
+                        bits = 0x5555u;
+                    }
+                }
+                const bool kept = bits != 0;
+                const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
+                if (kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)kt << 16) | bits;
+                count += __popc(ballot);
+            }
             if (lane == 0) {
-                tma_prefetch_desc(&tmQ);
-                tma_prefetch_desc(&tmK);
-                tma_prefetch_desc(&tmV);
-                mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
-                const int q0 = qblk * kRowsPerCta;
-#pragma unroll
-                for (int i = 0; i < kQTiles; ++i)
-#pragma unroll
-                    for (int b = 0; b < 2; ++b)
-                        tma_load_4d(smem + kSmemQ + i * kTileBytes + b * kBoxBytes, &tmQ, q_full, b * 64,
-                                    q0 + i * kBlockM, h, n);
+                s_unit[b] = u;
+                s_nkept[b] = count;
+                s_lkeff[b] = lk_eff;
             }
             __syncwarp();
-            uint32_t it = 0;
-            bool ok = true;
-            for (int j = 0; j < n_iter && ok; ++j) {
-                const int kt = (int)(list[j] >> 16);
-#pragma unroll 1
-                for (int w = 0; w < 2; ++w) {  // w = 0: K tile, w = 1: V tile
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1u;
-                    ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
-                    if (!ok) break;
-                    KD_TRACE(0, w, j);
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
-                        const CUtensorMap* map = w ? &tmV : &tmK;
+            mbar_arrive(&list_full[b]);  // every lane: releases its own list writes
+        }
+    } else if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        uint32_t it = 0;      // K/V ring position (continues across units)
+        uint32_t q_uses = 0;  // units whose Q was loaded
+        bool ok = true;
+        for (int t = 0; ok; ++t) {
+            const int b = t & 1;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int u = s_unit[b];
+            if (u < 0) break;
+            const int n_iter = s_nkept[b];
+            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+            const int hk = h / p.rk2, nk = n / p.rk3;
+            const uint32_t* list = lists + b * kMaxKvTiles;
+            if (n_iter > 0) {
+                // Q buffer is free once the previous unit's last S MMA has completed
+                if (q_uses > 0 &&
+                    !(ok = __all_sync(0xffffffffu, mbar_wait(q_empty, (q_uses - 1) & 1, ctl, kErrTimeoutQ))))
+                    break;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
 #pragma unroll
-                        for (int b = 0; b < 2; ++b)
-                            tma_load_4d(smem + kSmemKV + s * kTileBytes + b * kBoxBytes, map, &kv_full[s], b * 64,
-                                        kt * kBlockN, hk, nk);
-                    }
-                    __syncwarp();
-                    ++it;
+                    for (int i = 0; i < kQTiles; ++i)
+#pragma unroll
+                        for (int bx = 0; bx < 2; ++bx)
+                            tma_load_4d(smem + kSmemQ + i * kTileBytes + bx * kBoxBytes, &tmQ, q_full, bx * 64,
+                                        qblk * kRowsPerCta + i * kBlockM, h, n);
                 }
+                __syncwarp();
+                ++q_uses;
+                for (int j = 0; j < n_iter && ok; ++j) {
+                    const int kt = (int)(list[j] >> 16);
+#pragma unroll 1
+                    for (int w = 0; w < 2; ++w) {  // w = 0: K tile, w = 1: V tile
+                        const int s = it % kStages;
+                        const uint32_t ph = (it / kStages) & 1u;
+                        ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
+                        if (!ok) break;
+                        KD_TRACE(0, w, j);
+                        if (lane == 0) {
+                            mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+                            const CUtensorMap* map = w ? &tmV : &tmK;
+#pragma unroll
+                            for (int bx = 0; bx < 2; ++bx)
+                                tma_load_4d(smem + kSmemKV + s * kTileBytes + bx * kBoxBytes, map, &kv_full[s],
+                                            bx * 64, kt * kBlockN, hk, nk);
+                        }
+                        __syncwarp();
+                        ++it;
+                    }
+                }
+                if (!ok) break;
             }
-            if (!ok) {
-                // Abort path: wait (bounded, ignoring the abort flag) until every copy this warp
-                // issued has landed, so no TMA write targets shared memory after the CTA exits.
-                mbar_wait(q_full, 0, ctl, kErrTimeoutDrain, false);
-                for (uint32_t k = (it > (uint32_t)kStages ? it - kStages : 0u); k < it; ++k)
-                    mbar_wait(&kv_full[k % kStages], (k / kStages) & 1u, ctl, kErrTimeoutDrain, false);
-            }
+            mbar_arrive(&list_empty[b]);
+        }
+        if (!ok) {
+            // Abort path: wait (bounded, ignoring the abort flag) until every copy this warp issued has
+            // landed, so no TMA write targets shared memory after the CTA exits.
+            if (q_uses > 0) mbar_wait(q_full, (q_uses - 1) & 1, ctl, kErrTimeoutDrain, false);
+            for (uint32_t k = (it > (uint32_t)kStages ? it - kStages : 0u); k < it; ++k)
+                mbar_wait(&kv_full[k % kStages], (k / kStages) & 1u, ctl, kErrTimeoutDrain, false);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (n_iter > 0) {
-            const uint32_t qa = smem_u32(smem + kSmemQ);
-            const uint32_t kva = smem_u32(smem + kSmemKV);
-            constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
-            constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
-            uint32_t it = 0;
-            bool issued = false;
+        const uint32_t qa = smem_u32(smem + kSmemQ);
+        const uint32_t kva = smem_u32(smem + kSmemKV);
+        constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
+        constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
+        uint32_t it = 0;       // K/V ring position
+        uint32_t g = 0;        // (unit, tile) iterations: phase of p_half / p_full
+        uint32_t units = 0;    // units with at least one tile: phase of q_full / o_free
+        bool issued = false;
 
-            auto next_stage = [&](int& s) -> bool {
-                s = it % kStages;
-                const uint32_t ph = (it / kStages) & 1u;
-                ++it;
-                return __all_sync(0xffffffffu, mbar_wait(&kv_full[s], ph, ctl, kErrTimeoutKVFull));
-            };
-            auto issue_s = [&](int i, int s) {
-                if (lane == 0) {
+        auto next_stage = [&](int& s) -> bool {
+            s = it % kStages;
+            const uint32_t ph = (it / kStages) & 1u;
+            ++it;
+            return __all_sync(0xffffffffu, mbar_wait(&kv_full[s], ph, ctl, kErrTimeoutKVFull));
+        };
+        auto issue_s = [&](int i, int s) {
+            if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                        mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
-                               desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
-                    }
+                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
+                           desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
                 }
-                __syncwarp();
-            };
-            // O_i += P_i V for keys [64*half, 64*half + 64): P columns 32*half.., V rows 64*half..
-            auto issue_pv = [&](int i, int s, bool acc, int half) {
-                if (lane == 0) {
-#pragma unroll
-                    for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
-                        const int kk = half * (kBlockN / 32) + k4;
-                        mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
-                               desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
-                               (acc || kk > 0) ? 1u : 0u);
-                    }
-                }
-                __syncwarp();
-            };
-            // wait for one half of P_i (phase j), then issue that half of PV
-            auto pv_half = [&](int i, int s, int j, int half) -> bool {
-                if (!kSplitP) {  // one hand-off: wait for all of P, then issue both halves
-                    if (half) return true;
-                    if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], j & 1, ctl, kErrTimeoutP))) return false;
-                    tc_fence_after();
-                    issue_pv(i, s, j > 0, 0);
-                    issue_pv(i, s, j > 0, 1);
-                    return true;
-                }
-                uint64_t* bar = half ? &p_full[i] : &p_half[i];
-                if (!__all_sync(0xffffffffu, mbar_wait(bar, j & 1, ctl, kErrTimeoutP))) return false;
-                tc_fence_after();
-                issue_pv(i, s, j > 0, half);
-                return true;
-            };
-            auto commit = [&](uint64_t* b) {
-                if (lane == 0) tc_commit(b);
-                __syncwarp();
-            };
-
-            bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, ctl, kErrTimeoutQ));
-            int sK = 0, sV = 0;
-            if (ok) ok = next_stage(sK);
-            if (ok) {
-                tc_fence_after();
-                issue_s(0, sK);
-                commit(&s_full[0]);
-                issue_s(1, sK);
-                commit(&s_full[1]);
-                commit(&kv_empty[sK]);
-                issued = true;
             }
-            for (int j = 0; j < n_iter && ok; ++j) {
+            __syncwarp();
+        };
+        // O_i += P_i V for keys [64*half, 64*half + 64): P columns 32*half.., V rows 64*half..
+        auto issue_pv = [&](int i, int s, bool acc, int half) {
+            if (lane == 0) {
+#pragma unroll
+                for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+                    const int kk = half * (kBlockN / 32) + k4;
+                    mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
+                           desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
+                           (acc || kk > 0) ? 1u : 0u);
+                }
+            }
+            __syncwarp();
+        };
+        auto commit = [&](uint64_t* bar) {
+            if (lane == 0) tc_commit(bar);
+            __syncwarp();
+        };
+        // wait for P_i of iteration g (both halves, or each half with the split hand-off), issue PV_i
+        auto pv = [&](int i, int s, bool acc) -> bool {
+            if (kSplitP) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_half[i], g & 1, ctl, kErrTimeoutP))) return false;
+                tc_fence_after();
+                issue_pv(i, s, acc, 0);
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], g & 1, ctl, kErrTimeoutP))) return false;
+                tc_fence_after();
+                issue_pv(i, s, acc, 1);
+                return true;
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], g & 1, ctl, kErrTimeoutP))) return false;
+            tc_fence_after();
+            issue_pv(i, s, acc, 0);
+            issue_pv(i, s, acc, 1);
+            return true;
+        };
+
+        bool ok = true;
+        for (int t = 0; ok; ++t) {
+            const int b = t & 1;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int u = s_unit[b];
+            if (u < 0) break;
+            const int n_iter = s_nkept[b];
+            mbar_arrive(&list_empty[b]);
+            if (n_iter == 0) continue;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(q_full, units & 1, ctl, kErrTimeoutQ)))) break;
+            int sK = 0, sV = 0;
+            if (!(ok = next_stage(sK))) break;
+            tc_fence_after();
+            issue_s(0, sK);
+            commit(&s_full[0]);
+            issue_s(1, sK);
+            commit(&s_full[1]);
+            commit(&kv_empty[sK]);
+            if (n_iter == 1) commit(q_empty);  // the unit's last S MMA is issued: Q may be replaced
+            issued = true;
+            for (int j = 0; j < n_iter; ++j, ++g) {
                 const bool more = j + 1 < n_iter;
                 if (!(ok = next_stage(sV))) break;
-                KD_TRACE(1, 0, j);
-                if (!(ok = pv_half(0, sV, j, 0))) break;
-                if (!(ok = pv_half(0, sV, j, 1))) break;
-                KD_TRACE(1, 1, j);
+                KD_TRACE(1, 0, g);
+                // the first PV of a unit overwrites O_i: the previous unit's epilogue must have read it
+                if (j == 0 && units > 0 &&
+                    !(ok = __all_sync(0xffffffffu, mbar_wait(&o_free[0], (units - 1) & 1, ctl, kErrTimeoutO))))
+                    break;
+                if (!(ok = pv(0, sV, j > 0))) break;
+                KD_TRACE(1, 1, g);
                 if (!more) commit(&o_full[0]);
                 int sK2 = 0;
                 if (more) {
                     if (!(ok = next_stage(sK2))) break;
                     issue_s(0, sK2);
-                    KD_TRACE(1, 2, j);
+                    KD_TRACE(1, 2, g);
                     commit(&s_full[0]);
                 }
-                if (!(ok = pv_half(1, sV, j, 0))) break;
-                if (!(ok = pv_half(1, sV, j, 1))) break;
-                KD_TRACE(1, 3, j);
+                if (j == 0 && units > 0 &&
+                    !(ok = __all_sync(0xffffffffu, mbar_wait(&o_free[1], (units - 1) & 1, ctl, kErrTimeoutO))))
+                    break;
+                if (!(ok = pv(1, sV, j > 0))) break;
+                KD_TRACE(1, 3, g);
                 commit(&kv_empty[sV]);
                 if (!more) {
                     commit(&o_full[1]);
                 } else {
                     issue_s(1, sK2);
-                    KD_TRACE(1, 4, j);
+                    KD_TRACE(1, 4, g);
                     commit(&s_full[1]);
                     commit(&kv_empty[sK2]);
+                    if (j + 2 == n_iter) commit(q_empty);
                 }
             }
-            if (issued) {
-                // every MMA issued above must retire before the TMEM is released
-                commit(drain);
-                mbar_wait(drain, 0, ctl, kErrTimeoutDrain, false);
-            }
+            ++units;
+        }
+        if (issued) {
+            // every MMA issued above must retire before the TMEM is released
+            commit(drain);
+            mbar_wait(drain, 0, ctl, kErrTimeoutDrain, false);
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax / correction / epilogue
         const int wg = (warp - 4) >> 2;
         const int r = ((warp & 3) << 5) + lane;          // TMEM lane = row within the Q tile
-        const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
-        const bool row_valid = qrow < p.Lq;
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_addr + wg * 128;
         const uint32_t tO = tmem + lane_addr + 256 + wg * 128;
-        const int g = wg * 2 + (r >> 6);                 // 64-row group of this row within the CTA
-        const uint16_t* mrow = nullptr;
-        if (p.mask && row_valid)
-            mrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const char*>(p.mask) +
-                                                     (long long)(n % p.mn) * p.m_nb3 +
-                                                     (long long)(h % p.mh) * p.m_nb2 + (long long)qrow * p.m_nb1);
+        const int g4 = wg * 2 + (r >> 6);                // 64-row group of this row within the unit
         const float sl2 = p.scale_log2;
-
-        float m = -INFINITY, l = 0.f;
+        uint32_t g = 0;      // (unit, tile) iterations: phase of s_full
+        uint32_t units = 0;  // units with at least one tile: phase of o_full
         bool ok = true;
-        for (int j = 0; j < n_iter; ++j) {
-            const uint32_t e = list[j];
-            const int kbase = (int)(e >> 16) * kBlockN;
-            const uint32_t c0 = (e >> (4 * g)) & 3u, c1 = (e >> (4 * g + 2)) & 3u;
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], j & 1, ctl, kErrTimeoutS)))) break;
-            if ((warp & 3) == 0) KD_TRACE(2 + wg, 0, j);
-            tc_fence_after();
+        for (int t = 0; ok; ++t) {
+            const int b = t & 1;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int u = s_unit[b];
+            if (u < 0) break;
+            const int n_iter = s_nkept[b];
+            const int lk_eff = s_lkeff[b];
+            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+            const uint32_t* list = lists + b * kMaxKvTiles;
+            const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
+            const bool row_valid = qrow < p.Lq;
+            const uint16_t* mrow = nullptr;
+            if (p.mask && row_valid)
+                mrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const char*>(p.mask) +
+                                                         (long long)(n % p.mn) * p.m_nb3 +
+                                                         (long long)(h % p.mh) * p.m_nb2 + (long long)qrow * p.m_nb1);
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < n_iter; ++j, ++g) {
+                const uint32_t e = list[j];
+                const int kbase = (int)(e >> 16) * kBlockN;
+                const uint32_t c0 = (e >> (4 * g4)) & 3u, c1 = (e >> (4 * g4 + 2)) & 3u;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], g & 1, ctl, kErrTimeoutS)))) break;
+                if ((warp & 3) == 0) KD_TRACE(2 + wg, 0, g);
+                tc_fence_after();
 
-            // Mixed tiles: add the additive mask (divided by scale, so that scale*(s + m/scale) =
-            // scale*s + m) into S in TMEM, 32 columns at a time.  c0/c1 are warp-uniform (a warp's
-            // 32 rows lie in one 64-row group).
-            if (c0 == kTileMixed || c1 == kTileMixed) {
+                // Mixed tiles: add the additive mask (divided by scale, so that scale*(s + m/scale) =
+                // scale*s + m) into S in TMEM, 32 columns at a time.  c0/c1 are warp-uniform (a warp's
+                // 32 rows lie in one 64-row group).
+                if (c0 == kTileMixed || c1 == kTileMixed) {
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    if ((c < 2 ? c0 : c1) != kTileMixed) continue;
-                    uint32_t x[32];
-                    tmem_ld32_sync(tS + c * 32, x);
-                    if (mrow) {
+                    for (int c = 0; c < 4; ++c) {
+                        if ((c < 2 ? c0 : c1) != kTileMixed) continue;
+                        uint32_t x[32];
+                        tmem_ld32_sync(tS + c * 32, x);
+                        if (mrow) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int key = kbase + c * 32 + i;
-                            if (key < lk_eff) {
-                                const float mv = __half2float(__ushort_as_half(__ldg(mrow + key)));
-                                x[i] = __float_as_uint(fmaf(mv, p.inv_scale, __uint_as_float(x[i])));
+                            for (int i = 0; i < 32; ++i) {
+                                const int key = kbase + c * 32 + i;
+                                if (key < lk_eff) {
+                                    const float mv = __half2float(__ushort_as_half(__ldg(mrow + key)));
+                                    x[i] = __float_as_uint(fmaf(mv, p.inv_scale, __uint_as_float(x[i])));
+                                }
                             }
                         }
+                        tmem_st32(tS + c * 32, x);
                     }
-                    tmem_st32(tS + c * 32, x);
+                    tmem_wait_st();
                 }
-                tmem_wait_st();
-            }
-            uint32_t su[128];
-            tmem_ld128_sync(tS, su);
-            if ((warp & 3) == 0) KD_TRACE(2 + wg, 1, j);
-            // Skipped halves and keys past the valid length become -inf.
-            {
-                const int lim = lk_eff - kbase;
-                const int lim0 = c0 == kTileSkip ? 0 : lim;
-                const int lim1 = c1 == kTileSkip ? 0 : lim;
-                if (lim0 < 64 || lim1 < 128) {
+                uint32_t su[128];
+                tmem_ld128_sync(tS, su);
+                if ((warp & 3) == 0) KD_TRACE(2 + wg, 1, g);
+                // Skipped halves and keys past the valid length become -inf.
+                {
+                    const int lim = lk_eff - kbase;
+                    const int lim0 = c0 == kTileSkip ? 0 : lim;
+                    const int lim1 = c1 == kTileSkip ? 0 : lim;
+                    if (lim0 < 64 || lim1 < 128) {
 #pragma unroll
-                    for (int c = 0; c < 128; ++c)
-                        if (c >= (c < 64 ? lim0 : lim1)) su[c] = __float_as_uint(-INFINITY);
+                        for (int c = 0; c < 128; ++c)
+                            if (c >= (c < 64 ? lim0 : lim1)) su[c] = __float_as_uint(-INFINITY);
+                    }
                 }
-            }
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #if KD_FMHA_MAX3
 #pragma unroll
-            for (int c = 0; c < 128; c += 8) {
-                mx0 = fmax3(mx0, __uint_as_float(su[c]), __uint_as_float(su[c + 1]));
-                mx1 = fmax3(mx1, __uint_as_float(su[c + 2]), __uint_as_float(su[c + 3]));
-                mx2 = fmax3(mx2, __uint_as_float(su[c + 4]), __uint_as_float(su[c + 5]));
-                mx3 = fmax3(mx3, __uint_as_float(su[c + 6]), __uint_as_float(su[c + 7]));
-            }
+                for (int c = 0; c < 128; c += 8) {
+                    mx0 = fmax3(mx0, __uint_as_float(su[c]), __uint_as_float(su[c + 1]));
+                    mx1 = fmax3(mx1, __uint_as_float(su[c + 2]), __uint_as_float(su[c + 3]));
+                    mx2 = fmax3(mx2, __uint_as_float(su[c + 4]), __uint_as_float(su[c + 5]));
+                    mx3 = fmax3(mx3, __uint_as_float(su[c + 6]), __uint_as_float(su[c + 7]));
+                }
 #else
 #pragma unroll
-            for (int c = 0; c < 128; c += 4) {
-                mx0 = fmaxf(mx0, __uint_as_float(su[c]));
-                mx1 = fmaxf(mx1, __uint_as_float(su[c + 1]));
-                mx2 = fmaxf(mx2, __uint_as_float(su[c + 2]));
-                mx3 = fmaxf(mx3, __uint_as_float(su[c + 3]));
-            }
+                for (int c = 0; c < 128; c += 4) {
+                    mx0 = fmaxf(mx0, __uint_as_float(su[c]));
+                    mx1 = fmaxf(mx1, __uint_as_float(su[c + 1]));
+                    mx2 = fmaxf(mx2, __uint_as_float(su[c + 2]));
+                    mx3 = fmaxf(mx3, __uint_as_float(su[c + 3]));
+                }
 #endif
-            const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
-            if ((warp & 3) == 0) KD_TRACE(2 + wg, 2, j);
-            const float m_new = fmaxf(m, m_tile);
-            const bool resc = m_new > m + kRescaleThreshold;
-            const bool warp_resc = __any_sync(0xffffffffu, resc);
-            float alpha = 1.0f;
-            if (resc) {
-                alpha = ex2_approx(m - m_new);
-                l *= alpha;
-                m = m_new;
-            }
-            const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-            float rs0 = 0.f, rs1 = 0.f;
-            // P for 32 keys -> 16 packed columns of S_i's TMEM
-            auto p_chunk = [&](int c) {
-                uint32_t pk[16];
+                const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+                if ((warp & 3) == 0) KD_TRACE(2 + wg, 2, g);
+                const float m_new = fmaxf(m, m_tile);
+                const bool resc = m_new > m + kRescaleThreshold;
+                const bool warp_resc = __any_sync(0xffffffffu, resc);
+                float alpha = 1.0f;
+                if (resc) {
+                    alpha = ex2_approx(m - m_new);
+                    l *= alpha;
+                    m = m_new;
+                }
+                const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+                float rs0 = 0.f, rs1 = 0.f;
+                // P for 32 keys -> 16 packed columns of S_i's TMEM
+                auto p_chunk = [&](int c) {
+                    uint32_t pk[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float xa = fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu);
-                    const float xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
-                    float a, b;
-                    if ((kPolyPairs >> i) & 1u) {
-                        a = exp2_poly(xa);
-                        b = exp2_poly(xb);
-                    } else {
-                        a = ex2_approx(xa);
-                        b = ex2_approx(xb);
+                    for (int i = 0; i < 16; ++i) {
+                        const float xa = fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu);
+                        const float xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
+                        float a, bb;
+                        if ((kPolyPairs >> i) & 1u) {
+                            a = exp2_poly(xa);
+                            bb = exp2_poly(xb);
+                        } else {
+                            a = ex2_approx(xa);
+                            bb = ex2_approx(xb);
+                        }
+                        rs0 += a;
+                        rs1 += bb;
+                        pk[i] = Pack2<T>::pack(a, bb);
                     }
-                    rs0 += a;
-                    rs1 += b;
-                    pk[i] = Pack2<T>::pack(a, b);
-                }
-                tmem_st16(tS + c * 16, pk);
-            };
-            p_chunk(0);
-            p_chunk(1);
-            if ((warp & 3) == 0) KD_TRACE(2 + wg, 3, j);
-            // Rescale O_i (PV_i(j-1) is complete: its commit preceded S_i(j)'s).  It only has to
-            // precede the first PV_i(j) MMA, i.e. the p_half arrive; the first 64 scores are dead here.
-            if (warp_resc && j > 0) {
+                    tmem_st16(tS + c * 16, pk);
+                };
+                p_chunk(0);
+                p_chunk(1);
+                if ((warp & 3) == 0) KD_TRACE(2 + wg, 3, g);
+                // Rescale O_i (PV_i of the previous tile is complete: its commit preceded S_i's).  It only
+                // has to precede the first PV_i MMA of this tile; the first 64 scores are dead here.
+                if (warp_resc && j > 0) {
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32_sync(tO + c * 32, o);
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32_sync(tO + c * 32, o);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(tO + c * 32, o);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(tO + c * 32, o);
+                    }
                 }
-            }
-            if (kSplitP) {
+                if (kSplitP) {
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&p_half[wg]);
+                }
+                p_chunk(2);
+                p_chunk(3);
                 tmem_wait_st();
+                l += rs0 + rs1;
                 tc_fence_before();
-                mbar_arrive(&p_half[wg]);
+                mbar_arrive(&p_full[wg]);
+                if ((warp & 3) == 0) KD_TRACE(2 + wg, 4, g);
             }
-            p_chunk(2);
-            p_chunk(3);
-            tmem_wait_st();
-            l += rs0 + rs1;
-            tc_fence_before();
-            mbar_arrive(&p_full[wg]);
-            if ((warp & 3) == 0) KD_TRACE(2 + wg, 4, j);
-        }
+            if (!ok) break;
+            mbar_arrive(&list_empty[b]);
 
-        if (ok) {
+            // epilogue: O_i / l -> out rows, LSE
             TO* orow = nullptr;
             if (row_valid)
                 orow = reinterpret_cast<TO*>(reinterpret_cast<char*>(p.out) + (long long)n * p.o_nb3 +
                                              (long long)qrow * p.o_nb2 + (long long)h * p.o_nb1);
             if (n_iter > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&o_full[wg], 0, ctl, kErrTimeoutO));
-                if (ok) {
-                    tc_fence_after();
-                    const float inv = l > 0.f ? 1.0f / l : 0.f;
-#pragma unroll 1
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&o_full[wg], units & 1, ctl, kErrTimeoutO)))) break;
+                tc_fence_after();
+                uint32_t ov[128];
+                tmem_ld128_sync(tO, ov);
+                tc_fence_before();
+                mbar_arrive(&o_free[wg]);  // the next unit's PV_i may overwrite O_i now
+                ++units;
+                const float inv = l > 0.f ? 1.0f / l : 0.f;
+                if (orow) {
+#pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32_sync(tO + c * 32, o);
                         float v[32];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
-                        if (orow) store_row32<TO>(orow + c * 32, v);
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[c * 32 + i]) * inv;
+                        store_row32<TO>(orow + c * 32, v);
                     }
                 }
             } else if (orow) {
@@ -552,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) store_row32<TO>(orow + c * 32, z);
             }
-            if (ok && row_valid && p.lse)
+            if (row_valid && p.lse)
                 p.lse[((long long)n * p.H + h) * p.Lq + qrow] = (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
         }
     }
@@ -572,7 +665,11 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
     // set on every launch: the attribute belongs to the current device, and the call is cheap
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
     if (e != cudaSuccess) return e;
-    dim3 grid((p.Lq + kRowsPerCta - 1) / kRowsPerCta, p.H, p.N);
+    // Persistent: one CTA per SM (never more CTAs than units); units are handed out by p.work_counter,
+    // which also balances units of unequal cost (masks, kv_len).
+    const long long units = (long long)((p.Lq + kRowsPerCta - 1) / kRowsPerCta) * p.H * p.N;
+    const int grid = (int)(units < p.num_ctas ? units : p.num_ctas);
+    if (grid <= 0) return cudaSuccess;
     kern<<<grid, kThreads, kSmemAlloc, st>>>(tmQ, tmK, tmV, p);
     return cudaGetLastError();
 }

@@ -17,7 +17,7 @@ constexpr int kBlockM = 128;   // query rows per Q tile = one M=128 tcgen05 MMA
 constexpr int kQTiles = 2;     // Q tiles per CTA, one softmax warpgroup each
 constexpr int kRowsPerCta = kBlockM * kQTiles;
 constexpr int kBlockN = 128;   // keys per K/V tile
-constexpr int kMaxKvTiles = 4096;  // per-CTA kept-tile list capacity (Lk <= 524288)
+constexpr int kMaxKvTiles = 2048;  // per-unit kept-tile list capacity (Lk <= 262144)
 
 struct FmhaParams {
     int Lq, Lk, H, N;        // query rows, keys, heads, sequences
@@ -35,6 +35,8 @@ struct FmhaParams {
     const int32_t* kv_len;   // [N] or null
     unsigned* err;           // sticky device error word
     unsigned* abort_flag;    // per-launch abort flag (cleared by the host before each launch)
+    unsigned* work_counter;  // next unit to hand out (cleared by the host before each launch)
+    int num_ctas;            // persistent grid size (number of SMs)
     unsigned long long wait_ns;
 };
 
