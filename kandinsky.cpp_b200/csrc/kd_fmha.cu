@@ -80,8 +80,8 @@ constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
 // list_full, list_empty, and drain
 constexpr int kNumBars = 2 + 2 * kStages + 14 + 1;
 constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
-constexpr int kSmemUnit = kSmemTmemSlot + 16;              // unit, n_kept, lk_eff per list buffer (6 ints)
-constexpr int kSmemList = (kSmemUnit + 6 * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
+constexpr int kSmemUnit = kSmemTmemSlot + 16;               // unit, n_kept, lk_eff, last0, last1 per list buffer
+constexpr int kSmemList = (kSmemUnit + 10 * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
 constexpr int kSmemTotal = kSmemList + 2 * kMaxKvTiles * 4;
 constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
 // threads that release a list buffer: producer warp, MMA warp, both softmax warpgroups
@@ -106,6 +106,10 @@ constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8 between r
 #define KD_FMHA_MAX3 1
 #endif
 constexpr uint32_t kPolyPairs = KD_FMHA_POLY_PAIRS;
+
+// A list entry's class bits cover the unit's four 64-row groups, two per Q tile: Q tile i needs
+// the K/V tile unless all four of its (row group, key half) classes are "skip".
+__device__ __forceinline__ bool tile_needed(uint32_t entry, int i) { return ((entry >> (8 * i)) & 0xFFu) != 0; }
 constexpr bool kSplitP = KD_FMHA_SPLIT_P != 0;
 
 static_assert(kSmemAlloc <= 232448, "shared memory budget");
@@ -139,7 +143,7 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v
                           Pack2<__half>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
 
-template <typename T, typename TO>
+template <typename T, typename TO, bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FmhaParams p) {
@@ -169,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int* s_unit = reinterpret_cast<int*>(smem + kSmemUnit);     // [2] unit index, -1 = no more work
     int* s_nkept = s_unit + 2;                                   // [2] kept K/V tiles of the unit
     int* s_lkeff = s_unit + 4;                                   // [2] valid keys of the unit's sequence
+    int* s_last = s_unit + 6;                                    // [2][2] last list entry Q tile i needs, -1: none
     uint32_t* lists = reinterpret_cast<uint32_t*>(smem + kSmemList);  // [2][kMaxKvTiles]
 
     if (threadIdx.x == 0) {
@@ -200,6 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t tmem = *tmem_slot;
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    // Without a mask every listed K/V tile is needed by both Q tiles; the dense instantiation folds
+    // the per-Q-tile skip tests away.
+    auto need = [](uint32_t entry, int i) { return !kSparse || tile_needed(entry, i); };
+
 
     if (warp == 2) {
         // ------------------------------------------------------------ work scheduler + list builder
@@ -232,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_kv_tiles = (lk_eff + kBlockN - 1) / kBlockN;
             uint32_t* list = lists + b * kMaxKvTiles;
             int count = 0;
+            int last[2] = {-1, -1};
             const long long plane =
                 p.tile_cls ? ((long long)(n % p.mn) * p.mh + (h % p.mh)) * (long long)p.n_qb * p.n_kb : 0;
             for (int base = 0; base < n_kv_tiles; base += 32) {
@@ -257,12 +267,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool kept = bits != 0;
                 const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
                 if (kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)kt << 16) | bits;
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {  // position of the last entry Q tile i needs
+                    const uint32_t bi = __ballot_sync(0xffffffffu, tile_needed(bits, i));
+                    if (bi) last[i] = count + __popc(ballot & ((1u << (31 - __clz(bi))) - 1u));
+                }
                 count += __popc(ballot);
             }
             if (lane == 0) {
                 s_unit[b] = u;
                 s_nkept[b] = count;
                 s_lkeff[b] = lk_eff;
+                s_last[2 * b] = last[0];
+                s_last[2 * b + 1] = last[1];
             }
             __syncwarp();
             mbar_arrive(&list_full[b]);  // every lane: releases its own list writes
@@ -341,8 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
         constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
         uint32_t it = 0;       // K/V ring position
-        uint32_t g = 0;        // (unit, tile) iterations: phase of p_half / p_full
-        uint32_t units = 0;    // units with at least one tile: phase of q_full / o_free
+        uint32_t units = 0;    // units with at least one tile: phase of q_full
         bool issued = false;
 
         auto next_stage = [&](int& s) -> bool {
@@ -379,24 +395,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) tc_commit(bar);
             __syncwarp();
         };
-        // wait for P_i of iteration g (both halves, or each half with the split hand-off), issue PV_i
-        auto pv = [&](int i, int s, bool acc) -> bool {
+        // wait for P_i of its needed tile number gi (both halves, or each half with the split hand-off), issue PV_i
+        auto pv = [&](int i, int s, bool acc, uint32_t gi) -> bool {
             if (kSplitP) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&p_half[i], g & 1, ctl, kErrTimeoutP))) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_half[i], gi & 1, ctl, kErrTimeoutP))) return false;
                 tc_fence_after();
                 issue_pv(i, s, acc, 0);
-                if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], g & 1, ctl, kErrTimeoutP))) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], gi & 1, ctl, kErrTimeoutP))) return false;
                 tc_fence_after();
                 issue_pv(i, s, acc, 1);
                 return true;
             }
-            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], g & 1, ctl, kErrTimeoutP))) return false;
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], gi & 1, ctl, kErrTimeoutP))) return false;
             tc_fence_after();
             issue_pv(i, s, acc, 0);
             issue_pv(i, s, acc, 1);
             return true;
         };
 
+        // Per K/V tile j of the unit's list, in this order:  PV0(j), S0(j+1), PV1(j), S1(j+1), each
+        // only for the Q tiles that need that K/V tile (the list holds tiles some Q tile needs).
+        // S_i(next) is always issued after PV_i(now), so P_i's TMEM is read before S_i overwrites it.
+        uint32_t gq0 = 0, gq1 = 0;   // needed tiles so far, per Q tile: phase of p_full[i]
+        uint32_t uq0 = 0, uq1 = 0;   // units in which Q tile i had work: phase of o_free[i]
         bool ok = true;
         for (int t = 0; ok; ++t) {
             const int b = t & 1;
@@ -404,53 +425,70 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int u = s_unit[b];
             if (u < 0) break;
             const int n_iter = s_nkept[b];
-            mbar_arrive(&list_empty[b]);
-            if (n_iter == 0) continue;
+            const int last0 = s_last[2 * b], last1 = s_last[2 * b + 1];
+            const uint32_t* list = lists + b * kMaxKvTiles;
+            if (n_iter == 0) {
+                mbar_arrive(&list_empty[b]);
+                continue;
+            }
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(q_full, units & 1, ctl, kErrTimeoutQ)))) break;
             int sK = 0, sV = 0;
             if (!(ok = next_stage(sK))) break;
             tc_fence_after();
-            issue_s(0, sK);
-            commit(&s_full[0]);
-            issue_s(1, sK);
-            commit(&s_full[1]);
+            uint32_t e_next = list[0];
+            if (need(e_next, 0)) {
+                issue_s(0, sK);
+                commit(&s_full[0]);
+            }
+            if (need(e_next, 1)) {
+                issue_s(1, sK);
+                commit(&s_full[1]);
+            }
             commit(&kv_empty[sK]);
             if (n_iter == 1) commit(q_empty);  // the unit's last S MMA is issued: Q may be replaced
             issued = true;
-            for (int j = 0; j < n_iter; ++j, ++g) {
+            bool first0 = true, first1 = true;
+            // PV_i for K/V tile j when Q tile i needs it; the first one of a unit overwrites O_i, so
+            // the previous unit's epilogue must have read O_i first (o_free)
+            auto pv_tile = [&](int i, int j, bool& first, uint32_t& gi, uint32_t ui, int last) -> bool {
+                if (first && ui > 0 &&
+                    !__all_sync(0xffffffffu, mbar_wait(&o_free[i], (ui - 1) & 1, ctl, kErrTimeoutO)))
+                    return false;
+                if (!pv(i, sV, !first, gi)) return false;
+                ++gi;
+                first = false;
+                if (j == last) commit(&o_full[i]);
+                return true;
+            };
+            for (int j = 0; j < n_iter; ++j) {
+                const uint32_t e = e_next;
                 const bool more = j + 1 < n_iter;
+                if (more) e_next = list[j + 1];
                 if (!(ok = next_stage(sV))) break;
-                KD_TRACE(1, 0, g);
-                // the first PV of a unit overwrites O_i: the previous unit's epilogue must have read it
-                if (j == 0 && units > 0 &&
-                    !(ok = __all_sync(0xffffffffu, mbar_wait(&o_free[0], (units - 1) & 1, ctl, kErrTimeoutO))))
-                    break;
-                if (!(ok = pv(0, sV, j > 0))) break;
-                KD_TRACE(1, 1, g);
-                if (!more) commit(&o_full[0]);
+                KD_TRACE(1, 0, gq0);
+                if (need(e, 0) && !(ok = pv_tile(0, j, first0, gq0, uq0, last0))) break;
                 int sK2 = 0;
                 if (more) {
                     if (!(ok = next_stage(sK2))) break;
-                    issue_s(0, sK2);
-                    KD_TRACE(1, 2, g);
-                    commit(&s_full[0]);
+                    if (need(e_next, 0)) {
+                        issue_s(0, sK2);
+                        commit(&s_full[0]);
+                    }
                 }
-                if (j == 0 && units > 0 &&
-                    !(ok = __all_sync(0xffffffffu, mbar_wait(&o_free[1], (units - 1) & 1, ctl, kErrTimeoutO))))
-                    break;
-                if (!(ok = pv(1, sV, j > 0))) break;
-                KD_TRACE(1, 3, g);
+                if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1))) break;
                 commit(&kv_empty[sV]);
-                if (!more) {
-                    commit(&o_full[1]);
-                } else {
-                    issue_s(1, sK2);
-                    KD_TRACE(1, 4, g);
-                    commit(&s_full[1]);
+                if (more) {
+                    if (need(e_next, 1)) {
+                        issue_s(1, sK2);
+                        commit(&s_full[1]);
+                    }
                     commit(&kv_empty[sK2]);
                     if (j + 2 == n_iter) commit(q_empty);
                 }
             }
+            mbar_arrive(&list_empty[b]);
+            if (!first0) ++uq0;
+            if (!first1) ++uq1;
             ++units;
         }
         if (issued) {
@@ -467,8 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tO = tmem + lane_addr + 256 + wg * 128;
         const int g4 = wg * 2 + (r >> 6);                // 64-row group of this row within the unit
         const float sl2 = p.scale_log2;
-        uint32_t g = 0;      // (unit, tile) iterations: phase of s_full
-        uint32_t units = 0;  // units with at least one tile: phase of o_full
+        uint32_t g = 0;      // tiles this Q tile needed so far: phase of s_full / p_full
+        uint32_t units = 0;  // units in which this Q tile had work: phase of o_full / o_free
         bool ok = true;
         for (int t = 0; ok; ++t) {
             const int b = t & 1;
@@ -481,14 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t* list = lists + b * kMaxKvTiles;
             const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
             const bool row_valid = qrow < p.Lq;
-            const uint16_t* mrow = nullptr;
-            if (p.mask && row_valid)
-                mrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const char*>(p.mask) +
-                                                         (long long)(n % p.mn) * p.m_nb3 +
-                                                         (long long)(h % p.mh) * p.m_nb2 + (long long)qrow * p.m_nb1);
             float m = -INFINITY, l = 0.f;
-            for (int j = 0; j < n_iter; ++j, ++g) {
+            int k = 0;  // tiles of this unit processed by this warpgroup
+            for (int j = 0; j < n_iter; ++j) {
                 const uint32_t e = list[j];
+                if (!need(e, wg)) continue;  // all four sub-tiles masked for this Q tile
                 const int kbase = (int)(e >> 16) * kBlockN;
                 const uint32_t c0 = (e >> (4 * g4)) & 3u, c1 = (e >> (4 * g4 + 2)) & 3u;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], g & 1, ctl, kErrTimeoutS)))) break;
@@ -499,6 +534,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // scale*s + m) into S in TMEM, 32 columns at a time.  c0/c1 are warp-uniform (a warp's
                 // 32 rows lie in one 64-row group).
                 if (c0 == kTileMixed || c1 == kTileMixed) {
+                    // this row's mask values (only mixed tiles read them, so the pointer is made here)
+                    const uint16_t* mrow = nullptr;
+                    if (p.mask && row_valid)
+                        mrow = reinterpret_cast<const uint16_t*>(
+                            reinterpret_cast<const char*>(p.mask) + (long long)(n % p.mn) * p.m_nb3 +
+                            (long long)(h % p.mh) * p.m_nb2 + (long long)qrow * p.m_nb1);
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         if ((c < 2 ? c0 : c1) != kTileMixed) continue;
@@ -589,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if ((warp & 3) == 0) KD_TRACE(2 + wg, 3, g);
                 // Rescale O_i (PV_i of the previous tile is complete: its commit preceded S_i's).  It only
                 // has to precede the first PV_i MMA of this tile; the first 64 scores are dead here.
-                if (warp_resc && j > 0) {
+                if (warp_resc && k > 0) {
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         uint32_t o[32];
@@ -611,6 +652,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 mbar_arrive(&p_full[wg]);
                 if ((warp & 3) == 0) KD_TRACE(2 + wg, 4, g);
+                ++g;
+                ++k;
             }
             if (!ok) break;
             mbar_arrive(&list_empty[b]);
@@ -620,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (row_valid)
                 orow = reinterpret_cast<TO*>(reinterpret_cast<char*>(p.out) + (long long)n * p.o_nb3 +
                                              (long long)qrow * p.o_nb2 + (long long)h * p.o_nb1);
-            if (n_iter > 0) {
+            if (k > 0) {
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&o_full[wg], units & 1, ctl, kErrTimeoutO)))) break;
                 tc_fence_after();
                 uint32_t ov[128];
@@ -661,7 +704,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T, typename TO>
 cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const FmhaParams& p,
                      cudaStream_t st) {
-    auto kern = fmha_fwd_kernel<T, TO>;
+    // a mask (tile classes) selects the instantiation that skips K/V tiles per Q tile
+    auto kern = p.tile_cls ? fmha_fwd_kernel<T, TO, true> : fmha_fwd_kernel<T, TO, false>;
     // set on every launch: the attribute belongs to the current device, and the call is cheap
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
     if (e != cudaSuccess) return e;
@@ -677,7 +721,7 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
 template <typename T, typename TO>
 int regs_t() {
     cudaFuncAttributes a{};
-    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO>) != cudaSuccess) return -1;
+    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false>) != cudaSuccess) return -1;
     return a.numRegs;
 }
 
