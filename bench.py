@@ -13,8 +13,9 @@ TFLOP/s = 4*B*H*L^2*d / step time.  With --gpus N > 1 the 32 heads are sharded
 over the ranks (8 heads x 4 GPUs, ...) and the step ends with kd_attn_allgather_heads
 (one NCCL all-gather + permute) -- strong scaling of the same job.
 
-e2e: the same call through the public API from pinned HOST buffers: H2D of the
-step's Q/K/V projections, the call, D2H of the bf16 output, per step.
+e2e: the same job through the public host-buffer call kd_attn_self_attention_host from
+pinned HOST buffers: each step uploads the f32 Q/K/V projections, computes and downloads
+the output, head group by head group with copies overlapping compute.
 
 --impl reference: the reference's CPU algorithm (the oracle restatement of ggml's
 flash_attn_ext with the RMSNorm/RoPE prologue; ggml itself is not available here)
@@ -88,7 +89,8 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while the timed region runs
+    (entering waits for the first sample, so sampling is live when timing starts)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -102,10 +104,14 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
@@ -492,17 +498,16 @@ def main():
     pro_ms = pr0.elapsed_time(pr1) / args.steps
     del qs, ks, vs
 
-    # end to end from pinned host buffers through the public API
+    # end to end from pinned host buffers through the public API: kd_attn_self_attention_host
+    # uploads, computes and downloads head group by head group, the copies of one group
+    # overlapping the compute of the next.  With N > 1 ranks each rank carries its own heads'
+    # columns from host memory to host memory (no device all-gather on this path).
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    hout = torch.empty(out_full.shape, dtype=out_dt).pin_memory()
+    hout = torch.empty(out_shard.shape, dtype=out_dt).pin_memory()
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
 
     def e2e_step():
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        step()
-        hout.copy_(out_full, non_blocking=True)
+        ctx.self_attention_host(hq, hk, hv, Hs, hout, rope=rope, op_type=op, stream=stream)
 
     e2e_step()
     barrier()
@@ -519,6 +524,8 @@ def main():
     e2e_ms = float(t.item())
     h2d = 3 * N * L * Cs * 4
     d2h = hout.numel() * hout.element_size()
+    if not torch.equal(hout[:, :64].to(dev), out_shard[:, :64]):
+        raise SystemExit("host-buffer path disagrees with the device-buffer path")
 
     pk, pk_sus, pk_kind = peaks()
     fa_flop = 4.0 * N * Hs * L * L * d
@@ -542,7 +549,8 @@ def main():
                      "traffic": traffic, "kernel": "fmha_fwd_kernel<bf16>", "kernel_ms": fa_ms},
         "prologue": {"ms": pro_ms, "gbs": (3 * N * L * Cs * 4 + 3 * N * L * Cs * 2) / (pro_ms * 1e-3) / 1e9},
         "e2e": {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "call": "kd_attn_self_attention_host (head-group pipelined H2D / compute / D2H)"},
         "gpu_launches": args.steps * (4 + (1 if ws > 1 else 0)),
         "clocks": clk.summary(),
     }

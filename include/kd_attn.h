@@ -198,6 +198,22 @@ kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, c
                                       const float* k_gain, float eps, const kd_rope3d* rope,
                                       int32_t op_type, kd_tensor* out, float* lse, void* stream);
 
+/* Self-attention on HOST buffers: the executor's upload -> graph compute ->
+ * download sequence (src/core/executor.hpp:235, :241, :253) for this one op,
+ * pipelined by head groups.  The heads are split into >= 4 equal groups; the
+ * host->device copy of group g+1 and the device->host copy of group g-1 run on
+ * two context-owned copy streams while group g computes on `stream`.  When
+ * `stream` has drained, `out` holds the result (the caller's stream waits on
+ * the last device->host copy).  Host buffers should be page-locked
+ * (cudaMallocHost / cudaHostRegister); pageable memory is correct but does not
+ * overlap.  Arguments as kd_attn_self_attention, with q_in/k_in/v_in/out in host
+ * memory (f32 inputs; out f32 or op_type), rows of each sequence evenly spaced
+ * or not, no lse.  Results are bit-identical to kd_attn_self_attention. */
+kd_attn_status kd_attn_self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                           const kd_tensor* v_in, int32_t n_head, const float* q_gain,
+                                           const float* k_gain, float eps, const kd_rope3d* rope,
+                                           int32_t op_type, kd_tensor* out, void* stream);
+
 kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
                                        const kd_tensor* v_in, int32_t n_head, const float* q_gain,
                                        const float* k_gain, float eps, const kd_tensor* mask,

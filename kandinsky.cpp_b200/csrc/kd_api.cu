@@ -4,6 +4,7 @@
 // the kernels do not cover is rejected with KD_ATTN_ERR_UNSUPPORTED.
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -28,6 +29,10 @@ struct kd_attn_ctx {
     int num_sms = 148;
     void* nccl_comm = nullptr;
     unsigned long long wait_ns = 2000000000ull;  // bound on a single device-side wait
+    // host-buffer pipeline (kd_attn_self_attention_host): copy streams and ordering events
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
+    cudaEvent_t ev_start = nullptr, ev_last = nullptr;
 };
 
 namespace {
@@ -502,6 +507,132 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     return flash_core(ctx, fa, st);
 }
 
+kd_attn_status ensure_copy_streams(kd_attn_ctx* ctx) {
+    if (ctx->h2d) return KD_ATTN_OK;
+    KD_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking));
+    KD_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+        KD_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_in[i], cudaEventDisableTiming));
+        KD_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_done[i], cudaEventDisableTiming));
+        KD_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_out[i], cudaEventDisableTiming));
+    }
+    KD_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_start, cudaEventDisableTiming));
+    KD_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_last, cudaEventDisableTiming));
+    return KD_ATTN_OK;
+}
+
+// Rows of a [C, L, N] host tensor restricted to columns [c0, c0 + width) <-> a packed device slab
+// [width, L, N]: one 2-D copy when the sequences are evenly spaced, else one per sequence.
+kd_attn_status copy_columns(kd_attn_ctx* ctx, const kd_tensor* host, size_t col_byte0, size_t width, void* dev,
+                            bool to_device, cudaStream_t st) {
+    const int64_t L = host->ne[1], N = host->ne[2];
+    char* hbase = static_cast<char*>(host->data) + col_byte0;
+    if (N == 1 || host->nb[2] == host->nb[1] * (size_t)L) {
+        if (to_device)
+            KD_CUDA(ctx, cudaMemcpy2DAsync(dev, width, hbase, host->nb[1], width, (size_t)(L * N), cudaMemcpyHostToDevice, st));
+        else
+            KD_CUDA(ctx, cudaMemcpy2DAsync(hbase, host->nb[1], dev, width, width, (size_t)(L * N), cudaMemcpyDeviceToHost, st));
+        return KD_ATTN_OK;
+    }
+    for (int64_t n = 0; n < N; ++n) {
+        char* h = hbase + n * host->nb[2];
+        char* d = static_cast<char*>(dev) + (size_t)n * L * width;
+        if (to_device)
+            KD_CUDA(ctx, cudaMemcpy2DAsync(d, width, h, host->nb[1], width, (size_t)L, cudaMemcpyHostToDevice, st));
+        else
+            KD_CUDA(ctx, cudaMemcpy2DAsync(h, host->nb[1], d, width, width, (size_t)L, cudaMemcpyDeviceToHost, st));
+    }
+    return KD_ATTN_OK;
+}
+
+kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                   const kd_tensor* v_in, int32_t n_head, const float* q_gain, const float* k_gain,
+                                   float eps, const kd_rope3d* rope, int32_t op_type, kd_tensor* out,
+                                   cudaStream_t st) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
+        (rc = check_tensor(ctx, v_in, "v_in")) || (rc = check_tensor(ctx, out, "out")))
+        return rc;
+    if (q_in->type != KD_ATTN_TYPE_F32 || k_in->type != KD_ATTN_TYPE_F32 || v_in->type != KD_ATTN_TYPE_F32)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "host inputs must be f32");
+    const int64_t C = q_in->ne[0], L = q_in->ne[1], N = q_in->ne[2];
+    for (const kd_tensor* t : {k_in, v_in})
+        if (t->ne[0] != C || t->ne[1] != L || t->ne[2] != N || t->ne[3] != 1)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
+    if (n_head <= 0 || C != (int64_t)n_head * kHeadDim || q_in->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "inputs must be [n_head*128, L, N]");
+    if (out->ne[0] != C || out->ne[1] != L || out->ne[2] != N || out->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [n_head*128, L, N]");
+    if (out->type != KD_ATTN_TYPE_F32 && out->type != op_type)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out must be f32 or the operand type");
+    if (L * N == 0) return KD_ATTN_OK;
+    // Group count: 4 to 16 groups of >= 64 MB of input each (only the last group's compute and
+    // copy-out are exposed behind the copy-in); heads per group = the largest divisor of n_head
+    // that gives at least that many groups.
+    const size_t in_total = 3 * (size_t)C * 4 * (size_t)(L * N);
+    const int want = (int)std::min<size_t>(16, std::max<size_t>(4, in_total / ((size_t)64 << 20)));
+    int G = 1;
+    for (int g = 1; g <= n_head; ++g)
+        if (n_head % g == 0 && n_head / g >= want) G = g;
+    const int groups = n_head / G;
+    const size_t in_w = (size_t)G * kHeadDim * 4;                  // bytes per row of one input slab
+    const size_t out_es = elt_size(out->type);
+    const size_t out_w = (size_t)G * kHeadDim * out_es;
+    const size_t in_slab = align256(in_w * (size_t)(L * N));
+    const size_t out_slab = align256(out_w * (size_t)(L * N));
+    const size_t opb = align256((size_t)N * G * L * kHeadDim * 2);  // one operand for one group
+    const size_t core = 3 * opb;                                     // attention_core's operand scratch
+    if ((rc = ensure_copy_streams(ctx))) return rc;
+    if ((rc = ensure_scratch(ctx, core + 2 * (3 * in_slab + out_slab)))) return rc;
+    char* stage = static_cast<char*>(ctx->scratch) + core;
+    auto in_buf = [&](int b, int x) { return stage + ((size_t)b * 3 + x) * in_slab; };
+    auto out_buf = [&](int b) { return stage + 6 * in_slab + (size_t)b * out_slab; };
+
+    // the copies must not start before work already queued on the caller's stream
+    KD_CUDA(ctx, cudaEventRecord(ctx->ev_start, st));
+    KD_CUDA(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_start, 0));
+    KD_CUDA(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_start, 0));
+    const kd_tensor* ins[3] = {q_in, k_in, v_in};
+    for (int g = 0; g < groups; ++g) {
+        const int b = g & 1;
+        // inputs of group g go into slab b once group g-2's compute has finished with it
+        if (g >= 2) KD_CUDA(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_done[b], 0));
+        for (int x = 0; x < 3; ++x)
+            if ((rc = copy_columns(ctx, ins[x], (size_t)g * in_w, in_w, in_buf(b, x), true, ctx->h2d))) return rc;
+        KD_CUDA(ctx, cudaEventRecord(ctx->ev_in[b], ctx->h2d));
+        // compute group g on the caller's stream; its output slab must have been copied out (group g-2)
+        KD_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ev_in[b], 0));
+        if (g >= 2) KD_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ev_out[b], 0));
+        kd_tensor xs[3], os;
+        for (int x = 0; x < 3; ++x) {
+            xs[x] = *ins[x];
+            xs[x].data = in_buf(b, x);
+            xs[x].ne[0] = (int64_t)G * kHeadDim;
+            xs[x].nb[1] = in_w;
+            xs[x].nb[2] = in_w * (size_t)L;
+            xs[x].nb[3] = xs[x].nb[2] * (size_t)N;
+        }
+        os = *out;
+        os.data = out_buf(b);
+        os.ne[0] = (int64_t)G * kHeadDim;
+        os.nb[1] = out_w;
+        os.nb[2] = out_w * (size_t)L;
+        os.nb[3] = os.nb[2] * (size_t)N;
+        if ((rc = attention_core(ctx, &xs[0], &xs[1], &xs[2], G, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
+                                 &os, nullptr, st)))
+            return rc;
+        KD_CUDA(ctx, cudaEventRecord(ctx->ev_done[b], st));
+        // copy group g's heads out into their columns of the host output
+        KD_CUDA(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_done[b], 0));
+        if ((rc = copy_columns(ctx, out, (size_t)g * out_w, out_w, out_buf(b), false, ctx->d2h))) return rc;
+        KD_CUDA(ctx, cudaEventRecord(ctx->ev_out[b], ctx->d2h));
+    }
+    // completion of the caller's stream covers the whole call (last copy-out included)
+    KD_CUDA(ctx, cudaEventRecord(ctx->ev_last, ctx->d2h));
+    KD_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ev_last, 0));
+    return KD_ATTN_OK;
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -586,6 +717,19 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
 void kd_attn_destroy(kd_attn_ctx* ctx) {
     if (!ctx) return;
     DeviceGuard g(ctx->device);
+    if (ctx->h2d) {
+        cudaStreamSynchronize(ctx->h2d);
+        cudaStreamSynchronize(ctx->d2h);
+        cudaStreamDestroy(ctx->h2d);
+        cudaStreamDestroy(ctx->d2h);
+        for (int i = 0; i < 2; ++i) {
+            cudaEventDestroy(ctx->ev_in[i]);
+            cudaEventDestroy(ctx->ev_done[i]);
+            cudaEventDestroy(ctx->ev_out[i]);
+        }
+        cudaEventDestroy(ctx->ev_start);
+        cudaEventDestroy(ctx->ev_last);
+    }
     if (ctx->nccl_comm) {
         if (Nccl* n = nccl()) n->commDestroy(ctx->nccl_comm);
     }
@@ -637,6 +781,16 @@ kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, c
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "self-attention needs Lq == Lk");
     return attention_core(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type, out, lse,
                           static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                           const kd_tensor* v_in, int32_t n_head, const float* q_gain,
+                                           const float* k_gain, float eps, const kd_rope3d* rope, int32_t op_type,
+                                           kd_tensor* out, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return self_attention_host(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, rope, op_type, out,
+                               static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,

@@ -39,7 +39,7 @@ EXPORTED = [
     "kd_attn_create", "kd_attn_destroy", "kd_attn_last_error", "kd_attn_device_status",
     "kd_attn_prologue", "kd_attn_flash_ext", "kd_attn_self_attention", "kd_attn_cross_attention",
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
-    "kd_attn_flash_ext_noalloc",
+    "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -128,6 +128,9 @@ def _load():
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
                                          ctypes.POINTER(Rope3D), ctypes.c_int32, T, P, P]
     L.kd_attn_self_attention.restype = st
+    L.kd_attn_self_attention_host.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
+                                              ctypes.POINTER(Rope3D), ctypes.c_int32, T, P]
+    L.kd_attn_self_attention_host.restype = st
     L.kd_attn_cross_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float, T, P,
                                           ctypes.c_int32, T, P, P]
     L.kd_attn_cross_attention.restype = st
@@ -247,6 +250,19 @@ class Context:
                                               _ptr(q_gain), _ptr(k_gain), float(eps),
                                               None if rope is None else ctypes.byref(rope), int(op_type), _ref(out),
                                               _ptr(lse), _stream_ptr(stream)))
+        return out
+
+    def self_attention_host(self, q_in, k_in, v_in, n_head, out, rope=None, q_gain=None, k_gain=None, eps=1e-6,
+                            op_type=BF16, stream=None):
+        """Host tensors q_in/k_in/v_in: (N, L, C) f32 (pinned for overlap) -> host out (N, L, C) f32/bf16;
+        uploads, computes and downloads head group by head group.  Done when `stream` has drained."""
+        for name, t in (("q_in", q_in), ("k_in", k_in), ("v_in", v_in), ("out", out)):
+            if t.is_cuda:
+                raise ValueError(f"{name} must be a host tensor")
+        self.check(lib.kd_attn_self_attention_host(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), int(n_head),
+                                                   _ptr(q_gain), _ptr(k_gain), float(eps),
+                                                   None if rope is None else ctypes.byref(rope), int(op_type),
+                                                   _ref(out), _stream_ptr(stream)))
         return out
 
     def cross_attention(self, q_in, k_in, v_in, n_head, out, mask=None, kv_len=None, q_gain=None, k_gain=None,

@@ -232,3 +232,34 @@ def test_rejects_unsupported_and_invalid(ctx, kd):
         ctx.flash_attn_ext(q, q, q, torch.empty(1, 16, 2, 128, device="cuda"), max_bias=1.0)
     assert e.value.status == kd.ERR_UNSUPPORTED
     ctx.device_status()
+
+
+# ------------------------------------------------------------------ host-buffer pipelined entry point
+@pytest.mark.parametrize("H,grid,N,out_dtype,pinned,gap", [
+    (32, (5, 16, 16), 1, torch.float32, True, 0),     # config 0 shape: 4 groups of 8 heads
+    (6, (2, 8, 12), 2, torch.bfloat16, True, 0),      # 6 groups of 1 head, two sequences
+    (3, (1, 9, 13), 2, torch.float32, False, 5),      # fewer heads than 4 groups, pageable, sequence gaps
+])
+def test_self_attention_host_matches_device_path(ctx, kd, H, grid, N, out_dtype, pinned, gap):
+    """kd_attn_self_attention_host (upload / compute / download by head group) must equal the
+    device-buffer call on the same projections bit for bit, whatever the host layout."""
+    L, C = grid[0] * grid[1] * grid[2], H * 128
+    rope = kd.Rope3D.make(grid, scale=(1, 2, 2))
+    ins = []
+    for off in range(3):
+        x = torch.from_numpy(seeded((N, L + gap, C), 99, off))
+        ins.append((x.pin_memory() if pinned else x)[:, :L])   # gap rows between sequences
+    ref = torch.empty(N, L, C, device="cuda", dtype=out_dtype)
+    ctx.self_attention(*[x.cuda() for x in ins], H, ref, rope=rope, op_type=kd.BF16)
+    out = torch.full((N, L + gap, C), float("nan"), dtype=out_dtype)
+    out = (out.pin_memory() if pinned else out)[:, :L]
+    s = torch.cuda.Stream()
+    ctx.self_attention_host(*ins, H, out, rope=rope, op_type=kd.BF16, stream=s)
+    s.synchronize()
+    ctx.device_status()
+    assert torch.equal(out, ref.cpu())
+    # a second call reuses the context's copy streams and staging
+    out2 = torch.zeros_like(out)
+    ctx.self_attention_host(*ins, H, out2, rope=rope, op_type=kd.BF16, stream=s)
+    s.synchronize()
+    assert torch.equal(out2, ref.cpu())
