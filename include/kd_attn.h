@@ -110,12 +110,25 @@ kd_attn_status kd_attn_nccl_unique_id(void* out128);
 kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out);
 void kd_attn_destroy(kd_attn_ctx* ctx);
 
+/* Process-wide log callback (kandinsky.h:19 kd_log_cb_t shape): used by contexts
+ * created with log_cb = NULL and by kd_attn_flash_ext_noalloc; NULL restores
+ * the default (WARN and above to stderr).  Thread-safe. */
+void kd_attn_set_log_callback(kd_attn_log_cb cb, void* user_data);
+
 /* Text of the last error raised on this context ("" when none). */
 const char* kd_attn_last_error(const kd_attn_ctx* ctx);
 
 /* Synchronises `stream`, then reads and clears the device error word that the
  * kernels' bounded waits set; KD_ATTN_ERR_DEVICE_TIMEOUT if any wait expired. */
 kd_attn_status kd_attn_device_status(kd_attn_ctx* ctx, void* stream);
+
+/* Device counters of the flash kernel, accumulated over every launch on this
+ * context since the last reset: out[0] = K/V tiles (128 keys) loaded, out[1] =
+ * (Q tile of 128 rows) x (K/V tile) products computed.  Fully masked tiles are
+ * neither loaded nor computed, so with a block-sparse mask these equal the
+ * counts of kept tiles that the mask implies.  Synchronises `stream`; reset != 0
+ * zeroes the counters after reading.  No reference counterpart. */
+kd_attn_status kd_attn_tile_stats(kd_attn_ctx* ctx, void* stream, uint64_t out[2], int32_t reset);
 
 /* ---------------------------------------------------------------------------
  * Prologue: RMSNorm per head + 3D RoPE + cast + permute, one HBM pass.
@@ -133,6 +146,18 @@ kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_
                                 const float* gain, float eps, const kd_rope3d* rope, kd_tensor* y,
                                 void* stream);
 
+/* The prologue of one attention call in ONE launch: Q and K RMS-normalised
+ * (q_gain / k_gain, NULL = unit gain) and, when `rope` is given, rotated; V only
+ * permuted and cast (crossdit.hpp:132-141 for self-attention, :188-193 for
+ * cross-attention, + ops.hpp:122-131,167-169).  Tensors of equal length are
+ * processed row by row together (one sin/cos per token).  Any of the three
+ * pairs may be NULL.  n_head comes from the outputs' ne[2]; all outputs have
+ * type `out_dtype` (f16, bf16 or f32). */
+kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                   const kd_tensor* v_in, const float* q_gain, const float* k_gain, float eps,
+                                   const kd_rope3d* rope, int32_t out_dtype, kd_tensor* q_out,
+                                   kd_tensor* k_out, kd_tensor* v_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * ggml_flash_attn_ext semantics (called at ops.hpp:176):
  *   out[:, h, i, n] = softmax_j(scale * q[:, i, h, n] . k[:, j, hk, nk] + mask[j, i, h%mh, n%mn]) v[:, j, hk, nk]
@@ -144,6 +169,14 @@ kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_
  *        H % mh == 0, N % mn == 0.  Tiles that are entirely -inf are skipped.
  * kv_len: NULL or device int32 [N]: keys j >= kv_len[n] are masked (the
  *        variable text length of cross-attention without a dense mask).
+ * tile_mask: NULL or a device bitmap of 64 x 64 (query x key) tiles shared by
+ *        every head and sequence: tile (qb, kb) is bit (kb % 8) of byte
+ *        tile_mask[qb * ceil(Lk/64 / 8) + kb / 8], qb < ceil(Lq/64),
+ *        kb < ceil(Lk/64).  A clear bit means every pair in the tile is masked:
+ *        the tile is skipped and its mask elements are never read.  Without a
+ *        dense mask a set bit means the whole tile is kept (a block-sparse mask
+ *        in 1/8192 of the dense mask's bytes); with one, set tiles take their
+ *        values from the mask.  No ggml counterpart.
  * out  : [D, H, Lq, N] f32 | bf16 | f16 (ggml's dst permutation; with
  *        contiguous strides this is [H*D, Lq, N], the ops::attention result)
  * lse  : NULL or device f32 [N, H, Lq], natural-log softmax denominator
@@ -153,7 +186,7 @@ kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k,
                                  const kd_tensor* v, const kd_tensor* mask, float scale,
                                  float max_bias, float logit_softcap, const int32_t* kv_len,
-                                 kd_tensor* out, float* lse, void* stream);
+                                 const uint8_t* tile_mask, kd_tensor* out, float* lse, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Allocation-free variant of kd_attn_flash_ext.  It has no counterpart in the
@@ -180,8 +213,9 @@ kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_
 #define KD_ATTN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
                                          const kd_tensor* mask, float scale, float max_bias,
-                                         float logit_softcap, const int32_t* kv_len, kd_tensor* out,
-                                         float* lse, void* stream);
+                                         float logit_softcap, const int32_t* kv_len,
+                                         const uint8_t* tile_mask, kd_tensor* out, float* lse,
+                                         void* stream);
 
 /* ---------------------------------------------------------------------------
  * The two CrossDiT call sites end to end (prologue + flash), operands staged

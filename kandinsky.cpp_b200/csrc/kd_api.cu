@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/kd_attn.h"
@@ -23,7 +24,8 @@ struct kd_attn_ctx {
     kd_attn_log_cb log_cb = nullptr;
     void* log_user = nullptr;
     std::string last_error;
-    unsigned* d_words = nullptr;  // [0] sticky error bits, [1] per-launch abort flag, [2] work counter
+    unsigned* d_words = nullptr;  // [0] sticky error bits, [1] per-launch abort flag, [2] work counter,
+                                  // [4..7] two u64 tile counters (K/V tiles loaded, tile products computed)
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     int num_sms = 148;
@@ -38,6 +40,12 @@ struct kd_attn_ctx {
 namespace {
 
 // ------------------------------------------------------------------ errors / logging
+// Process-wide callback (kd_attn_set_log_callback) for contexts created without one and for
+// calls that have no context.
+std::mutex g_log_mu;
+kd_attn_log_cb g_log_cb = nullptr;
+void* g_log_user = nullptr;
+
 void log_msg(kd_attn_ctx* ctx, kd_attn_log_level lvl, const char* fmt, ...) {
     char buf[1024];
     va_list ap;
@@ -46,9 +54,19 @@ void log_msg(kd_attn_ctx* ctx, kd_attn_log_level lvl, const char* fmt, ...) {
     va_end(ap);
     if (ctx && ctx->log_cb) {
         ctx->log_cb(lvl, buf, ctx->log_user);
-    } else if (lvl >= KD_ATTN_LOG_WARN) {
-        fprintf(stderr, "[kd_attn] %s\n", buf);
+        return;
     }
+    kd_attn_log_cb cb;
+    void* user;
+    {
+        std::lock_guard<std::mutex> lock(g_log_mu);
+        cb = g_log_cb;
+        user = g_log_user;
+    }
+    if (cb)
+        cb(lvl, buf, user);
+    else if (lvl >= KD_ATTN_LOG_WARN)
+        fprintf(stderr, "[kd_attn] %s\n", buf);
 }
 
 kd_attn_status fail(kd_attn_ctx* ctx, kd_attn_status st, const char* fmt, ...) {
@@ -221,9 +239,70 @@ struct FlashArgs {
     const int32_t* kv_len;
     kd_tensor* out;
     float* lse;
+    const uint8_t* tile_mask;  // bit-packed 64x64 tile bitmap or null
 };
 
-kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) {
+// ------------------------------------------------------------------ allocation-free scratch
+// kd_attn_flash_ext_noalloc: the flash_attn_ext sequence (Q rounding, mask tile
+// classes, tcgen05 kernel) with every piece of scratch taken from statically
+// sized device arrays defined in this file, for callers that cannot allocate.
+constexpr size_t kNoAllocScratchBytes = KD_ATTN_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+
+// One copy per device, created when the module loads and kept until the process exits.
+// Host code must not use these names as addresses: it asks cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) unsigned g_noalloc_words[4];  // [0] sticky error bits, [1] abort flag, [2] work counter
+
+struct NoAllocDevice {
+    bool ready = false;
+    char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+    unsigned* words = nullptr; // device address of g_noalloc_words on this device
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// Once per device, with that device current: resolve the arrays' device addresses.
+kd_attn_status noalloc_setup(NoAllocDevice** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "device %d attributes unavailable", dev);
+        if (major != 10 || minor != 0)
+            return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device %d is sm_%d%d; built for sm_100a only", dev, major,
+                        minor);
+        void* s = nullptr;
+        void* w = nullptr;
+        e = cudaGetSymbolAddress(&s, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+        e = cudaGetSymbolAddress(&w, g_noalloc_words);
+        if (e != cudaSuccess)
+            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(words) failed: %s", cudaGetErrorString(e));
+        d.scratch = static_cast<char*>(s);
+        d.words = static_cast<unsigned*>(w);
+        d.num_sms = sms;
+        d.ready = true;
+    }
+    *out = &d;
+    return KD_ATTN_OK;
+}
+
+// The flash_attn_ext sequence: argument checks, Q rounding to the operand type when needed, tile
+// classes from the mask and/or the tile bitmap, tensor maps, the tcgen05 kernel.  With a context
+// the scratch and device words are the context's; without one (`ctx` null, the allocation-free
+// entry point) they are the static arrays above and messages go to stderr.
+kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, a.q, "q")) || (rc = check_tensor(ctx, a.k, "k")) ||
         (rc = check_tensor(ctx, a.v, "v")) || (rc = check_tensor(ctx, a.out, "out")))
@@ -248,25 +327,25 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
     if (Lk > (int64_t)kMaxKvTiles * kBlockN)
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "Lk %lld exceeds %d", (long long)Lk, kMaxKvTiles * kBlockN);
     if (H > 65535 || N > 65535) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than 65535 heads or sequences");
-    uint64_t onb[4];
+    uint64_t onb[4], knb[4], vnb[4], qnb[4];
     packed_strides(&o, onb);
-    if (!strides16(onb) || !aligned16(o.data))
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned");
-    if (Lq == 0 || H == 0 || N == 0) return KD_ATTN_OK;
-
-    const bool bf16 = k.type == KD_ATTN_TYPE_BF16;
-    uint64_t knb[4], vnb[4], qnb[4];
     packed_strides(&k, knb);
     packed_strides(&v, vnb);
     packed_strides(&q, qnb);
+    if (!strides16(onb) || !aligned16(o.data))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned");
     if (Lk > 0 && (!strides16(knb) || !strides16(vnb)))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k/v strides must be multiples of 16 bytes");
+    if (Lq == 0 || H == 0 || N == 0) return KD_ATTN_OK;
+    const bool bf16 = k.type == KD_ATTN_TYPE_BF16;
 
-    // scratch: Q rounded to the operand type (when needed) + mask tile classes
+    // scratch plan: [Q rounded to the operand type][tile classes]
     const bool q_direct = q.type == k.type && strides16(qnb) && aligned16(q.data);
     const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * kHeadDim * 2);
-    int n_qb = 0, n_kb = 0, mh = 1, mn = 1;
-    size_t cls_bytes = 0;
+    const bool tiled = a.mask || a.tile_mask;
+    const int n_qb = tiled ? (int)((Lq + 63) / 64) : 0, n_kb = tiled ? (int)((Lk + 63) / 64) : 0;
+    int mh = 1, mn = 1;
+    uint64_t mnb[4] = {0, 0, 0, 0};
     if (a.mask) {
         if ((rc = check_tensor(ctx, a.mask, "mask"))) return rc;
         const kd_tensor& m = *a.mask;
@@ -278,12 +357,35 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
             return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "mask planes must divide heads and sequences");
         mh = (int)m.ne[2];
         mn = (int)m.ne[3];
-        n_qb = (int)((Lq + 63) / 64);
-        n_kb = (int)((Lk + 63) / 64);
-        cls_bytes = align256((size_t)mh * mn * n_qb * n_kb);
+        packed_strides(a.mask, mnb);
     }
-    if ((rc = ensure_scratch(ctx, q_bytes + cls_bytes))) return rc;
-    char* scr = static_cast<char*>(ctx->scratch);
+    const size_t cls_bytes = tiled ? align256((size_t)mh * mn * n_qb * n_kb) : 0;
+
+    char* scr = nullptr;
+    unsigned* words = nullptr;
+    unsigned long long* stats = nullptr;
+    int num_sms = 0;
+    unsigned long long wait_ns = 2000000000ull;
+    if (ctx) {
+        if ((rc = ensure_scratch(ctx, q_bytes + cls_bytes))) return rc;
+        scr = static_cast<char*>(ctx->scratch);
+        words = ctx->d_words;
+        stats = reinterpret_cast<unsigned long long*>(ctx->d_words + 4);
+        num_sms = ctx->num_sms;
+        wait_ns = ctx->wait_ns;
+    } else {
+        if (q_bytes + cls_bytes > kNoAllocScratchBytes)
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED,
+                        "kd_attn_flash_ext_noalloc needs %zu bytes of scratch but holds %zu "
+                        "(KD_ATTN_NOALLOC_SCRATCH_BYTES); pass Q in K's type with 16-byte-aligned rows, or use "
+                        "kd_attn_flash_ext",
+                        q_bytes + cls_bytes, kNoAllocScratchBytes);
+        NoAllocDevice* d = nullptr;
+        if ((rc = noalloc_setup(&d))) return rc;
+        scr = d->scratch;
+        words = d->words;
+        num_sms = d->num_sms;
+    }
 
     const void* qdata = q.data;
     if (!q_direct) {
@@ -297,19 +399,19 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
         cp.L = (int)Lq;
         cp.H = (int)H;
         cp.N = (int)N;
-        KD_CUDA(ctx, launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, ctx->num_sms, st));
+        KD_CUDA(ctx, launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, num_sms, st));
         qdata = scr;
         qnb[1] = kHeadDim * 2;
         qnb[2] = qnb[1] * Lq;
         qnb[3] = qnb[2] * H;
     }
     uint8_t* cls = nullptr;
-    if (a.mask) {
+    if (tiled) {
         cls = reinterpret_cast<uint8_t*>(scr + q_bytes);
-        uint64_t mnb[4];
-        packed_strides(a.mask, mnb);
         MaskClassParams mp{};
-        mp.mask = static_cast<const uint16_t*>(a.mask->data);
+        mp.mask = a.mask ? static_cast<const uint16_t*>(a.mask->data) : nullptr;
+        mp.bits = a.tile_mask;
+        mp.bits_row_bytes = (n_kb + 7) / 8;
         mp.nb1 = (long long)mnb[1];
         mp.nb2 = (long long)mnb[2];
         mp.nb3 = (long long)mnb[3];
@@ -320,7 +422,7 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
         mp.cls = cls;
         mp.n_qb = n_qb;
         mp.n_kb = n_kb;
-        KD_CUDA(ctx, launch_mask_classify(mp, st));
+        KD_CUDA(ctx, launch_mask_classify(mp, st));  // writes every class byte
     }
 
     CUtensorMap tmQ, tmK, tmV;
@@ -351,8 +453,6 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
     p.n_qb = n_qb;
     p.n_kb = n_kb;
     if (a.mask) {
-        uint64_t mnb[4];
-        packed_strides(a.mask, mnb);
         p.mask = static_cast<const uint16_t*>(a.mask->data);
         p.m_nb1 = (long long)mnb[1];
         p.m_nb2 = (long long)mnb[2];
@@ -361,13 +461,14 @@ kd_attn_status flash_core(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st)
     p.mh = mh;
     p.mn = mn;
     p.kv_len = a.kv_len;
-    p.err = ctx->d_words;
-    p.abort_flag = ctx->d_words + 1;
-    p.work_counter = ctx->d_words + 2;
-    p.num_ctas = ctx->num_sms;
-    p.wait_ns = ctx->wait_ns;
+    p.err = words;
+    p.abort_flag = words + 1;
+    p.work_counter = words + 2;
+    p.num_ctas = num_sms;
+    p.wait_ns = wait_ns;
+    p.tile_stats = stats;
     // abort flag and work counter start at zero for every launch
-    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, 2 * sizeof(unsigned), st));
+    KD_CUDA(ctx, cudaMemsetAsync(words + 1, 0, 2 * sizeof(unsigned), st));
     KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
     return KD_ATTN_OK;
 }
@@ -398,8 +499,9 @@ kd_attn_status fill_rope(kd_attn_ctx* ctx, const kd_rope3d* rope, int64_t L, Rop
     return KD_ATTN_OK;
 }
 
-kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm, const float* gain,
-                             float eps, const kd_rope3d* rope, kd_tensor* y, cudaStream_t st) {
+// Checks one prologue tensor pair and fills its kernel description.
+kd_attn_status prep_prologue_tensor(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm,
+                                    const float* gain, bool rope, const kd_tensor* y, PrologueJob* t) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, x, "x")) || (rc = check_tensor(ctx, y, "y"))) return rc;
     if (x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "prologue input must be f32");
@@ -409,6 +511,7 @@ kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_hea
     const int64_t L = x->ne[1], N = x->ne[2];
     if (y->ne[0] != kHeadDim || y->ne[1] != L || y->ne[2] != n_head || y->ne[3] != N)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "y must be [128, L, n_head, N]");
+    if (L > INT32_MAX || N > INT32_MAX) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "L or N beyond 2^31");
     uint64_t xnb[4], ynb[4];
     packed_strides(x, xnb);
     packed_strides(y, ynb);
@@ -418,26 +521,66 @@ kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_hea
     if ((reinterpret_cast<uintptr_t>(y->data) % (4 * ye)) || ynb[1] % (4 * ye) || ynb[2] % (4 * ye) ||
         ynb[3] % (4 * ye))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "y rows must be aligned to 4 elements");
-    if (gain && !aligned16(gain)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "gain must be 16-byte aligned");
-    if (L * N == 0) return KD_ATTN_OK;
-    PrologueParams p{};
-    p.x = static_cast<const float*>(x->data);
-    p.x_nb1 = (long long)xnb[1];
-    p.x_nb2 = (long long)xnb[2];
-    p.y = y->data;
-    p.y_nb1 = (long long)ynb[1];
-    p.y_nb2 = (long long)ynb[2];
-    p.y_nb3 = (long long)ynb[3];
-    p.L = (int)L;
-    p.N = (int)N;
-    p.H = n_head;
-    p.norm = norm ? 1 : 0;
-    p.gain = gain;
-    p.eps = eps;
-    p.rope = rope ? 1 : 0;
-    if (rope && (rc = fill_rope(ctx, rope, L, &p.tab))) return rc;
-    KD_CUDA(ctx, launch_prologue(out_type_of(y->type), p, ctx->num_sms, st));
+    if (norm && gain && !aligned16(gain)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "gain must be 16-byte aligned");
+    *t = PrologueJob{};
+    t->x = static_cast<const float*>(x->data);
+    t->x_nb1 = (long long)xnb[1];
+    t->x_nb2 = (long long)xnb[2];
+    t->y = y->data;
+    t->y_nb1 = (long long)ynb[1];
+    t->y_nb2 = (long long)ynb[2];
+    t->y_nb3 = (long long)ynb[3];
+    t->norm = norm ? 1 : 0;
+    t->gain = norm ? gain : nullptr;
+    t->rope = rope ? 1 : 0;
+    t->L = (int)L;
+    t->N = (int)N;
+    t->H = n_head;
     return KD_ATTN_OK;
+}
+
+// One prologue launch over up to three projections (blockIdx.y = projection).  A RoPE grid must
+// cover the L of every projection it rotates.
+struct PrologueReq {
+    const kd_tensor* x;
+    int32_t norm;
+    const float* gain;
+    bool rope;
+    const kd_tensor* y;
+};
+
+kd_attn_status prologue_multi(kd_attn_ctx* ctx, const PrologueReq* req, int count, int32_t n_head, float eps,
+                              const kd_rope3d* rope, cudaStream_t st) {
+    kd_attn_status rc;
+    PrologueParams p{};
+    p.eps = eps;
+    int32_t ytype = -1;
+    int64_t rope_L = -1;
+    for (int i = 0; i < count; ++i) {
+        PrologueJob t;
+        const bool r = rope && req[i].rope;
+        if ((rc = prep_prologue_tensor(ctx, req[i].x, n_head, req[i].norm, req[i].gain, r, req[i].y, &t))) return rc;
+        if (ytype >= 0 && req[i].y->type != ytype)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "prologue outputs must share one type");
+        ytype = req[i].y->type;
+        if (r) {
+            if (rope_L >= 0 && rope_L != t.L)
+                return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "RoPE applied to tensors of different lengths");
+            if (rope_L < 0 && (rc = fill_rope(ctx, rope, t.L, &p.tab))) return rc;
+            rope_L = t.L;
+        }
+        if ((int64_t)t.L * t.N == 0) continue;
+        p.job[p.njobs++] = t;
+    }
+    if (p.njobs == 0) return KD_ATTN_OK;
+    KD_CUDA(ctx, launch_prologue(out_type_of(ytype), p, ctx->num_sms, st));
+    return KD_ATTN_OK;
+}
+
+kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm, const float* gain,
+                             float eps, const kd_rope3d* rope, kd_tensor* y, cudaStream_t st) {
+    const PrologueReq r{x, norm, gain, rope != nullptr, y};
+    return prologue_multi(ctx, &r, 1, n_head, eps, rope, st);
 }
 
 kd_tensor operand_view(void* data, int32_t type, int64_t L, int64_t H, int64_t N) {
@@ -500,11 +643,10 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N);
     kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_head, N);
     kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_head, N);
-    if ((rc = prologue_core(ctx, q_in, n_head, 1, q_gain, eps, rope, &Qs, st))) return rc;
-    if ((rc = prologue_core(ctx, k_in, n_head, 1, k_gain, eps, rope, &Ks, st))) return rc;
-    if ((rc = prologue_core(ctx, v_in, n_head, 0, nullptr, eps, nullptr, &Vs, st))) return rc;
+    const PrologueReq req[3] = {{q_in, 1, q_gain, true, &Qs}, {k_in, 1, k_gain, true, &Ks}, {v_in, 0, nullptr, false, &Vs}};
+    if ((rc = prologue_multi(ctx, req, 3, n_head, eps, rope, st))) return rc;
     FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, lse};
-    return flash_core(ctx, fa, st);
+    return flash_run(ctx, fa, st);
 }
 
 kd_attn_status ensure_copy_streams(kd_attn_ctx* ctx) {
@@ -686,8 +828,8 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
         return KD_ATTN_ERR_UNSUPPORTED;
     }
     ctx->num_sms = prop.multiProcessorCount;
-    if (cudaMalloc(&ctx->d_words, 4 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(ctx->d_words, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
+    if (cudaMalloc(&ctx->d_words, 8 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->d_words, 0, 8 * sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
         return KD_ATTN_ERR_OUT_OF_MEMORY;
@@ -753,6 +895,24 @@ kd_attn_status kd_attn_device_status(kd_attn_ctx* ctx, void* stream) {
     return KD_ATTN_OK;
 }
 
+void kd_attn_set_log_callback(kd_attn_log_cb cb, void* user_data) {
+    std::lock_guard<std::mutex> lock(g_log_mu);
+    g_log_cb = cb;
+    g_log_user = user_data;
+}
+
+kd_attn_status kd_attn_tile_stats(kd_attn_ctx* ctx, void* stream, uint64_t out[2], int32_t reset) {
+    if (!ctx || !out) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    KD_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    unsigned long long v[2] = {0, 0};
+    KD_CUDA(ctx, cudaMemcpy(v, ctx->d_words + 4, sizeof v, cudaMemcpyDeviceToHost));
+    out[0] = v[0];
+    out[1] = v[1];
+    if (reset) KD_CUDA(ctx, cudaMemset(ctx->d_words + 4, 0, sizeof v));
+    return KD_ATTN_OK;
+}
+
 kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm, const float* gain,
                                 float eps, const kd_rope3d* rope, kd_tensor* y, void* stream) {
     if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
@@ -760,15 +920,44 @@ kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_
     return prologue_core(ctx, x, n_head, norm, gain, eps, rope, y, static_cast<cudaStream_t>(stream));
 }
 
+kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                   const kd_tensor* v_in, const float* q_gain, const float* k_gain, float eps,
+                                   const kd_rope3d* rope, int32_t out_dtype, kd_tensor* q_out, kd_tensor* k_out,
+                                   kd_tensor* v_out, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    const kd_tensor* ins[3] = {q_in, k_in, v_in};
+    kd_tensor* outs[3] = {q_out, k_out, v_out};
+    PrologueReq req[3];
+    int count = 0;
+    int64_t n_head = -1;
+    for (int i = 0; i < 3; ++i) {
+        if (!ins[i] && !outs[i]) continue;
+        if (!ins[i] || !outs[i]) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "input and output must both be given");
+        if (outs[i]->type != out_dtype)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must have type out_dtype");
+        if (n_head >= 0 && outs[i]->ne[2] != n_head)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs disagree on the head count");
+        n_head = outs[i]->ne[2];
+        req[count++] = PrologueReq{ins[i], i < 2 ? 1 : 0, i == 0 ? q_gain : (i == 1 ? k_gain : nullptr), i < 2, outs[i]};
+    }
+    if (count == 0) return KD_ATTN_OK;
+    if (out_dtype != KD_ATTN_TYPE_F32 && out_dtype != KD_ATTN_TYPE_F16 && out_dtype != KD_ATTN_TYPE_BF16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_dtype must be f32, f16 or bf16");
+    if (n_head <= 0 || n_head > (1 << 20)) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "bad head count");
+    return prologue_multi(ctx, req, count, (int32_t)n_head, eps, rope, static_cast<cudaStream_t>(stream));
+}
+
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
                                  const kd_tensor* mask, float scale, float max_bias, float logit_softcap,
-                                 const int32_t* kv_len, kd_tensor* out, float* lse, void* stream) {
+                                 const int32_t* kv_len, const uint8_t* tile_mask, kd_tensor* out, float* lse,
+                                 void* stream) {
     if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
     if (max_bias != 0.f) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "max_bias (ALiBi) must be 0");
     if (logit_softcap != 0.f) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "logit_softcap must be 0");
     DeviceGuard g(ctx->device);
-    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse};
-    return flash_core(ctx, fa, static_cast<cudaStream_t>(stream));
+    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse, tile_mask};
+    return flash_run(ctx, fa, static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
@@ -849,223 +1038,13 @@ kd_attn_status kd_attn_fill_randn(kd_attn_ctx* ctx, float* dst, uint64_t n, uint
 }  // extern "C"
 
 // ====================================================================== allocation-free flash entry
-// kd_attn_flash_ext_noalloc: the flash_attn_ext sequence (Q rounding, mask tile
-// classes, tcgen05 kernel) with every piece of scratch taken from statically
-// sized device arrays defined in this file, for callers that cannot allocate.
-#include <mutex>
-
-namespace {
-
-constexpr size_t kNoAllocScratchBytes = KD_ATTN_NOALLOC_SCRATCH_BYTES;
-constexpr int kNoAllocMaxDevices = 64;
-
-// One copy per device, created when the module loads and kept until the process exits.
-// Host code must not use these names as addresses: it asks cudaGetSymbolAddress.
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static __device__ __align__(256) unsigned g_noalloc_words[4];  // [0] sticky error bits, [1] abort flag, [2] work counter
-
-struct NoAllocDevice {
-    bool ready = false;
-    char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
-    unsigned* words = nullptr; // device address of g_noalloc_words on this device
-    int num_sms = 0;
-};
-std::mutex g_noalloc_mu;
-NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
-
-// Once per device, with that device current: resolve the arrays' device addresses.
-kd_attn_status noalloc_setup(NoAllocDevice** out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= kNoAllocMaxDevices)
-        return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    NoAllocDevice& d = g_noalloc_dev[dev];
-    if (!d.ready) {
-        int major = 0, minor = 0, sms = 0;
-        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            return fail(nullptr, KD_ATTN_ERR_CUDA, "device %d attributes unavailable", dev);
-        if (major != 10 || minor != 0)
-            return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device %d is sm_%d%d; built for sm_100a only", dev, major,
-                        minor);
-        void* s = nullptr;
-        void* w = nullptr;
-        e = cudaGetSymbolAddress(&s, g_noalloc_scratch);
-        if (e != cudaSuccess)
-            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
-        e = cudaGetSymbolAddress(&w, g_noalloc_words);
-        if (e != cudaSuccess)
-            return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetSymbolAddress(words) failed: %s", cudaGetErrorString(e));
-        d.scratch = static_cast<char*>(s);
-        d.words = static_cast<unsigned*>(w);
-        d.num_sms = sms;
-        d.ready = true;
-    }
-    *out = &d;
-    return KD_ATTN_OK;
-}
-
-kd_attn_status flash_noalloc(const FlashArgs& a, cudaStream_t st) {
-    kd_attn_ctx* const nc = nullptr;  // no context: messages go to stderr
-    kd_attn_status rc;
-    if ((rc = check_tensor(nc, a.q, "q")) || (rc = check_tensor(nc, a.k, "k")) || (rc = check_tensor(nc, a.v, "v")) ||
-        (rc = check_tensor(nc, a.out, "out")))
-        return rc;
-    const kd_tensor &q = *a.q, &k = *a.k, &v = *a.v, &o = *a.out;
-    if (q.ne[0] != kHeadDim || k.ne[0] != kHeadDim || v.ne[0] != kHeadDim)
-        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128");
-    if (k.type != v.type || (k.type != KD_ATTN_TYPE_F16 && k.type != KD_ATTN_TYPE_BF16))
-        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "k and v must share type f16 or bf16");
-    const int64_t Lq = q.ne[1], H = q.ne[2], N = q.ne[3];
-    const int64_t Lk = k.ne[1], Hkv = k.ne[2], Nkv = k.ne[3];
-    if (v.ne[1] != Lk || v.ne[2] != Hkv || v.ne[3] != Nkv)
-        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "v shape differs from k");
-    if (Hkv <= 0 || Nkv <= 0 || H % Hkv || N % Nkv)
-        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "q heads/sequences are not multiples of k's");
-    if (o.ne[0] != kHeadDim || o.ne[1] != H || o.ne[2] != Lq || o.ne[3] != N)
-        return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [128, H, Lq, N]");
-    if (!(a.scale > 0.f) || !std::isfinite(a.scale))
-        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "scale must be positive and finite");
-    if (Lk > (int64_t)kMaxKvTiles * kBlockN) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "Lk too large");
-    if (H > 65535 || N > 65535) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "more than 65535 heads or sequences");
-    uint64_t onb[4], knb[4], vnb[4], qnb[4];
-    packed_strides(&o, onb);
-    packed_strides(&k, knb);
-    packed_strides(&v, vnb);
-    packed_strides(&q, qnb);
-    if (!strides16(onb) || !aligned16(o.data)) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned");
-    if (Lk > 0 && (!strides16(knb) || !strides16(vnb)))
-        return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "k/v strides must be multiples of 16 bytes");
-    if (Lq == 0 || H == 0 || N == 0) return KD_ATTN_OK;
-    const bool bf16 = k.type == KD_ATTN_TYPE_BF16;
-
-    // scratch plan: [Q rounded to the operand type][mask tile classes], both inside the static array
-    const bool q_direct = q.type == k.type && strides16(qnb) && aligned16(q.data);
-    const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * kHeadDim * 2);
-    int n_qb = 0, n_kb = 0, mh = 1, mn = 1;
-    size_t cls_bytes = 0;
-    uint64_t mnb[4] = {0, 0, 0, 0};
-    if (a.mask) {
-        if ((rc = check_tensor(nc, a.mask, "mask"))) return rc;
-        const kd_tensor& m = *a.mask;
-        if (m.type != KD_ATTN_TYPE_F16) return fail(nc, KD_ATTN_ERR_UNSUPPORTED, "mask must be f16");
-        if (m.ne[0] < Lk || m.ne[1] < Lq) return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "mask smaller than [Lk, Lq]");
-        if (m.ne[2] <= 0 || m.ne[3] <= 0 || H % m.ne[2] || N % m.ne[3])
-            return fail(nc, KD_ATTN_ERR_INVALID_ARGUMENT, "mask planes must divide heads and sequences");
-        mh = (int)m.ne[2];
-        mn = (int)m.ne[3];
-        n_qb = (int)((Lq + 63) / 64);
-        n_kb = (int)((Lk + 63) / 64);
-        cls_bytes = align256((size_t)mh * mn * n_qb * n_kb);
-        packed_strides(a.mask, mnb);
-    }
-    if (q_bytes + cls_bytes > kNoAllocScratchBytes)
-        return fail(nc, KD_ATTN_ERR_UNSUPPORTED,
-                    "kd_attn_flash_ext_noalloc needs %zu bytes of scratch but holds %zu (KD_ATTN_NOALLOC_SCRATCH_BYTES); "
-                    "pass Q in K's type with 16-byte-aligned rows, or use kd_attn_flash_ext",
-                    q_bytes + cls_bytes, kNoAllocScratchBytes);
-
-    NoAllocDevice* d = nullptr;
-    if ((rc = noalloc_setup(&d))) return rc;
-#define KD_CUDA_NC(call)                                                                                 \
-    do {                                                                                                 \
-        cudaError_t _e = (call);                                                                         \
-        if (_e != cudaSuccess) return fail(nc, KD_ATTN_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(_e)); \
-    } while (0)
-
-    const void* qdata = q.data;
-    if (!q_direct) {
-        ConvertParams cp{};
-        cp.src = q.data;
-        cp.src_type = q.type;
-        cp.nb1 = (long long)qnb[1];
-        cp.nb2 = (long long)qnb[2];
-        cp.nb3 = (long long)qnb[3];
-        cp.dst = d->scratch;
-        cp.L = (int)Lq;
-        cp.H = (int)H;
-        cp.N = (int)N;
-        KD_CUDA_NC(launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, d->num_sms, st));
-        qdata = d->scratch;
-        qnb[1] = kHeadDim * 2;
-        qnb[2] = qnb[1] * Lq;
-        qnb[3] = qnb[2] * H;
-    }
-    uint8_t* cls = nullptr;
-    if (a.mask) {
-        cls = reinterpret_cast<uint8_t*>(d->scratch + q_bytes);
-        MaskClassParams mp{};
-        mp.mask = static_cast<const uint16_t*>(a.mask->data);
-        mp.nb1 = (long long)mnb[1];
-        mp.nb2 = (long long)mnb[2];
-        mp.nb3 = (long long)mnb[3];
-        mp.Lq = (int)Lq;
-        mp.Lk = (int)Lk;
-        mp.mh = mh;
-        mp.mn = mn;
-        mp.cls = cls;
-        mp.n_qb = n_qb;
-        mp.n_kb = n_kb;
-        KD_CUDA_NC(launch_mask_classify(mp, st));  // overwrites every class byte it covers
-    }
-    CUtensorMap tmQ, tmK, tmV;
-    if ((rc = make_operand_map(nc, &tmQ, qdata, bf16, Lq, H, N, qnb))) return rc;
-    if (Lk > 0) {
-        if ((rc = make_operand_map(nc, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb))) return rc;
-        if ((rc = make_operand_map(nc, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb))) return rc;
-    } else {
-        tmK = tmQ;
-        tmV = tmQ;
-    }
-    FmhaParams p{};
-    p.Lq = (int)Lq;
-    p.Lk = (int)Lk;
-    p.H = (int)H;
-    p.N = (int)N;
-    p.rk2 = (int)(H / Hkv);
-    p.rk3 = (int)(N / Nkv);
-    p.scale_log2 = a.scale * 1.4426950408889634f;
-    p.inv_scale = 1.0f / a.scale;
-    p.out = o.data;
-    p.o_nb1 = (long long)onb[1];
-    p.o_nb2 = (long long)onb[2];
-    p.o_nb3 = (long long)onb[3];
-    p.lse = a.lse;
-    p.tile_cls = cls;
-    p.n_qb = n_qb;
-    p.n_kb = n_kb;
-    if (a.mask) {
-        p.mask = static_cast<const uint16_t*>(a.mask->data);
-        p.m_nb1 = (long long)mnb[1];
-        p.m_nb2 = (long long)mnb[2];
-        p.m_nb3 = (long long)mnb[3];
-    }
-    p.mh = mh;
-    p.mn = mn;
-    p.kv_len = a.kv_len;
-    p.err = d->words;
-    p.abort_flag = d->words + 1;
-    p.work_counter = d->words + 2;
-    p.num_ctas = d->num_sms;
-    p.wait_ns = 2000000000ull;
-    // abort flag and work counter must start at zero for every launch (the array keeps the last call's contents)
-    KD_CUDA_NC(cudaMemsetAsync(d->words + 1, 0, 2 * sizeof(unsigned), st));
-    KD_CUDA_NC(launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
-#undef KD_CUDA_NC
-    return KD_ATTN_OK;
-}
-
-}  // namespace
-
 extern "C" kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
                                                     const kd_tensor* mask, float scale, float max_bias,
-                                                    float logit_softcap, const int32_t* kv_len, kd_tensor* out,
-                                                    float* lse, void* stream) {
+                                                    float logit_softcap, const int32_t* kv_len,
+                                                    const uint8_t* tile_mask, kd_tensor* out, float* lse,
+                                                    void* stream) {
     if (max_bias != 0.f) return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "max_bias (ALiBi) must be 0");
     if (logit_softcap != 0.f) return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "logit_softcap must be 0");
-    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse};
-    return flash_noalloc(fa, static_cast<cudaStream_t>(stream));
+    FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse, tile_mask};
+    return flash_run(nullptr, fa, static_cast<cudaStream_t>(stream));
 }

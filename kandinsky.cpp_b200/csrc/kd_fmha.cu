@@ -274,6 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 count += __popc(ballot);
             }
+            if (p.tile_stats) {
+                // tiles this unit loads, and Q-tile x K/V-tile products it computes
+                __syncwarp();  // other lanes' list entries are read below
+                int pairs = 0;
+                for (int j = lane; j < count; j += 32) pairs += (int)need(list[j], 0) + (int)need(list[j], 1);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) pairs += __shfl_xor_sync(0xffffffffu, pairs, o);
+                if (lane == 0) {
+                    atomicAdd(p.tile_stats, (unsigned long long)count);
+                    atomicAdd(p.tile_stats + 1, (unsigned long long)pairs);
+                }
+            }
             if (lane == 0) {
                 s_unit[b] = u;
                 s_nkept[b] = count;

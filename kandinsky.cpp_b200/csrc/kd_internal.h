@@ -38,6 +38,7 @@ struct FmhaParams {
     unsigned* work_counter;  // next unit to hand out (cleared by the host before each launch)
     int num_ctas;            // persistent grid size (number of SMs)
     unsigned long long wait_ns;
+    unsigned long long* tile_stats;  // [2] or null: K/V tiles loaded, (Q tile, K/V tile) pairs computed
 };
 
 enum class OpType { F16, BF16 };
@@ -60,17 +61,26 @@ struct RopeTab {
     int grid_h, grid_w;      // token -> (t,h,w): t = l/(gh*gw), h = (l/gw)%gh, w = l%gw
 };
 
-struct PrologueParams {
-    const float* x;          // [C, L, N] f32
-    long long x_nb1, x_nb2;  // byte strides of x (token, sequence); dim 0 contiguous
-    void* y;                 // [128, L, H, N]
-    long long y_nb1, y_nb2, y_nb3;  // byte strides (row, head, sequence)
-    int L, N, H;
+// One projection handled by the prologue: x [C = H*128, L, N] f32 -> y [128, L, H, N].
+struct PrologueJob {
+    const float* x;          // dim 0 contiguous
+    long long x_nb1, x_nb2;  // byte strides of x (token, sequence)
+    void* y;
+    long long y_nb1, y_nb2, y_nb3;  // byte strides of y (row, head, sequence)
+    const float* gain;       // [128] or null (unit gain); used when norm
     int norm;                // 1: RMSNorm
-    const float* gain;       // [128] or null (unit gain)
+    int rope;                // 1: apply RoPE with the shared table
+    int L, N, H;
+};
+
+// Up to three projections in one launch (blockIdx.y = projection).
+constexpr int kPrologueMaxJobs = 3;
+constexpr int kPrologueHeads = 8;  // heads per warp item (8 row loads in flight per lane)
+struct PrologueParams {
+    PrologueJob job[kPrologueMaxJobs];
+    int njobs;
     float eps;
-    int rope;                // 1: apply RoPE with `tab`
-    RopeTab tab;
+    RopeTab tab;             // shared by every projection with rope = 1
 };
 cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st);
 
@@ -84,8 +94,12 @@ struct ConvertParams {
 cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st);
 
 // Classifies each 64x64 tile of an f16 additive mask as skip / full / mixed.
+// With a tile bitmap, tiles whose bit is clear are skip without reading the
+// mask; without a mask, set bits are full tiles.
 struct MaskClassParams {
-    const uint16_t* mask;
+    const uint16_t* mask;            // or null (bitmap only, one plane)
+    const uint8_t* bits;             // or null: bit kb of row qb (rows of bits_row_bytes bytes)
+    int bits_row_bytes;
     long long nb1, nb2, nb3;         // byte strides (query row, head plane, sequence plane)
     int Lq, Lk, mh, mn;
     uint8_t* cls;                    // [mn][mh][n_qb][n_kb]

@@ -30,85 +30,81 @@ __device__ __forceinline__ void store4<__half>(void* dst, float a, float b, floa
     *reinterpret_cast<uint2*>(dst) = make_uint2(Pack2<__half>::pack(a, b), Pack2<__half>::pack(c, d));
 }
 
-constexpr int kPrologueHeads = 4;  // heads per warp work item: 4 row loads in flight, one sin/cos per token
-
 __device__ __forceinline__ float pick_pos(int axis, int t, int h, int w) { return (float)(axis == 0 ? t : (axis == 1 ? h : w)); }
 
-// One warp per (sequence n, token l, group of 4 heads); lane owns elements
-// 4*lane .. 4*lane+3 of each 128-wide head row, i.e. rotary pairs 2*lane and
-// 2*lane+1, whose angle depends only on the token: sin/cos are computed once
-// per token and reused for the group's heads.
-// RMSNorm follows ggml's CPU rms_norm: squares formed in float, summed in
-// double, mean rounded to float, scale = 1/sqrtf(mean + eps), y = x*scale*g.
-// RoPE follows rope::apply (rope.hpp:140-141): x0' = x0*c - x1*s,
-// x1' = x0*s + x1*c, each product rounded separately (no contraction), with
-// angle = pos * freq / scale_factor as rope.hpp:78-95 computes it.
+// RMSNorm over one 128-wide head row held as one float4 per lane, following
+// ggml's CPU rms_norm: squares formed in float, summed in double, mean
+// rounded to float, scale = 1/sqrtf(mean + eps), y = x*scale*g.
+__device__ __forceinline__ float4 rms_norm_row(float4 x, float4 g, float eps) {
+    double ss = (double)__fmul_rn(x.x, x.x) + (double)__fmul_rn(x.y, x.y) + (double)__fmul_rn(x.z, x.z) +
+                (double)__fmul_rn(x.w, x.w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean = (float)(ss * (1.0 / kHeadDim));
+    const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
+    return make_float4(__fmul_rn(__fmul_rn(x.x, scale), g.x), __fmul_rn(__fmul_rn(x.y, scale), g.y),
+                       __fmul_rn(__fmul_rn(x.z, scale), g.z), __fmul_rn(__fmul_rn(x.w, scale), g.w));
+}
+
+// RoPE of rotary pairs (x, y) and (z, w) as rope::apply does it (rope.hpp:140-141):
+// x0' = x0*c - x1*s, x1' = x0*s + x1*c, each product rounded separately (no contraction).
+__device__ __forceinline__ float4 rope_row(float4 x, float s0, float c0, float s1, float c1) {
+    return make_float4(__fsub_rn(__fmul_rn(x.x, c0), __fmul_rn(x.y, s0)), __fadd_rn(__fmul_rn(x.x, s0), __fmul_rn(x.y, c0)),
+                       __fsub_rn(__fmul_rn(x.z, c1), __fmul_rn(x.w, s1)), __fadd_rn(__fmul_rn(x.z, s1), __fmul_rn(x.w, c1)));
+}
+
+// blockIdx.y selects the projection (its parameters stay in registers for the
+// whole loop); one warp per (sequence n, token l, group of kPrologueHeads
+// heads) of it, all of the group's row loads issued before any arithmetic.
+// Lane owns elements 4*lane .. 4*lane+3 of each 128-wide head row, i.e.
+// rotary pairs 2*lane and 2*lane+1, whose angle depends only on the token:
+// sin/cos are computed once per token and reused for the group's heads.  The
+// angle is pos * freq / scale_factor as rope.hpp:78-95 computes it.
+// (Q, K and V of one token in one item, sharing sin/cos between Q and K, was
+// measured slower: 12 rows per item needs 104 registers and halves occupancy.)
 template <typename TO>
-__global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
+__global__ void __launch_bounds__(256) prologue_kernel(const __grid_constant__ PrologueParams p) {
     const int lane = threadIdx.x & 31;
     // per-lane RoPE constants, read from the parameter bank once (not per row)
-    float fr0 = 0.f, fr1 = 0.f, dv0 = 1.f, dv1 = 1.f;
-    int ax0 = 0, ax1 = 0;
-    if (p.rope) {
-        fr0 = p.tab.freq[2 * lane];
-        fr1 = p.tab.freq[2 * lane + 1];
-        dv0 = p.tab.div[2 * lane];
-        dv1 = p.tab.div[2 * lane + 1];
-        ax0 = p.tab.axis[2 * lane];
-        ax1 = p.tab.axis[2 * lane + 1];
-    }
+    const float fr0 = p.tab.freq[2 * lane], fr1 = p.tab.freq[2 * lane + 1];
+    const float dv0 = p.tab.div[2 * lane], dv1 = p.tab.div[2 * lane + 1];
+    const int ax0 = p.tab.axis[2 * lane], ax1 = p.tab.axis[2 * lane + 1];
+    const PrologueJob& T = p.job[blockIdx.y];
     float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (p.norm && p.gain) g = __ldg(reinterpret_cast<const float4*>(p.gain) + lane);
-    const int hgroups = (p.H + kPrologueHeads - 1) / kPrologueHeads;
+    if (T.norm && T.gain) g = __ldg(reinterpret_cast<const float4*>(T.gain) + lane);
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    const long long items = (long long)p.N * p.L * hgroups;
+    const int hgroups = (T.H + kPrologueHeads - 1) / kPrologueHeads;
+    const long long items = (long long)T.N * T.L * hgroups;
     for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
         const int hg = (int)(it % hgroups);
         const long long nl = it / hgroups;
-        const int l = (int)(nl % p.L);
-        const int n = (int)(nl / p.L);
+        const int l = (int)(nl % T.L);
+        const int n = (int)(nl / T.L);
         const int h0 = hg * kPrologueHeads;
-        const int nh = min(kPrologueHeads, p.H - h0);
-        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(p.x) +
-                                                            (long long)n * p.x_nb2 + (long long)l * p.x_nb1) +
+        const int nh = min(kPrologueHeads, T.H - h0);
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(T.x) +
+                                                            (long long)n * T.x_nb2 + (long long)l * T.x_nb1) +
                             (h0 * kHeadDim) / 4 + lane;
         float4 v[kPrologueHeads];
 #pragma unroll
         for (int j = 0; j < kPrologueHeads; ++j)
             if (j < nh) v[j] = __ldcs(src + j * (kHeadDim / 4));
         float s0 = 0.f, c0 = 1.f, s1 = 0.f, c1 = 1.f;
-        if (p.rope) {
+        if (T.rope) {
             const int hw = p.tab.grid_h * p.tab.grid_w;
             const int t = l / hw, hh = (l / p.tab.grid_w) % p.tab.grid_h, w = l % p.tab.grid_w;
             sincosf(__fdiv_rn(__fmul_rn(pick_pos(ax0, t, hh, w), fr0), dv0), &s0, &c0);
             sincosf(__fdiv_rn(__fmul_rn(pick_pos(ax1, t, hh, w), fr1), dv1), &s1, &c1);
         }
+        char* dst = reinterpret_cast<char*>(T.y) + (long long)n * T.y_nb3 + (long long)h0 * T.y_nb2 +
+                    (long long)l * T.y_nb1 + (long long)lane * 4 * sizeof(TO);
 #pragma unroll
         for (int j = 0; j < kPrologueHeads; ++j) {
             if (j >= nh) break;
             float4 x = v[j];
-            if (p.norm) {
-                double ss = (double)__fmul_rn(x.x, x.x) + (double)__fmul_rn(x.y, x.y) + (double)__fmul_rn(x.z, x.z) +
-                            (double)__fmul_rn(x.w, x.w);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                const float mean = (float)(ss * (1.0 / kHeadDim));
-                const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, p.eps)));
-                x.x = __fmul_rn(__fmul_rn(x.x, scale), g.x);
-                x.y = __fmul_rn(__fmul_rn(x.y, scale), g.y);
-                x.z = __fmul_rn(__fmul_rn(x.z, scale), g.z);
-                x.w = __fmul_rn(__fmul_rn(x.w, scale), g.w);
-            }
-            if (p.rope) {
-                const float a0 = __fsub_rn(__fmul_rn(x.x, c0), __fmul_rn(x.y, s0));
-                const float a1 = __fadd_rn(__fmul_rn(x.x, s0), __fmul_rn(x.y, c0));
-                const float b0 = __fsub_rn(__fmul_rn(x.z, c1), __fmul_rn(x.w, s1));
-                const float b1 = __fadd_rn(__fmul_rn(x.z, s1), __fmul_rn(x.w, c1));
-                x = make_float4(a0, a1, b0, b1);
-            }
-            char* dst = reinterpret_cast<char*>(p.y) + (long long)n * p.y_nb3 + (long long)(h0 + j) * p.y_nb2 +
-                        (long long)l * p.y_nb1 + (long long)lane * 4 * sizeof(TO);
-            store4<TO>(dst, x.x, x.y, x.z, x.w);
+            if (T.norm) x = rms_norm_row(x, g, p.eps);
+            if (T.rope) x = rope_row(x, s0, c0, s1, c1);
+            store4<TO>(dst + (long long)j * T.y_nb2, x.x, x.y, x.z, x.w);
         }
     }
 }
@@ -148,6 +144,8 @@ __global__ void __launch_bounds__(256) convert_q_kernel(const ConvertParams p) {
 // flight at a time, and the warp votes whether every in-range element is -inf
 // (skip) or +-0 (full); anything else is mixed.  Elements outside
 // [0,Lq) x [0,Lk) are ignored; a tile with no in-range element is a skip tile.
+// A tile whose bit in the optional bitmap is clear is skip and its mask
+// elements are never read; without a mask, a set bit means full.
 __global__ void __launch_bounds__(256) mask_classify_kernel(const MaskClassParams p) {
     const int lane = threadIdx.x & 31;
     const long long tiles_per_plane = (long long)p.n_qb * p.n_kb;
@@ -157,6 +155,13 @@ __global__ void __launch_bounds__(256) mask_classify_kernel(const MaskClassParam
         const int plane = (int)(t / tiles_per_plane);
         const long long r = t % tiles_per_plane;
         const int qb = (int)(r / p.n_kb), kb = (int)(r % p.n_kb);
+        if (p.bits || !p.mask) {
+            const bool bit = !p.bits || ((p.bits[(long long)qb * p.bits_row_bytes + (kb >> 3)] >> (kb & 7)) & 1u);
+            if (!bit || !p.mask) {
+                if (lane == 0) p.cls[t] = bit ? kTileFull : kTileSkip;
+                continue;
+            }
+        }
         const int mhi = plane % p.mh, mni = plane / p.mh;
         const char* base = reinterpret_cast<const char*>(p.mask) + (long long)mni * p.nb3 + (long long)mhi * p.nb2;
         const int key = kb * 64 + 2 * lane;
@@ -237,9 +242,14 @@ int grid_for(long long warps_needed, int num_sms) {
 }  // namespace
 
 cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st) {
-    const long long items = (long long)p.N * p.L * ((p.H + kPrologueHeads - 1) / kPrologueHeads);
-    if (items == 0) return cudaSuccess;
-    const int grid = grid_for(items, num_sms);
+    long long items = 0;
+    for (int j = 0; j < p.njobs; ++j) {
+        const PrologueJob& J = p.job[j];
+        const long long n = (long long)J.N * J.L * ((J.H + kPrologueHeads - 1) / kPrologueHeads);
+        items = items > n ? items : n;
+    }
+    if (items == 0 || p.njobs <= 0) return cudaSuccess;
+    const dim3 grid(grid_for(items, num_sms), p.njobs);
     if (yt == OutType::BF16)
         prologue_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
     else if (yt == OutType::F16)

@@ -39,7 +39,8 @@ EXPORTED = [
     "kd_attn_create", "kd_attn_destroy", "kd_attn_last_error", "kd_attn_device_status",
     "kd_attn_prologue", "kd_attn_flash_ext", "kd_attn_self_attention", "kd_attn_cross_attention",
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
-    "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host",
+    "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
+    "kd_attn_tile_stats", "kd_attn_set_log_callback",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -123,7 +124,10 @@ def _load():
     L.kd_attn_prologue.argtypes = [P, T, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_float,
                                    ctypes.POINTER(Rope3D), T, P]
     L.kd_attn_prologue.restype = st
-    L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, T, P, P]
+    L.kd_attn_qk_prologue.argtypes = [P, T, T, T, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), ctypes.c_int32,
+                                      T, T, T, P]
+    L.kd_attn_qk_prologue.restype = st
+    L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
                                          ctypes.POINTER(Rope3D), ctypes.c_int32, T, P, P]
@@ -140,8 +144,13 @@ def _load():
     L.kd_attn_fill_randn.restype = st
     L.kd_attn_nccl_unique_id.argtypes = [P]
     L.kd_attn_nccl_unique_id.restype = st
-    L.kd_attn_flash_ext_noalloc.argtypes = [T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, T, P, P]
+    L.kd_attn_flash_ext_noalloc.argtypes = [T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P,
+                                            P]
     L.kd_attn_flash_ext_noalloc.restype = st
+    L.kd_attn_tile_stats.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
+    L.kd_attn_tile_stats.restype = st
+    L.kd_attn_set_log_callback.argtypes = [LOG_CB, P]
+    L.kd_attn_set_log_callback.restype = None
     L.kd_attn_version.argtypes = []
     L.kd_attn_version.restype = ctypes.c_int32
     return L
@@ -153,6 +162,26 @@ lib = _load()
 def version():
     v = lib.kd_attn_version()
     return (v >> 16, v & 0xFFFF)
+
+
+_global_log_cb = None
+
+
+def set_log_callback(log=None):
+    """kd_attn_set_log_callback: process-wide logger log(level, text) for contexts created without
+    one and for the allocation-free entry point; None restores the stderr default."""
+    global _global_log_cb
+    cb = LOG_CB(lambda lvl, txt, _u: log(lvl, txt.decode())) if log else LOG_CB()
+    lib.kd_attn_set_log_callback(cb, None)
+    _global_log_cb = cb  # keep the trampoline alive while the library may call it
+
+
+def tile_bitmap(keep):
+    """Pack a (n_qb, n_kb) bool array of kept 64x64 tiles into kd_attn_flash_ext's tile_mask layout
+    (row qb = ceil(n_kb / 8) bytes, tile kb = bit kb % 8 of byte kb // 8)."""
+    import numpy as np
+    keep = np.asarray(keep, dtype=bool)
+    return np.packbits(keep, axis=1, bitorder="little")
 
 
 def nccl_unique_id() -> bytes:
@@ -168,6 +197,10 @@ def _stream_ptr(stream):
         import torch
         stream = torch.cuda.current_stream()
     return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def torch_dtype_name(t):
+    return str(t.dtype)
 
 
 def _ptr(t):
@@ -232,16 +265,37 @@ class Context:
                                         _stream_ptr(stream)))
         return y
 
+    def qk_prologue(self, q_in, k_in, v_in, q_out, k_out, v_out, q_gain=None, k_gain=None, eps=1e-6, rope=None,
+                    stream=None):
+        """One launch: q_in/k_in (N, L, C) f32 -> RMSNorm (+RoPE) -> q_out/k_out (N, H, L, 128); v_in -> v_out
+        cast only.  Any (in, out) pair may be None."""
+        types = {torch_dtype_name(t) for t in (q_out, k_out, v_out) if t is not None}
+        if len(types) != 1:
+            raise ValueError("outputs must share one dtype")
+        out_dtype = KdTensor.of(next(t for t in (q_out, k_out, v_out) if t is not None)).type
+        self.check(lib.kd_attn_qk_prologue(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), _ptr(q_gain),
+                                           _ptr(k_gain), float(eps), None if rope is None else ctypes.byref(rope),
+                                           int(out_dtype), _ref(q_out), _ref(k_out), _ref(v_out),
+                                           _stream_ptr(stream)))
+        return q_out, k_out, v_out
+
     def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
-                       logit_softcap=0.0, stream=None):
+                       logit_softcap=0.0, tile_mask=None, stream=None):
         """ggml_flash_attn_ext.  q: (N, H, Lq, 128); k, v: (Nkv, Hkv, Lk, 128);
-        mask: (mn, mh, >=Lq, >=Lk) f16 or None; out: (N, Lq, H, 128); lse: (N, H, Lq) f32 or None."""
+        mask: (mn, mh, >=Lq, >=Lk) f16 or None; out: (N, Lq, H, 128); lse: (N, H, Lq) f32 or None;
+        tile_mask: device uint8 bitmap of kept 64x64 tiles (tile_bitmap layout) or None."""
         if scale is None:
             scale = 1.0 / (q.shape[-1] ** 0.5)
         self.check(lib.kd_attn_flash_ext(self.handle, _ref(q), _ref(k), _ref(v), _ref(mask), float(scale),
-                                         float(max_bias), float(logit_softcap), _ptr(kv_len), _ref(out), _ptr(lse),
-                                         _stream_ptr(stream)))
+                                         float(max_bias), float(logit_softcap), _ptr(kv_len), _ptr(tile_mask),
+                                         _ref(out), _ptr(lse), _stream_ptr(stream)))
         return out
+
+    def tile_stats(self, reset=False, stream=None):
+        """(K/V tiles loaded, Q-tile x K/V-tile products computed) since the last reset."""
+        out = (ctypes.c_uint64 * 2)()
+        self.check(lib.kd_attn_tile_stats(self.handle, _stream_ptr(stream), out, 1 if reset else 0))
+        return int(out[0]), int(out[1])
 
     def self_attention(self, q_in, k_in, v_in, n_head, out, rope=None, q_gain=None, k_gain=None, eps=1e-6,
                        op_type=BF16, lse=None, stream=None):
@@ -285,7 +339,7 @@ class Context:
 
 
 def flash_attn_ext_noalloc(q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
-                           logit_softcap=0.0, stream=None):
+                           logit_softcap=0.0, tile_mask=None, stream=None):
     """kd_attn_flash_ext_noalloc: flash_attn_ext without a Context and without any device allocation.
 
     For callers that may not allocate (graph capture, foreign memory arenas).  Runs on the current
@@ -296,7 +350,8 @@ def flash_attn_ext_noalloc(q, k, v, out, mask=None, scale=None, kv_len=None, lse
     if scale is None:
         scale = 1.0 / (q.shape[-1] ** 0.5)
     rc = lib.kd_attn_flash_ext_noalloc(_ref(q), _ref(k), _ref(v), _ref(mask), float(scale), float(max_bias),
-                                       float(logit_softcap), _ptr(kv_len), _ref(out), _ptr(lse), _stream_ptr(stream))
+                                       float(logit_softcap), _ptr(kv_len), _ptr(tile_mask), _ref(out), _ptr(lse),
+                                       _stream_ptr(stream))
     if rc != OK:
         raise KdAttnError(rc, "kd_attn_flash_ext_noalloc failed (details on stderr)")
     return out

@@ -51,7 +51,7 @@ def test_create_rejects_bad_arguments(kd):
     h = ctypes.c_void_p()
     assert kd.lib.kd_attn_create(ctypes.byref(init), ctypes.byref(h)) == kd.ERR_INVALID_ARGUMENT
     assert kd.lib.kd_attn_create(None, ctypes.byref(h)) == kd.ERR_INVALID_ARGUMENT
-    assert kd.lib.kd_attn_flash_ext(None, None, None, None, None, 1.0, 0.0, 0.0, None, None, None, None) == \
+    assert kd.lib.kd_attn_flash_ext(None, None, None, None, None, 1.0, 0.0, 0.0, None, None, None, None, None) == \
         kd.ERR_INVALID_ARGUMENT
 
 
@@ -66,3 +66,20 @@ def test_kd_tensor_maps_torch_layout_to_ggml(kd):
     assert list(k.ne) == [128, 32, 100, 2] and list(k.nb) == [2, 256 * 100, 256, 256 * 100 * 32]
     k = kd.KdTensor.of(torch.empty(5, 7, dtype=torch.float32))
     assert list(k.ne) == [7, 5, 1, 1] and list(k.nb) == [4, 28, 140, 140]
+
+
+def test_tile_bitmap_layout(kd):
+    """tile_mask layout of kd_attn_flash_ext: row qb holds ceil(n_kb / 8) bytes, tile kb is bit kb % 8
+    of byte kb // 8 (least significant bit first)."""
+    import numpy as np
+    keep = np.zeros((3, 11), bool)
+    keep[0, 0] = keep[1, 8] = keep[2, 10] = keep[2, 7] = True
+    b = kd.tile_bitmap(keep)
+    assert b.shape == (3, 2) and b.dtype == np.uint8
+    assert b[0].tolist() == [1, 0] and b[1].tolist() == [0, 1] and b[2].tolist() == [0x80, 0x04]
+
+
+def test_set_log_callback_roundtrip(kd):
+    """The process-wide logger is callable without a GPU: set, then restore the default."""
+    kd.set_log_callback(lambda lvl, txt: None)
+    kd.set_log_callback(None)

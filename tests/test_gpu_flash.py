@@ -263,3 +263,87 @@ def test_self_attention_host_matches_device_path(ctx, kd, H, grid, N, out_dtype,
     ctx.self_attention_host(*ins, H, out2, rope=rope, op_type=kd.BF16, stream=s)
     s.synchronize()
     assert torch.equal(out2, ref.cpu())
+
+
+# ------------------------------------------------------------------ tile bitmap, tile counters, fused prologue
+def expected_tile_counts(keep, Lq, Lk, units_per_plane_mult):
+    """K/V tiles (128 keys) loaded and Q-tile (128 rows) x K/V-tile products computed for one
+    (head, sequence) plane, times the number of planes: a 128-key tile is loaded when any of the
+    unit's (256 rows) 64x64 sub-tiles is kept, and computed for each Q tile with a kept sub-tile."""
+    n_qb, n_kb = keep.shape
+    n_units = (Lq + 255) // 256
+    n_kv = (Lk + 127) // 128
+    loaded = pairs = 0
+    for u in range(n_units):
+        for t in range(n_kv):
+            need = []
+            for i in range(2):
+                sub = keep[4 * u + 2 * i: 4 * u + 2 * i + 2, 2 * t: 2 * t + 2]
+                need.append(bool(sub.any()))
+            loaded += any(need)
+            pairs += sum(need)
+    return loaded * units_per_plane_mult, pairs * units_per_plane_mult
+
+
+def test_tile_bitmap_skips_tiles_and_matches_dense_mask(ctx, kd):
+    """Block-sparse attention from the 64x64 tile bitmap alone equals the dense f16 block mask bit for
+    bit, and the device counters show exactly the kept tiles were loaded and multiplied."""
+    N, H, Lq, Lk, D = 2, 2, 1000, 1000, 128
+    qf = seeded((N, H, Lq, D), 61, 0)
+    kf = seeded((N, H, Lk, D), 61, 1)
+    vf = seeded((N, H, Lk, D), 61, 2)
+    rng = np.random.default_rng(8)
+    n_qb, n_kb = (Lq + 63) // 64, (Lk + 63) // 64
+    keep = rng.random((n_qb, n_kb)) < 0.2
+    np.fill_diagonal(keep, True)
+    dense = np.where(np.kron(keep, np.ones((64, 64)))[:Lq, :Lk], 0, -np.inf).astype(np.float16)[None, None]
+    kb, vb = oracle.to_type(kf, oracle.BF16), oracle.to_type(vf, oracle.BF16)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, mask=dense, mode=oracle.EXACT, lse=True)
+    bits = torch.from_numpy(kd.tile_bitmap(keep)).cuda()
+    assert bits.shape == (n_qb, (n_kb + 7) // 8)
+    q, k, v = dev(qf), op_tensor(kf, oracle.BF16), op_tensor(vf, oracle.BF16)
+    outs = {}
+    want = expected_tile_counts(keep, Lq, Lk, H * N)
+    dense_counts = expected_tile_counts(np.ones_like(keep), Lq, Lk, H * N)
+    for name, kw in (("dense", dict(mask=torch.from_numpy(dense).cuda())), ("bitmap", dict(tile_mask=bits)),
+                     ("both", dict(mask=torch.from_numpy(dense).cuda(), tile_mask=bits)), ("none", {})):
+        ctx.tile_stats(reset=True)
+        out = torch.empty(N, Lq, H, D, device="cuda")
+        lse = torch.empty(N, H, Lq, device="cuda")
+        ctx.flash_attn_ext(q, k, v, out, lse=lse, **kw)
+        counts = ctx.tile_stats(reset=True)
+        ctx.device_status()
+        outs[name] = (out.cpu(), lse.cpu())
+        assert counts == (dense_counts if name == "none" else want), (name, counts)
+    assert want[0] < dense_counts[0]
+    assert_gates(outs["bitmap"][0].numpy(), exact, lse=outs["bitmap"][1].numpy(), lse_ref=lse_ref, label="bitmap")
+    for name in ("dense", "both"):
+        assert torch.equal(outs[name][0], outs["bitmap"][0]) and torch.equal(outs[name][1], outs["bitmap"][1])
+
+
+@pytest.mark.parametrize("Lq,Lk", [(1280, 1280), (700, 77)])
+def test_qk_prologue_one_launch_equals_separate_calls(ctx, kd, Lq, Lk):
+    """kd_attn_qk_prologue (Q, K, V in one launch; two jobs when Lq != Lk) equals three
+    kd_attn_prologue calls bit for bit, with gains, with and without RoPE, and with pairs left out."""
+    N, H = 2, 3
+    C = H * 128
+    q = dev(seeded((N, Lq, C), 71, 0))
+    k = dev(seeded((N, Lk, C), 71, 1))
+    v = dev(seeded((N, Lk, C), 71, 2))
+    gq = torch.linspace(0.5, 1.5, 128, device="cuda")
+    gk = torch.linspace(1.5, 0.5, 128, device="cuda")
+    rope = kd.Rope3D.make((5, 16, 16), scale=(1, 2, 2)) if Lq == Lk == 1280 else None
+    for dt in (torch.bfloat16, torch.float16, torch.float32):
+        ref = [torch.empty(N, H, L, 128, device="cuda", dtype=dt) for L in (Lq, Lk, Lk)]
+        ctx.prologue(q, H, ref[0], norm=True, gain=gq, rope=rope)
+        ctx.prologue(k, H, ref[1], norm=True, gain=gk, rope=rope)
+        ctx.prologue(v, H, ref[2], norm=False)
+        got = [torch.full_like(r, 3.0) for r in ref]
+        ctx.qk_prologue(q, k, v, *got, q_gain=gq, k_gain=gk, rope=rope)
+        ctx.device_status()
+        for g, r in zip(got, ref):
+            assert torch.equal(g, r)
+        only_kv = [torch.full_like(r, 3.0) for r in ref[1:]]
+        ctx.qk_prologue(None, k, v, None, *only_kv, k_gain=gk, rope=rope)
+        ctx.device_status()
+        assert torch.equal(only_kv[0], ref[1]) and torch.equal(only_kv[1], ref[2])
