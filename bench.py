@@ -414,12 +414,19 @@ def main():
     q, k, v = proj(0), proj(1), proj(2)
     rope = kd_attn.Rope3D.make(cfg["grid"])
     out_shard = torch.empty(N, L, Cs, device=dev, dtype=out_dt)
-    out_full = torch.empty(N, L, H * d, device=dev, dtype=out_dt) if ws > 1 else out_shard
+    # N > 1: every rank's copy of the full output is mapped into every other rank; the flash epilogue
+    # stores each row into all copies (kd_attn_self_attention_sharded)
+    out_full = ctx.symmetric_tensor((N, L, H * d), out_dt) if ws > 1 else out_shard
 
     def step():
-        ctx.self_attention(q, k, v, Hs, out_shard, rope=rope, op_type=op, stream=stream)
         if ws > 1:
-            ctx.allgather_heads(out_shard.view(N, L, Hs, d), out_full.view(N, L, H, d), stream=stream)
+            ctx.self_attention_sharded(q, k, v, Hs, out_full, rope=rope, op_type=op, stream=stream)
+        else:
+            ctx.self_attention(q, k, v, Hs, out_shard, rope=rope, op_type=op, stream=stream)
+
+    def step_nccl():  # the unfused alternative: attention into the shard, then ncclAllGather + permute
+        ctx.self_attention(q, k, v, Hs, out_shard, rope=rope, op_type=op, stream=stream)
+        ctx.allgather_heads(out_shard.view(N, L, Hs, d), out_nccl.view(N, L, H, d), stream=stream)
 
     def barrier():
         torch.cuda.synchronize()
@@ -476,6 +483,23 @@ def main():
     ms = float(t.item())
     flop = 4.0 * N * H * L * L * d
     value = flop / (ms * 1e-3) / 1e12
+
+    nccl_ms = None
+    if ws > 1:  # the same job with the exchange as a separate ncclAllGather + permute, for comparison
+        out_nccl = torch.empty(N, L, H * d, device=dev, dtype=out_dt)
+        for _ in range(2):
+            step_nccl()
+        barrier()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record(stream)
+        for _ in range(args.steps):
+            step_nccl()
+        n1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([n0.elapsed_time(n1) / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_ms = float(t.item())
+        del out_nccl
 
     # dominant kernel alone: flash attention on the bf16 operands the prologue produced
     qs = torch.empty(N, Hs, L, d, device=dev, dtype=torch.bfloat16 if op == kd_attn.BF16 else torch.float16)
@@ -544,18 +568,21 @@ def main():
         "data": "synthetic: seeded Philox4x32-10 N(0,1) projections generated on the device",
         "config": {"workload": cfg["name"], "global_batch": N, "seq_len": L, "heads": H, "head_dim": d,
                    "parallelism": f"heads{ws}" if ws > 1 else "single",
-                   "step": "kd_attn_self_attention (one fused RMSNorm+RoPE+cast prologue launch, tcgen05 flash attention)"
-                           + (" + allgather_heads" if ws > 1 else ""),
+                   "step": ("kd_attn_self_attention_sharded (barrier, fused prologue, tcgen05 flash attention whose "
+                            "epilogue stores every row into all ranks' symmetric copies over NVLink, barrier)")
+                           if ws > 1 else
+                           "kd_attn_self_attention (one fused RMSNorm+RoPE+cast prologue launch, tcgen05 flash attention)",
                    "l2": "inputs larger than L2 (3 x f32 projections per rank)"},
         "roofline": {"bound": "tensor", "achieved": fa_tflops, "peak": pk, "unit": "TFLOP/s",
                      "frac": fa_tflops / pk if pk else None, "peak_kind": f"{pk_kind} burst bf16",
                      "frac_of_sustained": fa_tflops / pk_sus if pk_sus else None,
                      "traffic": traffic, "kernel": "fmha_fwd_kernel<bf16>", "kernel_ms": fa_ms},
+        "unfused_nccl_step_ms": nccl_ms,
         "prologue": {"ms": pro_ms, "gbs": (3 * N * L * Cs * 4 + 3 * N * L * Cs * 2) / (pro_ms * 1e-3) / 1e9},
         "e2e": {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "call": "kd_attn_self_attention_host (head-group pipelined H2D / compute / D2H)"},
-        "gpu_launches": args.steps * (2 + (1 if ws > 1 else 0)),  # prologue + flash (+ unshard)
+        "gpu_launches": args.steps * 2,  # prologue + flash (the barriers are NCCL kernels)
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:

@@ -263,6 +263,35 @@ kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, 
 kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard, kd_tensor* full,
                                        void* stream);
 
+/* Symmetric buffers for the fused head exchange.  Collective over the
+ * context's group: every rank calls it with the same size, in the same order.
+ * Each rank gets `bytes` of its own device memory (*out) and maps every other
+ * rank's copy (CUDA IPC over NVLink); a kernel can then store into all copies.
+ * kd_attn_symmetric_free is collective too (it waits for every rank, on
+ * `stream`, before unmapping); kd_attn_destroy releases what is left. */
+kd_attn_status kd_attn_symmetric_alloc(kd_attn_ctx* ctx, size_t bytes, void** out);
+kd_attn_status kd_attn_symmetric_free(kd_attn_ctx* ctx, void* ptr, void* stream);
+
+/* Head-sharded self-attention with the all-gather fused into the flash
+ * kernel: the reference runs the whole of DiTSelfAttention::forward's
+ * attention (crossdit.hpp:132-150) on one device; here rank r of n computes
+ * heads [r*n_head_local, (r+1)*n_head_local) from its column shard of the
+ * projections (q_in, k_in, v_in: [n_head_local*128, L, N] f32) and its
+ * flash-kernel epilogue stores every output row both into its own copy of
+ * out_full and, over NVLink, into every other rank's copy, at the rank's
+ * columns, so the exchange overlaps the attention math instead of following it.
+ * out_full: [n_head_local*n_ranks*128, L, N] (f32 or op_type) inside a
+ * kd_attn_symmetric_alloc buffer, at the same offset on every rank.
+ * Collective: two barriers on the communicator, one before the kernels (no rank
+ * still reads the previous contents of its copy) and one after (every row has
+ * landed in every copy).  When `stream` has drained, each rank's out_full holds
+ * all heads -- the input of the out-projection (crossdit.hpp:153).  With one
+ * rank this is kd_attn_self_attention into out_full. */
+kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                              const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
+                                              const float* k_gain, float eps, const kd_rope3d* rope,
+                                              int32_t op_type, kd_tensor* out_full, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Seeded N(0,1) fill on the device: Philox4x32-10 + Box-Muller with the
  * counter layout of PhiloxRNG::randn (src/rng.hpp:51-69): element i of a call

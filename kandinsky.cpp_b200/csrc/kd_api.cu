@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/kd_attn.h"
 #include "kd_internal.h"
@@ -35,6 +36,14 @@ struct kd_attn_ctx {
     cudaStream_t h2d = nullptr, d2h = nullptr;
     cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
     cudaEvent_t ev_start = nullptr, ev_last = nullptr;
+    // head sharding: buffers allocated on every rank whose peers' copies are mapped here
+    struct SymBuf {
+        char* local = nullptr;
+        size_t bytes = 0;
+        char* peer[8] = {};  // indexed by rank; peer[rank] == local
+    };
+    std::vector<SymBuf> sym;
+    unsigned char* d_barrier = nullptr;  // [64]: NCCL barrier send/receive bytes
 };
 
 namespace {
@@ -225,6 +234,32 @@ constexpr int kNcclUint8 = 1;  // ncclDataType_t ncclUint8
 
 const char* nccl_err(Nccl* n, int r) { return (n && n->getErrorString) ? n->getErrorString(r) : "nccl error"; }
 
+// Every rank of the group reaches this point of its stream before any passes it: one 1-byte
+// all-gather on the context's communicator (a no-op for a single rank).
+kd_attn_status rank_barrier(kd_attn_ctx* ctx, cudaStream_t st) {
+    if (ctx->n_ranks <= 1) return KD_ATTN_OK;
+    Nccl* n = nccl();
+    if (!n || !ctx->nccl_comm) return fail(ctx, KD_ATTN_ERR_NCCL, "context has no NCCL communicator");
+    const int r = n->allGather(ctx->d_barrier, ctx->d_barrier + 8, 1, kNcclUint8, ctx->nccl_comm, st);
+    if (r != 0) return fail(ctx, KD_ATTN_ERR_NCCL, "ncclAllGather (barrier): %s", nccl_err(n, r));
+    return KD_ATTN_OK;
+}
+
+// The symmetric buffer holding [p, p + bytes), or null.
+kd_attn_ctx::SymBuf* find_sym(kd_attn_ctx* ctx, const void* p, size_t bytes) {
+    const char* c = static_cast<const char*>(p);
+    for (auto& b : ctx->sym)
+        if (c >= b.local && c + bytes <= b.local + b.bytes) return &b;
+    return nullptr;
+}
+
+void release_sym(kd_attn_ctx* ctx, kd_attn_ctx::SymBuf& b) {
+    for (int i = 0; i < ctx->n_ranks && i < 8; ++i)
+        if (i != ctx->rank && b.peer[i]) cudaIpcCloseMemHandle(b.peer[i]);
+    if (b.local) cudaFree(b.local);
+    b = kd_attn_ctx::SymBuf{};
+}
+
 OutType out_type_of(int32_t t) {
     return t == KD_ATTN_TYPE_F32 ? OutType::F32 : (t == KD_ATTN_TYPE_BF16 ? OutType::BF16 : OutType::F16);
 }
@@ -240,6 +275,10 @@ struct FlashArgs {
     kd_tensor* out;
     float* lse;
     const uint8_t* tile_mask;  // bit-packed 64x64 tile bitmap or null
+    // head sharding: the output's byte offset from `out_base` is also written at peer_base[i] + offset
+    const char* out_base = nullptr;
+    char* const* peer_base = nullptr;
+    int n_peers = 0;
 };
 
 // ------------------------------------------------------------------ allocation-free scratch
@@ -467,6 +506,10 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     p.num_ctas = num_sms;
     p.wait_ns = wait_ns;
     p.tile_stats = stats;
+    if (a.n_peers > kMaxPeers) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than %d peers", kMaxPeers);
+    for (int i = 0; i < a.n_peers; ++i)
+        p.peer_out[i] = a.peer_base[i] + (static_cast<const char*>(o.data) - a.out_base);
+    p.n_peer_out = a.n_peers;
     // abort flag and work counter start at zero for every launch
     KD_CUDA(ctx, cudaMemsetAsync(words + 1, 0, 2 * sizeof(unsigned), st));
     KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
@@ -618,7 +661,8 @@ kd_attn_status out_view(kd_attn_ctx* ctx, const kd_tensor* out, int32_t n_head, 
 kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
                               int32_t n_head, const float* q_gain, const float* k_gain, float eps,
                               const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
-                              kd_tensor* out, float* lse, cudaStream_t st) {
+                              kd_tensor* out, float* lse, cudaStream_t st, const char* out_base = nullptr,
+                              char* const* peer_base = nullptr, int n_peers = 0) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
         (rc = check_tensor(ctx, v_in, "v_in")))
@@ -646,6 +690,9 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     const PrologueReq req[3] = {{q_in, 1, q_gain, true, &Qs}, {k_in, 1, k_gain, true, &Ks}, {v_in, 0, nullptr, false, &Vs}};
     if ((rc = prologue_multi(ctx, req, 3, n_head, eps, rope, st))) return rc;
     FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, lse};
+    fa.out_base = out_base;
+    fa.peer_base = peer_base;
+    fa.n_peers = n_peers;
     return flash_run(ctx, fa, st);
 }
 
@@ -829,8 +876,11 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
     }
     ctx->num_sms = prop.multiProcessorCount;
     if (cudaMalloc(&ctx->d_words, 8 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(ctx->d_words, 0, 8 * sizeof(unsigned)) != cudaSuccess) {
+        cudaMemset(ctx->d_words, 0, 8 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&ctx->d_barrier, 64) != cudaSuccess || cudaMemset(ctx->d_barrier, 0, 64) != cudaSuccess) {
         cudaGetLastError();
+        if (ctx->d_words) cudaFree(ctx->d_words);
+        if (ctx->d_barrier) cudaFree(ctx->d_barrier);
         delete ctx;
         return KD_ATTN_ERR_OUT_OF_MEMORY;
     }
@@ -839,6 +889,7 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
         if (!n || !init->nccl_unique_id) {
             fail(ctx, KD_ATTN_ERR_NCCL, "n_ranks > 1 needs NCCL and an nccl_unique_id");
             cudaFree(ctx->d_words);
+            cudaFree(ctx->d_barrier);
             delete ctx;
             return KD_ATTN_ERR_NCCL;
         }
@@ -848,6 +899,7 @@ kd_attn_status kd_attn_create(const kd_attn_init* init, kd_attn_ctx** out) {
         if (r != 0) {
             fail(ctx, KD_ATTN_ERR_NCCL, "ncclCommInitRank: %s", nccl_err(n, r));
             cudaFree(ctx->d_words);
+            cudaFree(ctx->d_barrier);
             delete ctx;
             return KD_ATTN_ERR_NCCL;
         }
@@ -872,9 +924,14 @@ void kd_attn_destroy(kd_attn_ctx* ctx) {
         cudaEventDestroy(ctx->ev_start);
         cudaEventDestroy(ctx->ev_last);
     }
+    // Symmetric buffers: close this process's mappings of the peers' copies, free its own.  No
+    // kernel of any rank may still be writing (callers destroy after their last step completed).
+    for (auto& b : ctx->sym) release_sym(ctx, b);
+    ctx->sym.clear();
     if (ctx->nccl_comm) {
         if (Nccl* n = nccl()) n->commDestroy(ctx->nccl_comm);
     }
+    if (ctx->d_barrier) cudaFree(ctx->d_barrier);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->d_words) cudaFree(ctx->d_words);
     delete ctx;
@@ -990,6 +1047,116 @@ kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, 
     DeviceGuard g(ctx->device);
     return attention_core(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, nullptr, mask, kv_len, op_type, out, lse,
                           static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_symmetric_alloc(kd_attn_ctx* ctx, size_t bytes, void** out) {
+    if (!ctx || !out || bytes == 0) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    DeviceGuard g(ctx->device);
+    const int R = ctx->n_ranks;
+    if (R > 8) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "symmetric buffers span at most 8 ranks");
+    kd_attn_ctx::SymBuf b;
+    b.bytes = align256(bytes);
+    if (cudaMalloc(reinterpret_cast<void**>(&b.local), b.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, KD_ATTN_ERR_OUT_OF_MEMORY, "could not allocate %zu bytes", b.bytes);
+    }
+    b.peer[ctx->rank] = b.local;
+    if (R > 1) {
+        Nccl* n = nccl();
+        if (!n || !ctx->nccl_comm) {
+            cudaFree(b.local);
+            return fail(ctx, KD_ATTN_ERR_NCCL, "context has no NCCL communicator");
+        }
+        // exchange IPC handles: one 64-byte handle per rank, all-gathered over the communicator
+        cudaIpcMemHandle_t mine;
+        std::vector<cudaIpcMemHandle_t> all(R);
+        unsigned char* dev = nullptr;
+        cudaStream_t s = nullptr;
+        kd_attn_status rc = KD_ATTN_OK;
+        cudaError_t e = cudaIpcGetMemHandle(&mine, b.local);
+        if (e == cudaSuccess) e = cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * (R + 1));
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dev, &mine, sizeof mine, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) {
+            const int r = n->allGather(dev, dev + sizeof mine, sizeof mine, kNcclUint8, ctx->nccl_comm, s);
+            if (r != 0) rc = fail(ctx, KD_ATTN_ERR_NCCL, "ncclAllGather (IPC handles): %s", nccl_err(n, r));
+        }
+        if (e == cudaSuccess && rc == KD_ATTN_OK)
+            e = cudaMemcpyAsync(all.data(), dev + sizeof mine, sizeof mine * R, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && rc == KD_ATTN_OK) e = cudaStreamSynchronize(s);
+        for (int i = 0; e == cudaSuccess && rc == KD_ATTN_OK && i < R; ++i)
+            if (i != ctx->rank)
+                e = cudaIpcOpenMemHandle(reinterpret_cast<void**>(&b.peer[i]), all[i], cudaIpcMemLazyEnablePeerAccess);
+        if (s) cudaStreamDestroy(s);
+        if (dev) cudaFree(dev);
+        if (e != cudaSuccess && rc == KD_ATTN_OK)
+            rc = fail(ctx, KD_ATTN_ERR_CUDA, "symmetric buffer setup failed: %s", cudaGetErrorString(e));
+        if (rc != KD_ATTN_OK) {
+            cudaGetLastError();
+            release_sym(ctx, b);
+            return rc;
+        }
+    }
+    ctx->sym.push_back(b);
+    *out = b.local;
+    return KD_ATTN_OK;
+}
+
+kd_attn_status kd_attn_symmetric_free(kd_attn_ctx* ctx, void* ptr, void* stream) {
+    if (!ctx || !ptr) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    for (size_t i = 0; i < ctx->sym.size(); ++i) {
+        if (ctx->sym[i].local != ptr) continue;
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        kd_attn_status rc;
+        // no rank may still be writing into any copy
+        if ((rc = rank_barrier(ctx, st))) return rc;
+        KD_CUDA(ctx, cudaStreamSynchronize(st));
+        release_sym(ctx, ctx->sym[i]);
+        ctx->sym.erase(ctx->sym.begin() + (long)i);
+        return KD_ATTN_OK;
+    }
+    return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "not a symmetric buffer of this context");
+}
+
+kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                              const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
+                                              const float* k_gain, float eps, const kd_rope3d* rope,
+                                              int32_t op_type, kd_tensor* out_full, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, out_full, "out_full"))) return rc;
+    const int R = ctx->n_ranks;
+    const int64_t C = (int64_t)n_head_local * R * kHeadDim;
+    if (n_head_local <= 0 || out_full->ne[0] != C || out_full->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out_full must be [n_head_local * n_ranks * 128, L, N]");
+    const size_t es = elt_size(out_full->type);
+    if (out_full->nb[0] != es || out_full->nb[2] < out_full->nb[1] * (size_t)out_full->ne[1])
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_full rows must be contiguous and sequences not overlapping");
+    const size_t extent = out_full->nb[2] * (size_t)(out_full->ne[2] - 1) + out_full->nb[1] * (size_t)(out_full->ne[1] - 1) +
+                          (size_t)C * es;
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    char* peers[kMaxPeers];
+    int np = 0;
+    const char* base = nullptr;
+    if (R > 1) {
+        kd_attn_ctx::SymBuf* b = find_sym(ctx, out_full->data, out_full->ne[1] * out_full->ne[2] ? extent : 0);
+        if (!b) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out_full must lie in a kd_attn_symmetric_alloc buffer");
+        for (int i = 0; i < R; ++i)
+            if (i != ctx->rank) peers[np++] = b->peer[i];
+        base = b->local;
+    }
+    // this rank's heads are columns [rank * n_head_local * 128, +n_head_local * 128) of every copy
+    kd_tensor cols = *out_full;
+    cols.data = static_cast<char*>(out_full->data) + (size_t)ctx->rank * n_head_local * kHeadDim * es;
+    cols.ne[0] = (int64_t)n_head_local * kHeadDim;
+    if ((rc = rank_barrier(ctx, st))) return rc;  // nobody still reads the previous contents
+    if ((rc = attention_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
+                             &cols, nullptr, st, base, peers, np)))
+        return rc;
+    return rank_barrier(ctx, st);  // every rank's rows have landed in every copy
 }
 
 kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard, kd_tensor* full, void* stream) {

@@ -27,6 +27,7 @@ enum : unsigned {
     kErrBadLaunch = 1u << 6,     // launch geometry the kernel does not support
     kErrTimeoutDrain = 1u << 7,  // in-flight copies / MMAs did not drain on the abort path
     kErrTimeoutList = 1u << 8,   // a unit's K/V tile list was never published / released
+    kErrTimeoutOut = 1u << 9,    // head-sharded copy-out: a unit's rows never published / slot never freed
 };
 
 struct DevCtl {

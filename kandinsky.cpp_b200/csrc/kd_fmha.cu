@@ -17,6 +17,9 @@
 //   warp 2      scheduler: takes the next unit and publishes it with the list
 //               of K/V tiles it must visit (tiles whose mask is entirely -inf
 //               for all 256 rows are never loaded), one unit ahead
+//   warp 3      head-sharded runs only: copies each finished unit's output rows
+//               (already stored locally, read back from L2) into every peer
+//               GPU's copy of the output, one coalesced row per instruction
 //   warps 4-7   softmax + correction + epilogue for Q tile 0 (TMEM lanes 0-127)
 //   warps 8-11  the same for Q tile 1
 //
@@ -77,11 +80,13 @@ constexpr int kSmemQ = 0;
 constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
 constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
 // q_full, q_empty, kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full, o_free,
-// list_full, list_empty, and drain
-constexpr int kNumBars = 2 + 2 * kStages + 14 + 1;
+// list_full, list_empty, drain, then kOutSlots each of out_full, out_empty
+constexpr int kOutSlots = 4;  // units published to the copy-out warp and not yet copied
+constexpr int kNumBars = 2 + 2 * kStages + 14 + 1 + 2 * kOutSlots;
 constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
-constexpr int kSmemUnit = kSmemTmemSlot + 16;               // unit, n_kept, lk_eff, last0, last1 per list buffer
-constexpr int kSmemList = (kSmemUnit + 10 * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
+// unit, n_kept, lk_eff, last0, last1 per list buffer, then the copy-out ring's unit per slot
+constexpr int kSmemUnit = kSmemTmemSlot + 16;
+constexpr int kSmemList = (kSmemUnit + (10 + kOutSlots) * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
 constexpr int kSmemTotal = kSmemList + 2 * kMaxKvTiles * 4;
 constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
 // threads that release a list buffer: producer warp, MMA warp, both softmax warpgroups
@@ -169,11 +174,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* list_full = s_full + 10;       // [2] unit descriptor + kept-tile list published
     uint64_t* list_empty = s_full + 12;      // [2] every consumer is done with that list buffer
     uint64_t* drain = s_full + 14;
+    uint64_t* out_full = s_full + 15;        // [kOutSlots] a unit's rows are stored locally (256 arrivals)
+    uint64_t* out_empty = out_full + kOutSlots;  // [kOutSlots] the copy-out warp is done with the slot
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
     int* s_unit = reinterpret_cast<int*>(smem + kSmemUnit);     // [2] unit index, -1 = no more work
     int* s_nkept = s_unit + 2;                                   // [2] kept K/V tiles of the unit
     int* s_lkeff = s_unit + 4;                                   // [2] valid keys of the unit's sequence
     int* s_last = s_unit + 6;                                    // [2][2] last list entry Q tile i needs, -1: none
+    int* s_out_unit = s_unit + 10;                               // [kOutSlots] unit to copy out, -1 = finished
     uint32_t* lists = reinterpret_cast<uint32_t*>(smem + kSmemList);  // [2][kMaxKvTiles]
 
     if (threadIdx.x == 0) {
@@ -193,6 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&list_empty[i], kListConsumers);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < kOutSlots; ++i) {
+            mbar_init(&out_full[i], 2 * kBlockM);
+            mbar_init(&out_empty[i], 1);
+        }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -208,6 +220,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Without a mask every listed K/V tile is needed by both Q tiles; the dense instantiation folds
     // the per-Q-tile skip tests away.
     auto need = [](uint32_t entry, int i) { return !kSparse || tile_needed(entry, i); };
+    // Softmax threads: after storing their rows of the t-th unit (or -1 = no more units), wait for
+    // the ring slot to be free and arrive on out_full; thread 128 writes the unit index first.
+    auto publish_out = [&](int t, int u) -> bool {
+        const int slot = t % kOutSlots;
+        if (t >= kOutSlots &&
+            !__all_sync(0xffffffffu, mbar_wait(&out_empty[slot], ((t / kOutSlots) - 1) & 1, ctl, kErrTimeoutOut)))
+            return false;
+        if (threadIdx.x == 128) s_out_unit[slot] = u;
+        mbar_arrive(&out_full[slot]);
+        return true;
+    };
 
 
     if (warp == 2) {
@@ -508,6 +531,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             commit(drain);
             mbar_wait(drain, 0, ctl, kErrTimeoutDrain, false);
         }
+    } else if (warp == 3) {
+        // ------------------------------------------------------------ head-sharded copy-out
+        // Each finished unit's rows (256 rows of 128 outputs of one head) are read back from this
+        // GPU's output (L2-resident: just written) and stored into every peer GPU's copy at the same
+        // offset.  A row is 256 or 512 bytes; 16 bytes per lane, so one instruction moves one (f32)
+        // or two (16-bit) whole rows: NVLink sees full contiguous rows, and the softmax warps never
+        // wait on remote memory.
+        if (p.n_peer_out) {
+            constexpr int kChunks = kHeadDim * (int)sizeof(TO) / 16;  // 16-byte chunks per row
+            constexpr int kRowsPerInstr = 32 / kChunks;
+            constexpr int kBatch = 8;                                  // instructions of loads in flight
+            const int chunk = lane % kChunks, sub = lane / kChunks;
+            for (int t = 0;; ++t) {
+                const int slot = t % kOutSlots;
+                if (!__all_sync(0xffffffffu, mbar_wait(&out_full[slot], (t / kOutSlots) & 1, ctl, kErrTimeoutOut)))
+                    break;
+                const int u = s_out_unit[slot];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&out_empty[slot]);  // the unit index has been read
+                if (u < 0) break;
+                const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+                const int row0 = qblk * kRowsPerCta;
+                const int rows = min(kRowsPerCta, p.Lq - row0);
+                const long long base = (long long)n * p.o_nb3 + (long long)h * p.o_nb1 + (long long)chunk * 16;
+                for (int r0 = 0; r0 < rows; r0 += kBatch * kRowsPerInstr) {
+                    uint4 v[kBatch];
+#pragma unroll
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int row = r0 + i * kRowsPerInstr + sub;
+                        if (row < rows)
+                            v[i] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const char*>(p.out) + base +
+                                                                         (long long)(row0 + row) * p.o_nb2));
+                    }
+#pragma unroll 1
+                    for (int d = 0; d < p.n_peer_out; ++d) {
+#pragma unroll
+                        for (int i = 0; i < kBatch; ++i) {
+                            const int row = r0 + i * kRowsPerInstr + sub;
+                            if (row < rows)
+                                *reinterpret_cast<uint4*>(p.peer_out[d] + base + (long long)(row0 + row) * p.o_nb2) = v[i];
+                        }
+                    }
+                }
+            }
+            // the peers' copies are complete and visible system-wide before this CTA retires
+            __threadfence_system();
+        }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax / correction / epilogue
         const int wg = (warp - 4) >> 2;
@@ -520,7 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t g = 0;      // tiles this Q tile needed so far: phase of s_full / p_full
         uint32_t units = 0;  // units in which this Q tile had work: phase of o_full / o_free
         bool ok = true;
-        for (int t = 0; ok; ++t) {
+        int t = 0;  // units taken (the last, u < 0, ends the loop): also the copy-out ring position
+        for (; ok; ++t) {
             const int b = t & 1;
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
             const int u = s_unit[b];
@@ -702,7 +773,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (row_valid && p.lse)
                 p.lse[((long long)n * p.H + h) * p.Lq + qrow] = (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+            // head sharding: hand the unit's locally stored rows to the copy-out warp
+            if (p.n_peer_out && !(ok = publish_out(t, u))) break;
         }
+        // tell the copy-out warp there are no more units (after an abort it leaves on its own)
+        if (ok && p.n_peer_out) publish_out(t, -1);
     }
 
     tc_fence_before();

@@ -18,6 +18,7 @@ constexpr int kQTiles = 2;     // Q tiles per CTA, one softmax warpgroup each
 constexpr int kRowsPerCta = kBlockM * kQTiles;
 constexpr int kBlockN = 128;   // keys per K/V tile
 constexpr int kMaxKvTiles = 2048;  // per-unit kept-tile list capacity (Lk <= 262144)
+constexpr int kMaxPeers = 7;       // other ranks an output row is also written to (8 GPUs)
 
 struct FmhaParams {
     int Lq, Lk, H, N;        // query rows, keys, heads, sequences
@@ -39,6 +40,10 @@ struct FmhaParams {
     int num_ctas;            // persistent grid size (number of SMs)
     unsigned long long wait_ns;
     unsigned long long* tile_stats;  // [2] or null: K/V tiles loaded, (Q tile, K/V tile) pairs computed
+    // Head-sharded output exchange: every output row is also stored at the same byte offset from
+    // each of these bases (other GPUs' copies of the output, mapped into this process).
+    char* peer_out[kMaxPeers];
+    int n_peer_out;
 };
 
 enum class OpType { F16, BF16 };

@@ -40,7 +40,8 @@ EXPORTED = [
     "kd_attn_prologue", "kd_attn_flash_ext", "kd_attn_self_attention", "kd_attn_cross_attention",
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
     "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
-    "kd_attn_tile_stats", "kd_attn_set_log_callback",
+    "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
+    "kd_attn_self_attention_sharded",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -147,6 +148,13 @@ def _load():
     L.kd_attn_flash_ext_noalloc.argtypes = [T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P,
                                             P]
     L.kd_attn_flash_ext_noalloc.restype = st
+    L.kd_attn_symmetric_alloc.argtypes = [P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+    L.kd_attn_symmetric_alloc.restype = st
+    L.kd_attn_symmetric_free.argtypes = [P, P, P]
+    L.kd_attn_symmetric_free.restype = st
+    L.kd_attn_self_attention_sharded.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
+                                                 ctypes.POINTER(Rope3D), ctypes.c_int32, T, P]
+    L.kd_attn_self_attention_sharded.restype = st
     L.kd_attn_tile_stats.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
     L.kd_attn_tile_stats.restype = st
     L.kd_attn_set_log_callback.argtypes = [LOG_CB, P]
@@ -209,6 +217,24 @@ def _ptr(t):
 
 def _ref(t):
     return None if t is None else ctypes.byref(KdTensor.of(t))
+
+
+class _DeviceBuffer:
+    """__cuda_array_interface__ over library-owned device memory, so torch can view it without a copy."""
+
+    def __init__(self, ptr, shape, dtype, device):
+        self.ptr, self.shape, self.dtype, self.device = ptr, shape, dtype, device
+
+    def tensor(self):
+        import torch
+        if self.dtype == torch.bfloat16:   # no bf16 typestr: view 16-bit storage, reinterpret
+            t = _DeviceBuffer(self.ptr, self.shape, torch.int16, self.device).tensor()
+            return t.view(torch.bfloat16)
+        self.__cuda_array_interface__ = {"shape": self.shape, "typestr": {torch.float32: "<f4", torch.float16: "<f2",
+                                                                         torch.int16: "<i2"}[self.dtype],
+                                         "data": (self.ptr, False), "version": 3, "strides": None}
+        with torch.cuda.device(self.device):
+            return torch.as_tensor(self, device=f"cuda:{self.device}")
 
 
 class Context:
@@ -325,6 +351,32 @@ class Context:
                                                _ptr(q_gain), _ptr(k_gain), float(eps), _ref(mask), _ptr(kv_len),
                                                int(op_type), _ref(out), _ptr(lse), _stream_ptr(stream)))
         return out
+
+    def symmetric_tensor(self, shape, dtype):
+        """kd_attn_symmetric_alloc (collective): a device tensor whose copies on every rank are mapped
+        into each other, for self_attention_sharded's out_full.  Freed by symmetric_free or close()."""
+        import torch
+        n = 1
+        for s_ in shape:
+            n *= int(s_)
+        nbytes = n * torch.empty((), dtype=dtype).element_size()
+        ptr = ctypes.c_void_p()
+        self.check(lib.kd_attn_symmetric_alloc(self.handle, nbytes, ctypes.byref(ptr)))
+        return _DeviceBuffer(ptr.value, tuple(int(x) for x in shape), dtype, self.device).tensor()
+
+    def symmetric_free(self, t, stream=None):
+        """kd_attn_symmetric_free (collective)."""
+        self.check(lib.kd_attn_symmetric_free(self.handle, ctypes.c_void_p(t.data_ptr()), _stream_ptr(stream)))
+
+    def self_attention_sharded(self, q_in, k_in, v_in, n_head_local, out_full, rope=None, q_gain=None, k_gain=None,
+                               eps=1e-6, op_type=BF16, stream=None):
+        """This rank's column shard (N, L, n_head_local*128) f32 of the projections -> every rank's
+        out_full (N, L, n_ranks*n_head_local*128), the exchange fused into the flash epilogue."""
+        self.check(lib.kd_attn_self_attention_sharded(self.handle, _ref(q_in), _ref(k_in), _ref(v_in),
+                                                      int(n_head_local), _ptr(q_gain), _ptr(k_gain), float(eps),
+                                                      None if rope is None else ctypes.byref(rope), int(op_type),
+                                                      _ref(out_full), _stream_ptr(stream)))
+        return out_full
 
     def allgather_heads(self, shard, full, stream=None):
         """shard: (N, Lq, H/n, 128) -> full: (N, Lq, H, 128), one NCCL all-gather + permute."""

@@ -70,3 +70,62 @@ def test_two_gpu_head_sharding_matches_single_gpu(tmp_path):
     mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     r = torch.load(os.path.join(str(tmp_path), "r0.pt"))
     assert torch.equal(r["got"], r["ref"])
+
+
+def _rank_main_fused(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "kandinsky.cpp_b200"))
+    import kd_attn
+    from kd_attn.sharding import column_shard
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank), timeout=datetime.timedelta(seconds=60))
+    obj = [kd_attn.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    N, H, d, grid = 2, 8, 128, (4, 16, 16)
+    L, C = grid[0] * grid[1] * grid[2], H * d
+    rope = kd_attn.Rope3D.make(grid, scale=(1, 2, 2))
+    res = {}
+    with kd_attn.Context(device=rank, n_ranks=world, rank=rank, nccl_id=obj[0]) as ctx:
+        full_in = []
+        for off in range(3):
+            t = torch.empty(N * L * C, device="cuda")
+            ctx.fill_randn(t, seed=78, offset=off)
+            full_in.append(t.view(N, L, C))
+        shard_in = [column_shard(x, rank, world, H).contiguous() for x in full_in]
+        Hs = H // world
+        for dt in (torch.float32, torch.bfloat16):
+            out_full = ctx.symmetric_tensor((N, L, C), dt)
+            out_full.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[rank])
+            for _ in range(2):    # the second call overwrites the first in place
+                ctx.self_attention_sharded(*shard_in, Hs, out_full, rope=rope, op_type=kd_attn.BF16)
+            ctx.device_status()
+            with kd_attn.Context(device=rank) as single:
+                ref = torch.empty(N, L, C, device="cuda", dtype=dt)
+                single.self_attention(*full_in, H, ref, rope=rope, op_type=kd_attn.BF16)
+                single.device_status()
+            res[str(dt)] = (out_full.cpu(), ref.cpu())
+            ctx.symmetric_free(out_full)
+    torch.save(res, os.path.join(out_dir, f"fused_r{rank}.pt"))
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+def test_two_gpu_fused_exchange_matches_single_gpu(tmp_path):
+    """kd_attn_self_attention_sharded: each rank's flash epilogue stores its heads into both ranks'
+    symmetric out_full; every rank must end with the full single-GPU result, bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_rank_main_fused, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        res = torch.load(os.path.join(str(tmp_path), f"fused_r{r}.pt"))
+        for got, ref in res.values():
+            assert torch.equal(got, ref)
