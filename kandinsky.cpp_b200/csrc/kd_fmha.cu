@@ -122,6 +122,34 @@ static_assert(kSmemAlloc <= 232448, "shared memory budget");
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO* dst, const float (&v)[32]);
 
+// 32 bytes per store instruction (st.global.v8.b32): a lane writes whole 32-byte sectors of its row.
+// dst must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* dst, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
+                                             uint32_t a5, uint32_t a6, uint32_t a7) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(a0), "r"(a1), "r"(a2),
+                 "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+                 : "memory");
+}
+template <typename TO>
+__device__ __forceinline__ void store_row32_v8(TO* dst, const float (&v)[32]);
+template <>
+__device__ __forceinline__ void store_row32_v8<float>(float* dst, const float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        st_global_v8(dst + 8 * i, __float_as_uint(v[8 * i]), __float_as_uint(v[8 * i + 1]), __float_as_uint(v[8 * i + 2]),
+                     __float_as_uint(v[8 * i + 3]), __float_as_uint(v[8 * i + 4]), __float_as_uint(v[8 * i + 5]),
+                     __float_as_uint(v[8 * i + 6]), __float_as_uint(v[8 * i + 7]));
+}
+template <typename TO>
+__device__ __forceinline__ void store_row32_v8(TO* dst, const float (&v)[32]) {  // 16-bit outputs
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        st_global_v8(dst + 16 * i, Pack2<TO>::pack(v[16 * i], v[16 * i + 1]), Pack2<TO>::pack(v[16 * i + 2], v[16 * i + 3]),
+                     Pack2<TO>::pack(v[16 * i + 4], v[16 * i + 5]), Pack2<TO>::pack(v[16 * i + 6], v[16 * i + 7]),
+                     Pack2<TO>::pack(v[16 * i + 8], v[16 * i + 9]), Pack2<TO>::pack(v[16 * i + 10], v[16 * i + 11]),
+                     Pack2<TO>::pack(v[16 * i + 12], v[16 * i + 13]), Pack2<TO>::pack(v[16 * i + 14], v[16 * i + 15]));
+}
+
 template <>
 __device__ __forceinline__ void store_row32<float>(float* dst, const float (&v)[32]) {
     float4* d = reinterpret_cast<float4*>(dst);
@@ -761,7 +789,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float v[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[c * 32 + i]) * inv;
-                        store_row32<TO>(orow + c * 32, v);
+                        if (p.out_v8)
+                            store_row32_v8<TO>(orow + c * 32, v);
+                        else
+                            store_row32<TO>(orow + c * 32, v);
                     }
                 }
             } else if (orow) {

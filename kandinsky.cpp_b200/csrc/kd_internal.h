@@ -44,6 +44,7 @@ struct FmhaParams {
     // each of these bases (other GPUs' copies of the output, mapped into this process).
     char* peer_out[kMaxPeers];
     int n_peer_out;
+    int out_v8;              // 1: out rows are 32-byte aligned (256-bit stores in the epilogue)
 };
 
 enum class OpType { F16, BF16 };
