@@ -89,22 +89,26 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 50 ms while the timed region runs
-    (entering waits for the first sample, so sampling is live when timing starts)."""
+    """nvidia-smi clocks / throttle reasons of the job's GPUs, sampled every 100 ms while the timed
+    region runs (entering waits for the first sample, so sampling is live when timing starts).  One
+    process per node, started by local rank 0 for all of the node's GPUs: one poller per rank
+    perturbed 8-GPU steps measurably."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
-        self.device = device
+    def __init__(self, devices):
+        self.devices = list(devices)   # nvidia-smi indices; empty = this rank does not sample
         self.proc = None
         self.lines = []
 
     def __enter__(self):
+        if not self.devices:
+            return self
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", ",".join(str(d) for d in self.devices),
+                                          f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -149,6 +153,14 @@ class ClockSampler:
         sm.sort()
         med = sm[len(sm) // 2] if sm else None
         return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def node_gpus(local, ws):
+    """nvidia-smi indices of the GPUs this node's ranks use (rank i on cuda:i, through CUDA_VISIBLE_DEVICES)."""
+    per_node = int(os.environ.get("LOCAL_WORLD_SIZE", str(ws)))
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [v.strip() for v in vis.split(",")] if vis else [str(i) for i in range(per_node)]
+    return ids[:per_node]
 
 
 def dist_setup():
@@ -469,7 +481,10 @@ def main():
     ctx.device_status()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(node_gpus(local, ws) if local == 0 else []) as clk:
+        # the sampler starts on local rank 0 only: align every rank after it is live, so no rank's
+        # timed region contains another rank's sampler start-up
+        barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
