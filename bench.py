@@ -371,6 +371,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (profiling runs)")
     ap.add_argument("--heads", type=int, default=None, help="override the config's head count (profiling runs)")
+    ap.add_argument("--frames", type=int, default=None,
+                    help="override the config's number of latent frames (grid[0]; profiling runs)")
     ap.add_argument("--fa-only", action="store_true",
                     help="time only the flash-attention kernel on prologue-made operands (profiling runs)")
     args = ap.parse_args()
@@ -379,8 +381,10 @@ def main():
         cfg["N"] = args.batch
     if args.heads:
         cfg["H"] = args.heads
-    if args.batch or args.heads:
-        cfg["name"] += f" [override B{cfg['N']} H{cfg['H']}]"
+    if args.frames:
+        cfg["grid"] = (args.frames,) + tuple(cfg["grid"][1:])
+    if args.batch or args.heads or args.frames:
+        cfg["name"] += f" [override B{cfg['N']} H{cfg['H']} grid {'x'.join(str(g) for g in cfg['grid'])}]"
 
     if args.impl == "reference":
         run_reference(args, cfg)
