@@ -451,6 +451,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         mp.mask = a.mask ? static_cast<const uint16_t*>(a.mask->data) : nullptr;
         mp.bits = a.tile_mask;
         mp.bits_row_bytes = (n_kb + 7) / 8;
+        mp.vec16 = (a.mask && aligned16(a.mask->data) && mnb[1] % 16 == 0 && mnb[2] % 16 == 0 && mnb[3] % 16 == 0) ? 1 : 0;
         mp.nb1 = (long long)mnb[1];
         mp.nb2 = (long long)mnb[2];
         mp.nb3 = (long long)mnb[3];

@@ -529,11 +529,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (more) e_next = list[j + 1];
                 if (!(ok = next_stage(sV))) break;
                 KD_TRACE(1, 0, gq0);
+                int sK2 = -1;
+                bool early0 = false, early1 = false;
+                // Masked lists: a Q tile with no PV at this K/V tile has nothing to wait for, so its
+                // next S is issued before the other Q tile's PV (which waits on that tile's softmax)
+                // and the tensor core keeps working.  Its previous PV is already queued ahead of it.
+                if (kSparse && more) {
+                    early0 = !need(e, 0) && need(e_next, 0);
+                    early1 = !need(e, 1) && need(e_next, 1);
+                    if (early0 || early1) {
+                        if (!(ok = next_stage(sK2))) break;
+                        if (early0) {
+                            issue_s(0, sK2);
+                            commit(&s_full[0]);
+                        }
+                        if (early1) {
+                            issue_s(1, sK2);
+                            commit(&s_full[1]);
+                        }
+                    }
+                }
                 if (need(e, 0) && !(ok = pv_tile(0, j, first0, gq0, uq0, last0))) break;
-                int sK2 = 0;
                 if (more) {
-                    if (!(ok = next_stage(sK2))) break;
-                    if (need(e_next, 0)) {
+                    if (sK2 < 0 && !(ok = next_stage(sK2))) break;
+                    if (!early0 && need(e_next, 0)) {
                         issue_s(0, sK2);
                         commit(&s_full[0]);
                     }
@@ -541,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1))) break;
                 commit(&kv_empty[sV]);
                 if (more) {
-                    if (need(e_next, 1)) {
+                    if (!early1 && need(e_next, 1)) {
                         issue_s(1, sK2);
                         commit(&s_full[1]);
                     }

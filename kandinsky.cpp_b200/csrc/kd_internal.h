@@ -106,6 +106,7 @@ struct MaskClassParams {
     const uint16_t* mask;            // or null (bitmap only, one plane)
     const uint8_t* bits;             // or null: bit kb of row qb (rows of bits_row_bytes bytes)
     int bits_row_bytes;
+    int vec16;                       // 1: mask base and row stride are 16-byte aligned (vector loads)
     long long nb1, nb2, nb3;         // byte strides (query row, head plane, sequence plane)
     int Lq, Lk, mh, mn;
     uint8_t* cls;                    // [mn][mh][n_qb][n_kb]

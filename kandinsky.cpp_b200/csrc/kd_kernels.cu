@@ -164,6 +164,27 @@ __global__ void __launch_bounds__(256) mask_classify_kernel(const MaskClassParam
         }
         const int mhi = plane % p.mh, mni = plane / p.mh;
         const char* base = reinterpret_cast<const char*>(p.mask) + (long long)mni * p.nb3 + (long long)mhi * p.nb2;
+        if (p.vec16 && (qb + 1) * 64 <= p.Lq && (kb + 1) * 64 <= p.Lk) {
+            // Interior tile, 16-byte aligned rows: lane reads 8 values (16 B) of a row, 4 rows per
+            // warp load, and folds them into a running OR and AND of the 32-bit words.  All -inf
+            // <=> AND == OR == 0xFC00FC00; all +-0 <=> (OR & 0x7FFF7FFF) == 0.
+            const int rsub = lane >> 3, c16 = lane & 7;
+            const char* t0 = base + (long long)(qb * 64 + rsub) * p.nb1 + (long long)kb * 128 + c16 * 16;
+            uint32_t vor = 0u, vand = 0xFFFFFFFFu;
+#pragma unroll 8
+            for (int r0 = 0; r0 < 64; r0 += 4) {
+                const uint4 w = __ldg(reinterpret_cast<const uint4*>(t0 + (long long)r0 * p.nb1));
+                vor |= w.x | w.y | w.z | w.w;
+                vand &= w.x & w.y & w.z & w.w;
+            }
+            vor = __reduce_or_sync(0xffffffffu, vor);
+            vand = __reduce_and_sync(0xffffffffu, vand);
+            if (lane == 0)
+                p.cls[t] = (vand == 0xFC00FC00u && vor == 0xFC00FC00u)
+                               ? kTileSkip
+                               : ((vor & 0x7FFF7FFFu) == 0u ? kTileFull : kTileMixed);
+            continue;
+        }
         const int key = kb * 64 + 2 * lane;
         const int rows = min(64, p.Lq - qb * 64);
         bool all_inf = true, all_zero = true;
