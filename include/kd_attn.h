@@ -292,6 +292,15 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
                                               const float* k_gain, float eps, const kd_rope3d* rope,
                                               int32_t op_type, kd_tensor* out_full, void* stream);
 
+/* The same for DiTCrossAttention::forward (crossdit.hpp:186-198): this rank's heads of the
+ * visual queries against the text keys/values (column shards of k_in/v_in), no RoPE, the
+ * optional mask / kv_len of kd_attn_cross_attention, every row exchanged in the flash epilogue. */
+kd_attn_status kd_attn_cross_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                               const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
+                                               const float* k_gain, float eps, const kd_tensor* mask,
+                                               const int32_t* kv_len, int32_t op_type, kd_tensor* out_full,
+                                               void* stream);
+
 /* ---------------------------------------------------------------------------
  * Seeded N(0,1) fill on the device: Philox4x32-10 + Box-Muller with the
  * counter layout of PhiloxRNG::randn (src/rng.hpp:51-69): element i of a call

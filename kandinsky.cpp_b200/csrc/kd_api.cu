@@ -1123,11 +1123,16 @@ kd_attn_status kd_attn_symmetric_free(kd_attn_ctx* ctx, void* ptr, void* stream)
     return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "not a symmetric buffer of this context");
 }
 
-kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
-                                              const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
-                                              const float* k_gain, float eps, const kd_rope3d* rope,
-                                              int32_t op_type, kd_tensor* out_full, void* stream) {
-    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+}  // extern "C"
+
+namespace {
+
+// Head-sharded attention into a symmetric out_full: barrier, this rank's heads (prologue + flash whose
+// copy-out warp also stores every row into the other ranks' copies), barrier.
+kd_attn_status sharded_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
+                            int32_t n_head_local, const float* q_gain, const float* k_gain, float eps,
+                            const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
+                            kd_tensor* out_full, cudaStream_t st) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, out_full, "out_full"))) return rc;
     const int R = ctx->n_ranks;
@@ -1139,8 +1144,6 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_full rows must be contiguous and sequences not overlapping");
     const size_t extent = out_full->nb[2] * (size_t)(out_full->ne[2] - 1) + out_full->nb[1] * (size_t)(out_full->ne[1] - 1) +
                           (size_t)C * es;
-    DeviceGuard g(ctx->device);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     char* peers[kMaxPeers];
     int np = 0;
     const char* base = nullptr;
@@ -1156,10 +1159,35 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
     cols.data = static_cast<char*>(out_full->data) + (size_t)ctx->rank * n_head_local * kHeadDim * es;
     cols.ne[0] = (int64_t)n_head_local * kHeadDim;
     if ((rc = rank_barrier(ctx, st))) return rc;  // nobody still reads the previous contents
-    if ((rc = attention_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
+    if ((rc = attention_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, rope, mask, kv_len, op_type,
                              &cols, nullptr, st, base, peers, np)))
         return rc;
     return rank_barrier(ctx, st);  // every rank's rows have landed in every copy
+}
+
+}  // namespace
+
+extern "C" {
+
+kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                              const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
+                                              const float* k_gain, float eps, const kd_rope3d* rope,
+                                              int32_t op_type, kd_tensor* out_full, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return sharded_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
+                        out_full, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_cross_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                               const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,
+                                               const float* k_gain, float eps, const kd_tensor* mask,
+                                               const int32_t* kv_len, int32_t op_type, kd_tensor* out_full,
+                                               void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return sharded_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, nullptr, mask, kv_len, op_type,
+                        out_full, static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard, kd_tensor* full, void* stream) {

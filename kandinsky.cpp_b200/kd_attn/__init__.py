@@ -41,7 +41,7 @@ EXPORTED = [
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
     "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
-    "kd_attn_self_attention_sharded",
+    "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -155,6 +155,9 @@ def _load():
     L.kd_attn_self_attention_sharded.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
                                                  ctypes.POINTER(Rope3D), ctypes.c_int32, T, P]
     L.kd_attn_self_attention_sharded.restype = st
+    L.kd_attn_cross_attention_sharded.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float, T, P,
+                                                  ctypes.c_int32, T, P]
+    L.kd_attn_cross_attention_sharded.restype = st
     L.kd_attn_tile_stats.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
     L.kd_attn_tile_stats.restype = st
     L.kd_attn_set_log_callback.argtypes = [LOG_CB, P]
@@ -205,10 +208,6 @@ def _stream_ptr(stream):
         import torch
         stream = torch.cuda.current_stream()
     return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
-
-
-def torch_dtype_name(t):
-    return str(t.dtype)
 
 
 def _ptr(t):
@@ -295,8 +294,7 @@ class Context:
                     stream=None):
         """One launch: q_in/k_in (N, L, C) f32 -> RMSNorm (+RoPE) -> q_out/k_out (N, H, L, 128); v_in -> v_out
         cast only.  Any (in, out) pair may be None."""
-        types = {torch_dtype_name(t) for t in (q_out, k_out, v_out) if t is not None}
-        if len(types) != 1:
+        if len({t.dtype for t in (q_out, k_out, v_out) if t is not None}) != 1:
             raise ValueError("outputs must share one dtype")
         out_dtype = KdTensor.of(next(t for t in (q_out, k_out, v_out) if t is not None)).type
         self.check(lib.kd_attn_qk_prologue(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), _ptr(q_gain),
@@ -376,6 +374,15 @@ class Context:
                                                       int(n_head_local), _ptr(q_gain), _ptr(k_gain), float(eps),
                                                       None if rope is None else ctypes.byref(rope), int(op_type),
                                                       _ref(out_full), _stream_ptr(stream)))
+        return out_full
+
+    def cross_attention_sharded(self, q_in, k_in, v_in, n_head_local, out_full, mask=None, kv_len=None,
+                                q_gain=None, k_gain=None, eps=1e-6, op_type=BF16, stream=None):
+        """Cross-attention on this rank's heads -> every rank's out_full (exchange fused as above)."""
+        self.check(lib.kd_attn_cross_attention_sharded(self.handle, _ref(q_in), _ref(k_in), _ref(v_in),
+                                                       int(n_head_local), _ptr(q_gain), _ptr(k_gain), float(eps),
+                                                       _ref(mask), _ptr(kv_len), int(op_type), _ref(out_full),
+                                                       _stream_ptr(stream)))
         return out_full
 
     def allgather_heads(self, shard, full, stream=None):

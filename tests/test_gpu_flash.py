@@ -347,3 +347,34 @@ def test_qk_prologue_one_launch_equals_separate_calls(ctx, kd, Lq, Lk):
         ctx.qk_prologue(None, k, v, None, *only_kv, k_gain=gk, rope=rope)
         ctx.device_status()
         assert torch.equal(only_kv[0], ref[1]) and torch.equal(only_kv[1], ref[2])
+
+
+def test_sharded_entry_points_on_one_rank(ctx, kd):
+    """With one rank the sharded calls are the plain ones into out_full (no peers, barriers no-ops):
+    self- and cross-attention bit-identical to kd_attn_self_attention / kd_attn_cross_attention, into
+    a symmetric buffer and into an ordinary tensor."""
+    N, H, grid = 2, 4, (2, 8, 8)
+    L, Lt, C = 128, 77, 4 * 128
+    rope = kd.Rope3D.make(grid)
+    q = dev(seeded((N, L, C), 81, 0))
+    k = dev(seeded((N, L, C), 81, 1))
+    v = dev(seeded((N, L, C), 81, 2))
+    kt = dev(seeded((N, Lt, C), 81, 3))
+    vt = dev(seeded((N, Lt, C), 81, 4))
+    kv_len = torch.tensor([77, 30], dtype=torch.int32, device="cuda")
+    ref_self = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+    ctx.self_attention(q, k, v, H, ref_self, rope=rope, op_type=kd.BF16)
+    ref_cross = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+    ctx.cross_attention(q, kt, vt, H, ref_cross, kv_len=kv_len, op_type=kd.BF16)
+    sym = ctx.symmetric_tensor((N, L, C), torch.bfloat16)
+    plain = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+    for out in (sym, plain):
+        out.fill_(7.0)
+        ctx.self_attention_sharded(q, k, v, H, out, rope=rope, op_type=kd.BF16)
+        ctx.device_status()
+        assert torch.equal(out, ref_self)
+        out.fill_(7.0)
+        ctx.cross_attention_sharded(q, kt, vt, H, out, kv_len=kv_len, op_type=kd.BF16)
+        ctx.device_status()
+        assert torch.equal(out, ref_cross)
+    ctx.symmetric_free(sym)

@@ -110,6 +110,24 @@ def _rank_main_fused(rank, world, port, out_dir):
                 single.self_attention(*full_in, H, ref, rope=rope, op_type=kd_attn.BF16)
                 single.device_status()
             res[str(dt)] = (out_full.cpu(), ref.cpu())
+            # cross-attention against text states of 77 tokens, valid lengths per sequence
+            Lt = 77
+            kt = torch.empty(N * Lt * C, device="cuda"); ctx.fill_randn(kt, seed=79, offset=0)
+            vt = torch.empty(N * Lt * C, device="cuda"); ctx.fill_randn(vt, seed=79, offset=1)
+            kt, vt = kt.view(N, Lt, C), vt.view(N, Lt, C)
+            kv_len = torch.tensor([77, 40], dtype=torch.int32, device="cuda")
+            out_full.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[rank])
+            ctx.cross_attention_sharded(shard_in[0], column_shard(kt, rank, world, H).contiguous(),
+                                        column_shard(vt, rank, world, H).contiguous(), Hs, out_full, kv_len=kv_len,
+                                        op_type=kd_attn.BF16)
+            ctx.device_status()
+            with kd_attn.Context(device=rank) as single:
+                ref = torch.empty(N, L, C, device="cuda", dtype=dt)
+                single.cross_attention(full_in[0], kt, vt, H, ref, kv_len=kv_len, op_type=kd_attn.BF16)
+                single.device_status()
+            res[str(dt) + " cross"] = (out_full.cpu(), ref.cpu())
             ctx.symmetric_free(out_full)
     torch.save(res, os.path.join(out_dir, f"fused_r{rank}.pt"))
     dist.barrier(device_ids=[rank])
