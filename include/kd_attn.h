@@ -17,7 +17,10 @@
  *   - the caller owns every buffer passed in; the library never frees them;
  *   - device pointers only in kd_tensor.data (except where noted), work is
  *     enqueued on the given cudaStream_t (passed as void*), nothing blocks;
- *   - a context may be used from one host thread at a time;
+ *   - a context may be used from one host thread at a time, and its calls share
+ *     the context's device scratch: issue them on one stream, or order calls on
+ *     different streams with events (the host-buffer call orders its own copy
+ *     streams after the given stream);
  *   - there is no CPU fallback: shapes the kernels do not cover return
  *     KD_ATTN_ERR_UNSUPPORTED and the caller keeps its own path;
  *   - kd_tensor mirrors ggml_tensor's {type, ne[4], nb[4], data}, sizes in
