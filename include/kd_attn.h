@@ -230,6 +230,18 @@ kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k,
  * q_in, k_in, v_in : [C = n_head*128, L, N] f32
  * op_type          : operand type, KD_ATTN_TYPE_F16 (ggml semantics) or BF16
  * out              : [C, Lq, N] f32 | bf16 */
+/* ops::attention's flash branch as it stands (ops.hpp:107-185,204-206), for
+ * callers that apply no RMSNorm / RoPE first: q_in [n_head*128, Lq, N], k_in and
+ * v_in [n_kv_head*128, Lk, N] (f32, n_head % n_kv_head == 0: the GQA expansion of
+ * ops.hpp:135-157 is done by indexing, not by copies); Q, K and V are permuted and
+ * rounded to op_type (ops.hpp:122-131,167-169, f16 in ggml), then flash attention
+ * with scale 1/sqrt(128).  mask: NULL or f16 in ggml's flash orientation
+ * [>=Lk, >=Lq, mh, mn] (ops.hpp:171-174 transposes an [N, Lq, Lk] mask first; that
+ * branch is never reached by the CrossDiT call sites).  out [n_head*128, Lq, N]. */
+kd_attn_status kd_attn_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
+                                 const kd_tensor* v_in, int32_t n_head, const kd_tensor* mask,
+                                 int32_t op_type, kd_tensor* out, float* lse, void* stream);
+
 kd_attn_status kd_attn_self_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
                                       const kd_tensor* v_in, int32_t n_head, const float* q_gain,
                                       const float* k_gain, float eps, const kd_rope3d* rope,

@@ -665,7 +665,7 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
                               int32_t n_head, const float* q_gain, const float* k_gain, float eps,
                               const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
                               kd_tensor* out, float* lse, cudaStream_t st, const char* out_base = nullptr,
-                              char* const* peer_base = nullptr, int n_peers = 0) {
+                              char* const* peer_base = nullptr, int n_peers = 0, bool norm_qk = true) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
         (rc = check_tensor(ctx, v_in, "v_in")))
@@ -673,14 +673,20 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     if (op_type != KD_ATTN_TYPE_F16 && op_type != KD_ATTN_TYPE_BF16)
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "op_type must be f16 or bf16");
     const int64_t Lq = q_in->ne[1], N = q_in->ne[2], Lk = k_in->ne[1];
-    if (k_in->ne[2] != N || v_in->ne[1] != Lk || v_in->ne[2] != N || v_in->ne[0] != k_in->ne[0] ||
-        k_in->ne[0] != q_in->ne[0])
+    if (k_in->ne[2] != N || v_in->ne[1] != Lk || v_in->ne[2] != N || v_in->ne[0] != k_in->ne[0])
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
+    // K/V heads: k_in->ne[0] / 128, a divisor of n_head (grouped-query attention, ops.hpp:135-157)
+    if (k_in->ne[0] % kHeadDim)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k_in.ne[0] = %lld is not a multiple of 128", (long long)k_in->ne[0]);
+    const int64_t n_kv_head = k_in->ne[0] / kHeadDim;
+    if (n_kv_head <= 0 || n_head % n_kv_head)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "invalid GQA ratio n_head=%d n_kv_head=%lld", n_head,
+                    (long long)n_kv_head);
     kd_tensor ov;
     if ((rc = out_view(ctx, out, n_head, Lq, N, &ov))) return rc;
     const size_t es = 2;
     const size_t qb = align256((size_t)N * n_head * Lq * kHeadDim * es);
-    const size_t kb = align256((size_t)N * n_head * Lk * kHeadDim * es);
+    const size_t kb = align256((size_t)N * n_kv_head * Lk * kHeadDim * es);
     // operand scratch sits after the flash core's own scratch needs: reserve them up front
     const size_t flash_extra =
         mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
@@ -688,10 +694,19 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     // The flash core carves its scratch from the start of the buffer; operands go after it.
     char* base = static_cast<char*>(ctx->scratch) + flash_extra;
     kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N);
-    kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_head, N);
-    kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_head, N);
-    const PrologueReq req[3] = {{q_in, 1, q_gain, true, &Qs}, {k_in, 1, k_gain, true, &Ks}, {v_in, 0, nullptr, false, &Vs}};
-    if ((rc = prologue_multi(ctx, req, 3, n_head, eps, rope, st))) return rc;
+    kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_kv_head, N);
+    kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_kv_head, N);
+    const int32_t nq = norm_qk ? 1 : 0;
+    if (n_kv_head == n_head) {
+        const PrologueReq req[3] = {{q_in, nq, q_gain, true, &Qs}, {k_in, nq, k_gain, true, &Ks},
+                                    {v_in, 0, nullptr, false, &Vs}};
+        if ((rc = prologue_multi(ctx, req, 3, n_head, eps, rope, st))) return rc;
+    } else {  // different head counts: Q in one launch, K and V in another
+        const PrologueReq rq[1] = {{q_in, nq, q_gain, true, &Qs}};
+        const PrologueReq rkv[2] = {{k_in, nq, k_gain, true, &Ks}, {v_in, 0, nullptr, false, &Vs}};
+        if ((rc = prologue_multi(ctx, rq, 1, n_head, eps, rope, st))) return rc;
+        if ((rc = prologue_multi(ctx, rkv, 2, (int32_t)n_kv_head, eps, rope, st))) return rc;
+    }
     FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, lse};
     fa.out_base = out_base;
     fa.peer_base = peer_base;
@@ -1040,6 +1055,15 @@ kd_attn_status kd_attn_self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_
     DeviceGuard g(ctx->device);
     return self_attention_host(ctx, q_in, k_in, v_in, n_head, q_gain, k_gain, eps, rope, op_type, out,
                                static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
+                                 int32_t n_head, const kd_tensor* mask, int32_t op_type, kd_tensor* out, float* lse,
+                                 void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return attention_core(ctx, q_in, k_in, v_in, n_head, nullptr, nullptr, 0.f, nullptr, mask, nullptr, op_type, out,
+                          lse, static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, /*norm_qk=*/false);
 }
 
 kd_attn_status kd_attn_cross_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
