@@ -41,7 +41,7 @@ EXPORTED = [
     "kd_attn_allgather_heads", "kd_attn_fill_randn", "kd_attn_nccl_unique_id", "kd_attn_version",
     "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
-    "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded",
+    "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -125,6 +125,8 @@ def _load():
     L.kd_attn_prologue.argtypes = [P, T, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_float,
                                    ctypes.POINTER(Rope3D), T, P]
     L.kd_attn_prologue.restype = st
+    L.kd_attn_attention.argtypes = [P, T, T, T, ctypes.c_int32, T, ctypes.c_int32, T, P, P]
+    L.kd_attn_attention.restype = st
     L.kd_attn_qk_prologue.argtypes = [P, T, T, T, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), ctypes.c_int32,
                                       T, T, T, P]
     L.kd_attn_qk_prologue.restype = st
@@ -321,6 +323,13 @@ class Context:
         self.check(lib.kd_attn_tile_stats(self.handle, _stream_ptr(stream), out, 1 if reset else 0))
         return int(out[0]), int(out[1])
 
+    def ops_attention(self, q_in, k_in, v_in, n_head, out, mask=None, op_type=F16, lse=None, stream=None):
+        """kd_attn_attention = ops::attention's flash branch: q_in (N, Lq, C), k_in/v_in (N, Lk, C_kv) f32
+        (GQA when C_kv < C), no RMSNorm/RoPE; mask f16 (mn, mh, >=Lq, >=Lk) or None; out (N, Lq, C)."""
+        self.check(lib.kd_attn_attention(self.handle, _ref(q_in), _ref(k_in), _ref(v_in), int(n_head), _ref(mask),
+                                         int(op_type), _ref(out), _ptr(lse), _stream_ptr(stream)))
+        return out
+
     def self_attention(self, q_in, k_in, v_in, n_head, out, rope=None, q_gain=None, k_gain=None, eps=1e-6,
                        op_type=BF16, lse=None, stream=None):
         """q_in/k_in/v_in: (N, L, C) f32 -> out (N, L, C) f32/bf16."""
@@ -429,21 +438,12 @@ def attention(ctx: Context, q, k, v, n_head, mask=None, flash=True, op_type=F16,
     if not flash:
         raise KdAttnError(ERR_UNSUPPORTED, "only the flash branch of ops::attention is implemented")
     N, Lq, C = q.shape
-    Lk = k.shape[1]
-    d = C // n_head
-    n_kv = k.shape[2] // d
-    dt = torch.float16 if op_type == F16 else torch.bfloat16
-    qh = q.view(N, Lq, n_head, d).permute(0, 2, 1, 3)           # strided view, rounded by the library
-    # K/V permute + cast (ops.hpp:127-131,167-169) in the library's prologue kernel, no norm/RoPE
-    kh = torch.empty(N, n_kv, Lk, d, device=q.device, dtype=dt)
-    vh = torch.empty(N, n_kv, Lk, d, device=q.device, dtype=dt)
-    ctx.prologue(k, n_kv, kh, norm=False, stream=stream)
-    ctx.prologue(v, n_kv, vh, norm=False, stream=stream)
-    out = torch.empty(N, Lq, n_head, d, device=q.device, dtype=out_dtype or torch.float32)
+    out = torch.empty(N, Lq, C, device=q.device, dtype=out_dtype or torch.float32)
     m = None
     if mask is not None:
         m = mask.to(torch.float16)
         while m.dim() < 4:
             m = m.unsqueeze(0)
-    ctx.flash_attn_ext(qh, kh, vh, out, mask=m, scale=1.0 / d ** 0.5, stream=stream)
-    return out.view(N, Lq, C)
+    # one kd_attn_attention call: permutes + casts in the prologue kernel, then flash attention
+    ctx.ops_attention(q, k, v, n_head, out, mask=m, op_type=op_type, stream=stream)
+    return out
