@@ -6,7 +6,8 @@
 //
 // Persistent: one CTA per SM takes "units" -- 2 x 128 query rows of one
 // (head, sequence) -- from a global counter in increasing order and streams
-// the K/V tiles of each unit's head through a 4-stage shared-memory ring:
+// the K/V tiles of each unit's head through a shared-memory ring (5 stages of one
+// 128 x 128 tile in the dense kernel, 4 plus the kept-tile lists in the masked one):
 //
 //   warp 0      TMA producer: Q0, Q1 per unit (as soon as the previous unit's
 //               last S MMA frees the Q buffer), then K_j, V_j (128 x 128 tiles,
@@ -71,24 +72,32 @@ __device__ unsigned long long kd_fmha_trace[4][8][512];
 
 namespace {
 
-constexpr int kStages = 4;
 constexpr int kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB: one 128 x 128 16-bit tile
 constexpr int kBoxBytes = kTileBytes / 2;           // one 128-row x 64-column box
 constexpr int kThreads = 384;
-
-constexpr int kSmemQ = 0;
-constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
-constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
-// q_full, q_empty, kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full, o_free,
-// list_full, list_empty, drain, then kOutSlots each of out_full, out_empty
 constexpr int kOutSlots = 4;  // units published to the copy-out warp and not yet copied
-constexpr int kNumBars = 2 + 2 * kStages + 14 + 1 + 2 * kOutSlots;
-constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
-// unit, n_kept, lk_eff, last0, last1 per list buffer, then the copy-out ring's unit per slot
-constexpr int kSmemUnit = kSmemTmemSlot + 16;
-constexpr int kSmemList = (kSmemUnit + (10 + kOutSlots) * 4 + 15) & ~15;  // 2 list buffers of kMaxKvTiles entries
-constexpr int kSmemTotal = kSmemList + 2 * kMaxKvTiles * 4;
-constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
+
+// Shared-memory layout of one instantiation.  The K/V ring gets every byte the 227 KB allow: the
+// masked kernel keeps two kept-tile lists (16 KB) and 4 stages; the dense kernel visits every tile
+// in order, needs no lists, and gets a 5th stage (its measured bottleneck was waiting for K/V
+// tiles to land with only 2 tiles of lookahead per Q tile pair).
+template <bool kSparse>
+struct Layout {
+    static constexpr int kStages = kSparse ? 4 : 5;
+    static constexpr int kSmemQ = 0;
+    static constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
+    static constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
+    // q_full, q_empty, kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full,
+    // o_free, list_full, list_empty, drain, then kOutSlots each of out_full, out_empty
+    static constexpr int kNumBars = 2 + 2 * kStages + 14 + 1 + 2 * kOutSlots;
+    static constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
+    // unit, n_kept, lk_eff, last0, last1 per list buffer, then the copy-out ring's unit per slot
+    static constexpr int kSmemUnit = kSmemTmemSlot + 16;
+    static constexpr int kSmemList = (kSmemUnit + (10 + kOutSlots) * 4 + 15) & ~15;  // 2 lists (masked only)
+    static constexpr int kSmemTotal = kSmemList + (kSparse ? 2 * kMaxKvTiles * 4 : 0);
+    static constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
+    static_assert(kSmemAlloc <= 232448, "shared memory budget");
+};
 // threads that release a list buffer: producer warp, MMA warp, both softmax warpgroups
 constexpr int kListConsumers = 32 + 32 + 2 * kBlockM;
 
@@ -117,7 +126,6 @@ constexpr uint32_t kPolyPairs = KD_FMHA_POLY_PAIRS;
 __device__ __forceinline__ bool tile_needed(uint32_t entry, int i) { return ((entry >> (8 * i)) & 0xFFu) != 0; }
 constexpr bool kSplitP = KD_FMHA_SPLIT_P != 0;
 
-static_assert(kSmemAlloc <= 232448, "shared memory budget");
 
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO* dst, const float (&v)[32]);
@@ -182,6 +190,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const FmhaParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    using L = Layout<kSparse>;
+    constexpr int kStages = L::kStages;
+    constexpr int kSmemQ = L::kSmemQ;
+    constexpr int kSmemKV = L::kSmemKV;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -189,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_qblk = (p.Lq + kRowsPerCta - 1) / kRowsPerCta;
     const int n_units = n_qblk * p.H * p.N;
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kSmemBar);
     uint64_t* q_full = bars + 0;
     uint64_t* q_empty = bars + 1;
     uint64_t* kv_full = bars + 2;
@@ -204,13 +216,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* drain = s_full + 14;
     uint64_t* out_full = s_full + 15;        // [kOutSlots] a unit's rows are stored locally (256 arrivals)
     uint64_t* out_empty = out_full + kOutSlots;  // [kOutSlots] the copy-out warp is done with the slot
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
-    int* s_unit = reinterpret_cast<int*>(smem + kSmemUnit);     // [2] unit index, -1 = no more work
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kSmemTmemSlot);
+    int* s_unit = reinterpret_cast<int*>(smem + L::kSmemUnit);  // [2] unit index, -1 = no more work
     int* s_nkept = s_unit + 2;                                   // [2] kept K/V tiles of the unit
     int* s_lkeff = s_unit + 4;                                   // [2] valid keys of the unit's sequence
     int* s_last = s_unit + 6;                                    // [2][2] last list entry Q tile i needs, -1: none
     int* s_out_unit = s_unit + 10;                               // [kOutSlots] unit to copy out, -1 = finished
-    uint32_t* lists = reinterpret_cast<uint32_t*>(smem + kSmemList);  // [2][kMaxKvTiles]
+    // [2][kMaxKvTiles] kept-tile lists, masked kernel only; the dense kernel's entry j is tile j, all full
+    uint32_t* lists = kSparse ? reinterpret_cast<uint32_t*>(smem + L::kSmemList) : nullptr;
+    auto entry = [](const uint32_t* list, int j) -> uint32_t {
+        return kSparse ? list[j] : (((uint32_t)j << 16) | 0x5555u);
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -290,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 lk_eff = kl < 0 ? 0 : (kl < p.Lk ? kl : p.Lk);
             }
             const int n_kv_tiles = (lk_eff + kBlockN - 1) / kBlockN;
-            uint32_t* list = lists + b * kMaxKvTiles;
+            uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             int count = 0;
             int last[2] = {-1, -1};
             const long long plane =
@@ -317,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const bool kept = bits != 0;
                 const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
-                if (kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)kt << 16) | bits;
+                if (kSparse && kept) list[count + __popc(ballot & ((1u << lane) - 1u))] = ((uint32_t)kt << 16) | bits;
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {  // position of the last entry Q tile i needs
                     const uint32_t bi = __ballot_sync(0xffffffffu, tile_needed(bits, i));
@@ -329,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // tiles this unit loads, and Q-tile x K/V-tile products it computes
                 __syncwarp();  // other lanes' list entries are read below
                 int pairs = 0;
-                for (int j = lane; j < count; j += 32) pairs += (int)need(list[j], 0) + (int)need(list[j], 1);
+                for (int j = lane; j < count; j += 32) pairs += (int)need(entry(list, j), 0) + (int)need(entry(list, j), 1);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) pairs += __shfl_xor_sync(0xffffffffu, pairs, o);
                 if (lane == 0) {
@@ -365,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_iter = s_nkept[b];
             const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
             const int hk = h / p.rk2, nk = n / p.rk3;
-            const uint32_t* list = lists + b * kMaxKvTiles;
+            const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             if (n_iter > 0) {
                 // Q buffer is free once the previous unit's last S MMA has completed
                 if (q_uses > 0 &&
@@ -383,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 ++q_uses;
                 for (int j = 0; j < n_iter && ok; ++j) {
-                    const int kt = (int)(list[j] >> 16);
+                    const int kt = (int)(entry(list, j) >> 16);
 #pragma unroll 1
                     for (int w = 0; w < 2; ++w) {  // w = 0: K tile, w = 1: V tile
                         const int s = it % kStages;
@@ -489,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (u < 0) break;
             const int n_iter = s_nkept[b];
             const int last0 = s_last[2 * b], last1 = s_last[2 * b + 1];
-            const uint32_t* list = lists + b * kMaxKvTiles;
+            const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             if (n_iter == 0) {
                 mbar_arrive(&list_empty[b]);
                 continue;
@@ -498,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int sK = 0, sV = 0;
             if (!(ok = next_stage(sK))) break;
             tc_fence_after();
-            uint32_t e_next = list[0];
+            uint32_t e_next = entry(list, 0);
             if (need(e_next, 0)) {
                 issue_s(0, sK);
                 commit(&s_full[0]);
@@ -526,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < n_iter; ++j) {
                 const uint32_t e = e_next;
                 const bool more = j + 1 < n_iter;
-                if (more) e_next = list[j + 1];
+                if (more) e_next = entry(list, j + 1);
                 if (!(ok = next_stage(sV))) break;
                 KD_TRACE(1, 0, gq0);
                 int sK2 = -1;
@@ -646,13 +662,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_iter = s_nkept[b];
             const int lk_eff = s_lkeff[b];
             const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
-            const uint32_t* list = lists + b * kMaxKvTiles;
+            const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
             const bool row_valid = qrow < p.Lq;
             float m = -INFINITY, l = 0.f;
             int k = 0;  // tiles of this unit processed by this warpgroup
             for (int j = 0; j < n_iter; ++j) {
-                const uint32_t e = list[j];
+                const uint32_t e = entry(list, j);
                 if (!need(e, wg)) continue;  // all four sub-tiles masked for this Q tile
                 const int kbase = (int)(e >> 16) * kBlockN;
                 const uint32_t c0 = (e >> (4 * g4)) & 3u, c1 = (e >> (4 * g4 + 2)) & 3u;
@@ -844,14 +860,15 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
     // a mask (tile classes) selects the instantiation that skips K/V tiles per Q tile
     auto kern = p.tile_cls ? fmha_fwd_kernel<T, TO, true> : fmha_fwd_kernel<T, TO, false>;
     // set on every launch: the attribute belongs to the current device, and the call is cheap
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+    const int smem_bytes = p.tile_cls ? Layout<true>::kSmemAlloc : Layout<false>::kSmemAlloc;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     // Persistent: one CTA per SM (never more CTAs than units); units are handed out by p.work_counter,
     // which also balances units of unequal cost (masks, kv_len).
     const long long units = (long long)((p.Lq + kRowsPerCta - 1) / kRowsPerCta) * p.H * p.N;
     const int grid = (int)(units < p.num_ctas ? units : p.num_ctas);
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, kThreads, kSmemAlloc, st>>>(tmQ, tmK, tmV, p);
+    kern<<<grid, kThreads, smem_bytes, st>>>(tmQ, tmK, tmV, p);
     return cudaGetLastError();
 }
 
@@ -864,7 +881,7 @@ int regs_t() {
 
 }  // namespace
 
-int fmha_smem_bytes() { return kSmemAlloc; }
+int fmha_smem_bytes() { return Layout<true>::kSmemAlloc; }
 
 #ifdef KD_FMHA_TRACE
 extern "C" int kd_fmha_trace_read(unsigned long long* host, unsigned long long n) {
