@@ -133,6 +133,13 @@ kd_attn_status kd_attn_device_status(kd_attn_ctx* ctx, void* stream);
  * zeroes the counters after reading.  No reference counterpart. */
 kd_attn_status kd_attn_tile_stats(kd_attn_ctx* ctx, void* stream, uint64_t out[2], int32_t reset);
 
+/* Self-test of failure detection: launches one bounded device wait that nothing
+ * releases (the wait the kernels use, on a barrier nobody arrives on).  After
+ * wait_ms (1..10000) it gives up and sets the context's error word, so the next
+ * kd_attn_device_status returns KD_ATTN_ERR_DEVICE_TIMEOUT (and clears it); the
+ * context stays usable.  Nothing faults, traps or spins without a bound. */
+kd_attn_status kd_attn_selftest_wait(kd_attn_ctx* ctx, uint32_t wait_ms, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Prologue: RMSNorm per head + 3D RoPE + cast + permute, one HBM pass.
  * Replaces, per projection x (crossdit.hpp:132-141, :188-193):

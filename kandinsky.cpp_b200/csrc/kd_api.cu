@@ -976,6 +976,14 @@ void kd_attn_set_log_callback(kd_attn_log_cb cb, void* user_data) {
     g_log_user = user_data;
 }
 
+kd_attn_status kd_attn_selftest_wait(kd_attn_ctx* ctx, uint32_t wait_ms, void* stream) {
+    if (!ctx || wait_ms == 0 || wait_ms > 10000) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    KD_CUDA(ctx, launch_wait_selftest(ctx->d_words, ctx->d_words + 1, (unsigned long long)wait_ms * 1000000ull,
+                                      static_cast<cudaStream_t>(stream)));
+    return KD_ATTN_OK;
+}
+
 kd_attn_status kd_attn_tile_stats(kd_attn_ctx* ctx, void* stream, uint64_t out[2], int32_t reset) {
     if (!ctx || !out) return KD_ATTN_ERR_INVALID_ARGUMENT;
     DeviceGuard g(ctx->device);

@@ -28,6 +28,7 @@ enum : unsigned {
     kErrTimeoutDrain = 1u << 7,  // in-flight copies / MMAs did not drain on the abort path
     kErrTimeoutList = 1u << 8,   // a unit's K/V tile list was never published / released
     kErrTimeoutOut = 1u << 9,    // head-sharded copy-out: a unit's rows never published / slot never freed
+    kErrSelfTest = 1u << 10,     // kd_attn_selftest_wait: the wait nothing releases ran out (expected)
 };
 
 struct DevCtl {

@@ -114,6 +114,9 @@ struct MaskClassParams {
 };
 cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st);
 
+// One bounded wait that nothing releases (sets the self-test error bit after wait_ns).
+cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned long long wait_ns, cudaStream_t st);
+
 cudaError_t launch_randn(float* dst, unsigned long long n, unsigned long long seed, unsigned offset, int num_sms,
                          cudaStream_t st);
 

@@ -253,6 +253,18 @@ __global__ void unshard_kernel(const uint4* src, uint4* dst, long long rows, int
     }
 }
 
+// Self-test of the bounded-wait path: one thread waits on a shared-memory mbarrier that nothing
+// arrives on, with the same mbar_wait the flash kernel uses.  After ctl.wait_ns the wait gives
+// up, sets kErrSelfTest in the error word and the abort flag, and the kernel returns.
+__global__ void wait_selftest_kernel(DevCtl ctl) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, ctl, kErrSelfTest, /*honor_abort=*/false, /*sleep_ns=*/1000);
+    }
+}
+
 int grid_for(long long warps_needed, int num_sms) {
     long long blocks = (warps_needed + 7) / 8;
     long long cap = (long long)num_sms * 16;
@@ -277,6 +289,11 @@ cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cu
         prologue_kernel<__half><<<grid, 256, 0, st>>>(p);
     else
         prologue_kernel<float><<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned long long wait_ns, cudaStream_t st) {
+    wait_selftest_kernel<<<1, 32, 0, st>>>(DevCtl{err, abort_flag, wait_ns});
     return cudaGetLastError();
 }
 

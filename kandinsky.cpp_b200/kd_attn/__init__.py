@@ -42,6 +42,7 @@ EXPORTED = [
     "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
+    "kd_attn_selftest_wait",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -160,6 +161,8 @@ def _load():
     L.kd_attn_cross_attention_sharded.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float, T, P,
                                                   ctypes.c_int32, T, P]
     L.kd_attn_cross_attention_sharded.restype = st
+    L.kd_attn_selftest_wait.argtypes = [P, ctypes.c_uint32, P]
+    L.kd_attn_selftest_wait.restype = st
     L.kd_attn_tile_stats.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
     L.kd_attn_tile_stats.restype = st
     L.kd_attn_set_log_callback.argtypes = [LOG_CB, P]
@@ -316,6 +319,11 @@ class Context:
                                          float(max_bias), float(logit_softcap), _ptr(kv_len), _ptr(tile_mask),
                                          _ref(out), _ptr(lse), _stream_ptr(stream)))
         return out
+
+    def selftest_wait(self, wait_ms=50, stream=None):
+        """kd_attn_selftest_wait: one bounded device wait that nothing releases; the next
+        device_status() raises ERR_DEVICE_TIMEOUT."""
+        self.check(lib.kd_attn_selftest_wait(self.handle, int(wait_ms), _stream_ptr(stream)))
 
     def tile_stats(self, reset=False, stream=None):
         """(K/V tiles loaded, Q-tile x K/V-tile products computed) since the last reset."""

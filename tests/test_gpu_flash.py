@@ -378,3 +378,21 @@ def test_sharded_entry_points_on_one_rank(ctx, kd):
         ctx.device_status()
         assert torch.equal(out, ref_cross)
     ctx.symmetric_free(sym)
+
+
+def test_bounded_wait_reports_timeout_and_context_recovers(ctx, kd):
+    """Failure detection without a fault: a device wait that nothing releases gives up after its
+    limit, the host reads ERR_DEVICE_TIMEOUT from the error word, and the next call works."""
+    import time
+    t0 = time.time()
+    ctx.selftest_wait(wait_ms=50)
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.device_status()
+    assert e.value.status == kd.ERR_DEVICE_TIMEOUT
+    assert time.time() - t0 < 30
+    ctx.device_status()   # the error word was cleared
+    q = op_tensor(seeded((1, 1, 130, 128), 91, 0), oracle.BF16)
+    out = torch.empty(1, 130, 1, 128, device="cuda")
+    ctx.flash_attn_ext(q, q, q, out)
+    ctx.device_status()
+    assert torch.isfinite(out).all()
