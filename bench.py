@@ -232,8 +232,10 @@ def run_reference(args, cfg):
         return
     steps = []
     cb = None
+    # each step is a bounded sample; the whole arm stays near 150 s of CPU time for any --steps
+    per_step = max(2.0, min(args.ref_seconds, 150.0 / max(1, args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
-        cb = cpu_reference(cfg, seconds_target=args.ref_seconds)
+        cb = cpu_reference(cfg, seconds_target=per_step)
         if i >= args.warmup:
             steps.append(cb)
     vals = [s["value"] for s in steps]
