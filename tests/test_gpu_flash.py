@@ -396,3 +396,23 @@ def test_bounded_wait_reports_timeout_and_context_recovers(ctx, kd):
     ctx.flash_attn_ext(q, q, q, out)
     ctx.device_status()
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("Lt", [77, 512])
+def test_text_block_self_attention_with_1d_rope(ctx, kd, Lt):
+    """The CrossDiT text blocks (crossdit.hpp:606) run DiTSelfAttention with 1D text RoPE
+    (rope.hpp:36-49): the same fused path with axes (128, 0, 0) over a (L, 1, 1) grid, checked
+    against the oracle with the text table pinned to the reference's compute_text_rope."""
+    N, H = 1, 32
+    C = H * 128
+    q = seeded((N, Lt, C), 97, 0)
+    k = seeded((N, Lt, C), 97, 1)
+    v = seeded((N, Lt, C), 97, 2)
+    tab = oracle.text_rope_table(Lt, 128)
+    exact, lse_ref = oracle.self_attention(q, k, v, H, rope_table=tab, kv_type=oracle.BF16, mode=oracle.EXACT, lse=True)
+    out = torch.empty(N, Lt, C, device="cuda")
+    lse = torch.empty(N, H, Lt, device="cuda")
+    rope = kd.Rope3D.make((Lt, 1, 1), axes=(128, 0, 0))
+    ctx.self_attention(dev(q), dev(k), dev(v), H, out, rope=rope, op_type=kd.BF16, lse=lse)
+    ctx.device_status()
+    assert_gates(out.cpu().numpy(), exact, lse=lse.cpu().numpy(), lse_ref=lse_ref, label=f"text L{Lt}")
