@@ -511,6 +511,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     for (int i = 0; i < a.n_peers; ++i)
         p.peer_out[i] = a.peer_base[i] + (static_cast<const char*>(o.data) - a.out_base);
     p.n_peer_out = a.n_peers;
+    p.head_pairs = (tiled && mh == 1 && H % 2 == 0 && a.n_peers == 0) ? 1 : 0;
     p.out_v8 = (reinterpret_cast<uintptr_t>(o.data) % 32 == 0 && onb[1] % 32 == 0 && onb[2] % 32 == 0 &&
                 onb[3] % 32 == 0) ? 1 : 0;
     // abort flag and work counter start at zero for every launch

@@ -184,7 +184,7 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v
                           Pack2<__half>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
 
-template <typename T, typename TO, bool kSparse>
+template <typename T, typename TO, bool kSparse, bool kPairs>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FmhaParams p) {
@@ -198,8 +198,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
-    const int n_qblk = (p.Lq + kRowsPerCta - 1) / kRowsPerCta;
-    const int n_units = n_qblk * p.H * p.N;
+    // Units: normally 256 query rows (Q tiles 0, 1) of one head; in head-pair mode (masked kernel,
+    // one mask plane for all heads) the same 128 rows of heads 2hp and 2hp + 1, which need exactly
+    // the same K/V tiles, so both Q tiles always have work at every listed tile.
+    constexpr int kUnitRows = kPairs ? kBlockM : kRowsPerCta;
+    const int n_qblk = (p.Lq + kUnitRows - 1) / kUnitRows;
+    const int unit_heads = kPairs ? p.H / 2 : p.H;
+    const int n_units = n_qblk * unit_heads * p.N;
+    struct UnitGeo {
+        int qblk, n;
+        int row0[2], head[2];
+    };
+    auto geo = [&](int u) {
+        UnitGeo g;
+        g.qblk = u % n_qblk;
+        const int hu = (u / n_qblk) % unit_heads;
+        g.n = u / (n_qblk * unit_heads);
+        for (int i = 0; i < 2; ++i) {
+            g.row0[i] = kPairs ? g.qblk * kBlockM : g.qblk * kRowsPerCta + i * kBlockM;
+            g.head[i] = kPairs ? 2 * hu + i : hu;
+        }
+        return g;
+    };
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kSmemBar);
     uint64_t* q_full = bars + 0;
@@ -299,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&list_full[b]);
                 break;
             }
-            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+            const UnitGeo ug = geo(u);
+            const int n = ug.n, h = ug.head[0];
             int lk_eff = p.Lk;
             if (p.kv_len) {
                 const int kl = p.kv_len[n];
@@ -316,9 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t bits = 0;
                 if (kt < n_kv_tiles) {
                     if (p.tile_cls) {
+                        // class of each (64-row group g of the unit, 64-key half hh); head-pair units
+                        // have 2 row groups shared by both Q tiles: their byte is copied for tile 1
 #pragma unroll
-                        for (int g = 0; g < 4; ++g) {
-                            const int qb = qblk * 4 + g;
+                        for (int g = 0; g < (kPairs ? 2 : 4); ++g) {
+                            const int qb = ug.row0[0] / 64 + g;
 #pragma unroll
                             for (int hh = 0; hh < 2; ++hh) {
                                 const int kb = 2 * kt + hh;
@@ -327,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 bits |= (c & 3u) << (4 * g + 2 * hh);
                             }
                         }
+                        if (kPairs) bits |= bits << 8;
                     } else {
                         bits = 0x5555u;
                     }
@@ -348,8 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = lane; j < count; j += 32) pairs += (int)need(entry(list, j), 0) + (int)need(entry(list, j), 1);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) pairs += __shfl_xor_sync(0xffffffffu, pairs, o);
-                if (lane == 0) {
-                    atomicAdd(p.tile_stats, (unsigned long long)count);
+                if (lane == 0) {  // head-pair units load every listed tile for both heads
+                    atomicAdd(p.tile_stats, (unsigned long long)(kPairs ? 2 * count : count));
                     atomicAdd(p.tile_stats + 1, (unsigned long long)pairs);
                 }
             }
@@ -379,8 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int u = s_unit[b];
             if (u < 0) break;
             const int n_iter = s_nkept[b];
-            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
-            const int hk = h / p.rk2, nk = n / p.rk3;
+            const UnitGeo ug = geo(u);
+            const int n = ug.n, nk = n / p.rk3;
+            const int hk0 = ug.head[0] / p.rk2, hk1 = ug.head[1] / p.rk2;
             const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             if (n_iter > 0) {
                 // Q buffer is free once the previous unit's last S MMA has completed
@@ -394,14 +419,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int bx = 0; bx < 2; ++bx)
                             tma_load_4d(smem + kSmemQ + i * kTileBytes + bx * kBoxBytes, &tmQ, q_full, bx * 64,
-                                        qblk * kRowsPerCta + i * kBlockM, h, n);
+                                        ug.row0[i], ug.head[i], n);
                 }
                 __syncwarp();
                 ++q_uses;
                 for (int j = 0; j < n_iter && ok; ++j) {
                     const int kt = (int)(entry(list, j) >> 16);
+                    // ring order per entry: K, V -- or for head-pair units K(head 0), K(head 1),
+                    // V(head 0), V(head 1), the order the MMA warp consumes them in
 #pragma unroll 1
-                    for (int w = 0; w < 2; ++w) {  // w = 0: K tile, w = 1: V tile
+                    for (int w = 0; w < (kPairs ? 4 : 2); ++w) {
+                        const bool is_v = kPairs ? (w >= 2) : (w == 1);
+                        const int hk = (kPairs && (w & 1)) ? hk1 : hk0;
                         const int s = it % kStages;
                         const uint32_t ph = (it / kStages) & 1u;
                         ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
@@ -409,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         KD_TRACE(0, w, j);
                         if (lane == 0) {
                             mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
-                            const CUtensorMap* map = w ? &tmV : &tmK;
+                            const CUtensorMap* map = is_v ? &tmV : &tmK;
 #pragma unroll
                             for (int bx = 0; bx < 2; ++bx)
                                 tma_load_4d(smem + kSmemKV + s * kTileBytes + bx * kBoxBytes, map, &kv_full[s],
@@ -511,77 +540,114 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(q_full, units & 1, ctl, kErrTimeoutQ)))) break;
-            int sK = 0, sV = 0;
-            if (!(ok = next_stage(sK))) break;
-            tc_fence_after();
-            uint32_t e_next = entry(list, 0);
-            if (need(e_next, 0)) {
-                issue_s(0, sK);
-                commit(&s_full[0]);
-            }
-            if (need(e_next, 1)) {
-                issue_s(1, sK);
-                commit(&s_full[1]);
-            }
-            commit(&kv_empty[sK]);
-            if (n_iter == 1) commit(q_empty);  // the unit's last S MMA is issued: Q may be replaced
-            issued = true;
             bool first0 = true, first1 = true;
             // PV_i for K/V tile j when Q tile i needs it; the first one of a unit overwrites O_i, so
             // the previous unit's epilogue must have read O_i first (o_free)
-            auto pv_tile = [&](int i, int j, bool& first, uint32_t& gi, uint32_t ui, int last) -> bool {
+            auto pv_tile = [&](int i, int j, bool& first, uint32_t& gi, uint32_t ui, int last, int sv) -> bool {
                 if (first && ui > 0 &&
                     !__all_sync(0xffffffffu, mbar_wait(&o_free[i], (ui - 1) & 1, ctl, kErrTimeoutO)))
                     return false;
-                if (!pv(i, sV, !first, gi)) return false;
+                if (!pv(i, sv, !first, gi)) return false;
                 ++gi;
                 first = false;
                 if (j == last) commit(&o_full[i]);
                 return true;
             };
-            for (int j = 0; j < n_iter; ++j) {
-                const uint32_t e = e_next;
-                const bool more = j + 1 < n_iter;
-                if (more) e_next = entry(list, j + 1);
-                if (!(ok = next_stage(sV))) break;
-                KD_TRACE(1, 0, gq0);
-                int sK2 = -1;
-                bool early0 = false, early1 = false;
-                // Masked lists: a Q tile with no PV at this K/V tile has nothing to wait for, so its
-                // next S is issued before the other Q tile's PV (which waits on that tile's softmax)
-                // and the tensor core keeps working.  Its previous PV is already queued ahead of it.
-                if (kSparse && more) {
-                    early0 = !need(e, 0) && need(e_next, 0);
-                    early1 = !need(e, 1) && need(e_next, 1);
-                    if (early0 || early1) {
-                        if (!(ok = next_stage(sK2))) break;
-                        if (early0) {
+            if constexpr (kPairs) {
+                // head-pair unit: ring order per entry K(head 0), K(head 1), V(head 0), V(head 1);
+                // same PV0(j), S0(j+1), PV1(j), S1(j+1) order, each Q tile on its own head's tiles
+                int sK0 = 0, sK1 = 0;
+                if (!(ok = next_stage(sK0)) || !(ok = next_stage(sK1))) break;
+                tc_fence_after();
+                issue_s(0, sK0);
+                commit(&s_full[0]);
+                issue_s(1, sK1);
+                commit(&s_full[1]);
+                commit(&kv_empty[sK0]);
+                commit(&kv_empty[sK1]);
+                if (n_iter == 1) commit(q_empty);
+                issued = true;
+                for (int j = 0; j < n_iter; ++j) {
+                    const bool more = j + 1 < n_iter;
+                    int sV0 = 0, sV1 = 0, sK0n = 0, sK1n = 0;
+                    if (!(ok = next_stage(sV0)) || !(ok = next_stage(sV1))) break;
+                    if (!(ok = pv_tile(0, j, first0, gq0, uq0, last0, sV0))) break;
+                    if (more) {
+                        if (!(ok = next_stage(sK0n)) || !(ok = next_stage(sK1n))) break;
+                        issue_s(0, sK0n);
+                        commit(&s_full[0]);
+                    }
+                    if (!(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV1))) break;
+                    commit(&kv_empty[sV0]);
+                    commit(&kv_empty[sV1]);
+                    if (more) {
+                        issue_s(1, sK1n);
+                        commit(&s_full[1]);
+                        commit(&kv_empty[sK0n]);
+                        commit(&kv_empty[sK1n]);
+                        if (j + 2 == n_iter) commit(q_empty);
+                    }
+                }
+            } else {
+                int sK = 0, sV = 0;
+                if (!(ok = next_stage(sK))) break;
+                tc_fence_after();
+                uint32_t e_next = entry(list, 0);
+                if (need(e_next, 0)) {
+                    issue_s(0, sK);
+                    commit(&s_full[0]);
+                }
+                if (need(e_next, 1)) {
+                    issue_s(1, sK);
+                    commit(&s_full[1]);
+                }
+                commit(&kv_empty[sK]);
+                if (n_iter == 1) commit(q_empty);  // the unit's last S MMA is issued: Q may be replaced
+                issued = true;
+                for (int j = 0; j < n_iter; ++j) {
+                    const uint32_t e = e_next;
+                    const bool more = j + 1 < n_iter;
+                    if (more) e_next = entry(list, j + 1);
+                    if (!(ok = next_stage(sV))) break;
+                    KD_TRACE(1, 0, gq0);
+                    int sK2 = -1;
+                    bool early0 = false, early1 = false;
+                    // Masked lists: a Q tile with no PV at this K/V tile has nothing to wait for, so its
+                    // next S is issued before the other Q tile's PV (which waits on that tile's softmax)
+                    // and the tensor core keeps working.  Its previous PV is already queued ahead of it.
+                    if (kSparse && more) {
+                        early0 = !need(e, 0) && need(e_next, 0);
+                        early1 = !need(e, 1) && need(e_next, 1);
+                        if (early0 || early1) {
+                            if (!(ok = next_stage(sK2))) break;
+                            if (early0) {
+                                issue_s(0, sK2);
+                                commit(&s_full[0]);
+                            }
+                            if (early1) {
+                                issue_s(1, sK2);
+                                commit(&s_full[1]);
+                            }
+                        }
+                    }
+                    if (need(e, 0) && !(ok = pv_tile(0, j, first0, gq0, uq0, last0, sV))) break;
+                    if (more) {
+                        if (sK2 < 0 && !(ok = next_stage(sK2))) break;
+                        if (!early0 && need(e_next, 0)) {
                             issue_s(0, sK2);
                             commit(&s_full[0]);
                         }
-                        if (early1) {
+                    }
+                    if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV))) break;
+                    commit(&kv_empty[sV]);
+                    if (more) {
+                        if (!early1 && need(e_next, 1)) {
                             issue_s(1, sK2);
                             commit(&s_full[1]);
                         }
+                        commit(&kv_empty[sK2]);
+                        if (j + 2 == n_iter) commit(q_empty);
                     }
-                }
-                if (need(e, 0) && !(ok = pv_tile(0, j, first0, gq0, uq0, last0))) break;
-                if (more) {
-                    if (sK2 < 0 && !(ok = next_stage(sK2))) break;
-                    if (!early0 && need(e_next, 0)) {
-                        issue_s(0, sK2);
-                        commit(&s_full[0]);
-                    }
-                }
-                if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1))) break;
-                commit(&kv_empty[sV]);
-                if (more) {
-                    if (!early1 && need(e_next, 1)) {
-                        issue_s(1, sK2);
-                        commit(&s_full[1]);
-                    }
-                    commit(&kv_empty[sK2]);
-                    if (j + 2 == n_iter) commit(q_empty);
                 }
             }
             mbar_arrive(&list_empty[b]);
@@ -614,9 +680,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&out_empty[slot]);  // the unit index has been read
                 if (u < 0) break;
-                const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
-                const int row0 = qblk * kRowsPerCta;
-                const int rows = min(kRowsPerCta, p.Lq - row0);
+                const UnitGeo ug = geo(u);
+                // a unit's rows: 256 rows of one head, or 128 rows of each of two heads
+#pragma unroll 1
+                for (int part = 0; part < (kPairs ? 2 : 1); ++part) {
+                const int row0 = part ? ug.row0[1] : ug.row0[0], h = part ? ug.head[1] : ug.head[0], n = ug.n;
+                const int rows = min(kUnitRows, p.Lq - row0);
                 const long long base = (long long)n * p.o_nb3 + (long long)h * p.o_nb1 + (long long)chunk * 16;
                 for (int r0 = 0; r0 < rows; r0 += kBatch * kRowsPerInstr) {
                     uint4 v[kBatch];
@@ -637,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                }
             }
             // the peers' copies are complete and visible system-wide before this CTA retires
             __threadfence_system();
@@ -648,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_addr + wg * 128;
         const uint32_t tO = tmem + lane_addr + 256 + wg * 128;
-        const int g4 = wg * 2 + (r >> 6);                // 64-row group of this row within the unit
+        const int g4 = kPairs ? (r >> 6) : wg * 2 + (r >> 6);  // 64-row group of this row within the unit
         const float sl2 = p.scale_log2;
         uint32_t g = 0;      // tiles this Q tile needed so far: phase of s_full / p_full
         uint32_t units = 0;  // units in which this Q tile had work: phase of o_full / o_free
@@ -661,9 +731,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (u < 0) break;
             const int n_iter = s_nkept[b];
             const int lk_eff = s_lkeff[b];
-            const int qblk = u % n_qblk, h = (u / n_qblk) % p.H, n = u / (n_qblk * p.H);
+            const UnitGeo ug = geo(u);
+            const int h = wg ? ug.head[1] : ug.head[0], n = ug.n;  // selects: no dynamic indexing
             const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
-            const int qrow = qblk * kRowsPerCta + wg * kBlockM + r;
+            const int qrow = (wg ? ug.row0[1] : ug.row0[0]) + r;
             const bool row_valid = qrow < p.Lq;
             float m = -INFINITY, l = 0.f;
             int k = 0;  // tiles of this unit processed by this warpgroup
@@ -858,14 +929,18 @@ template <typename T, typename TO>
 cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const FmhaParams& p,
                      cudaStream_t st) {
     // a mask (tile classes) selects the instantiation that skips K/V tiles per Q tile
-    auto kern = p.tile_cls ? fmha_fwd_kernel<T, TO, true> : fmha_fwd_kernel<T, TO, false>;
+    // head-pair units when every head shares one mask plane (p.head_pairs, set by the host)
+    auto kern = !p.tile_cls ? fmha_fwd_kernel<T, TO, false, false>
+                            : (p.head_pairs ? fmha_fwd_kernel<T, TO, true, true> : fmha_fwd_kernel<T, TO, true, false>);
     // set on every launch: the attribute belongs to the current device, and the call is cheap
     const int smem_bytes = p.tile_cls ? Layout<true>::kSmemAlloc : Layout<false>::kSmemAlloc;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     // Persistent: one CTA per SM (never more CTAs than units); units are handed out by p.work_counter,
     // which also balances units of unequal cost (masks, kv_len).
-    const long long units = (long long)((p.Lq + kRowsPerCta - 1) / kRowsPerCta) * p.H * p.N;
+    const long long units = p.tile_cls && p.head_pairs
+                                ? (long long)((p.Lq + kBlockM - 1) / kBlockM) * (p.H / 2) * p.N
+                                : (long long)((p.Lq + kRowsPerCta - 1) / kRowsPerCta) * p.H * p.N;
     const int grid = (int)(units < p.num_ctas ? units : p.num_ctas);
     if (grid <= 0) return cudaSuccess;
     kern<<<grid, kThreads, smem_bytes, st>>>(tmQ, tmK, tmV, p);
@@ -875,7 +950,7 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
 template <typename T, typename TO>
 int regs_t() {
     cudaFuncAttributes a{};
-    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false>) != cudaSuccess) return -1;
+    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false, false>) != cudaSuccess) return -1;
     return a.numRegs;
 }
 

@@ -45,6 +45,8 @@ struct FmhaParams {
     char* peer_out[kMaxPeers];
     int n_peer_out;
     int out_v8;              // 1: out rows are 32-byte aligned (256-bit stores in the epilogue)
+    int head_pairs;          // masked kernel: units of 128 rows x heads (2hp, 2hp+1) -- needs one mask
+                             // plane for all heads (mh == 1), an even head count and no peers
 };
 
 enum class OpType { F16, BF16 };

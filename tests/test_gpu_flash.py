@@ -266,13 +266,21 @@ def test_self_attention_host_matches_device_path(ctx, kd, H, grid, N, out_dtype,
 
 
 # ------------------------------------------------------------------ tile bitmap, tile counters, fused prologue
-def expected_tile_counts(keep, Lq, Lk, units_per_plane_mult):
-    """K/V tiles (128 keys) loaded and Q-tile (128 rows) x K/V-tile products computed for one
-    (head, sequence) plane, times the number of planes: a 128-key tile is loaded when any of the
-    unit's (256 rows) 64x64 sub-tiles is kept, and computed for each Q tile with a kept sub-tile."""
+def expected_tile_counts(keep, Lq, Lk, units_per_plane_mult, head_pairs=False):
+    """K/V tiles (128 keys of one head) loaded and Q-tile (128 rows) x K/V-tile products computed for
+    one (head, sequence) plane, times the number of planes.  Units of 256 rows of one head: a tile is
+    loaded when any of the unit's 64x64 sub-tiles is kept and computed for each Q tile with a kept
+    sub-tile.  Head-pair units (one mask plane for all heads): 128 rows of two heads, every tile
+    the rows need is loaded and computed once per head."""
     n_qb, n_kb = keep.shape
-    n_units = (Lq + 255) // 256
     n_kv = (Lk + 127) // 128
+    if head_pairs:
+        n = 0
+        for b in range((Lq + 127) // 128):
+            for t in range(n_kv):
+                n += bool(keep[2 * b: 2 * b + 2, 2 * t: 2 * t + 2].any())
+        return n * units_per_plane_mult, n * units_per_plane_mult
+    n_units = (Lq + 255) // 256
     loaded = pairs = 0
     for u in range(n_units):
         for t in range(n_kv):
@@ -287,7 +295,8 @@ def expected_tile_counts(keep, Lq, Lk, units_per_plane_mult):
 
 def test_tile_bitmap_skips_tiles_and_matches_dense_mask(ctx, kd):
     """Block-sparse attention from the 64x64 tile bitmap alone equals the dense f16 block mask bit for
-    bit, and the device counters show exactly the kept tiles were loaded and multiplied."""
+    bit, and the device counters show exactly the kept tiles were loaded and multiplied (one mask
+    plane for the even head count: head-pair units)."""
     N, H, Lq, Lk, D = 2, 2, 1000, 1000, 128
     qf = seeded((N, H, Lq, D), 61, 0)
     kf = seeded((N, H, Lk, D), 61, 1)
@@ -303,7 +312,7 @@ def test_tile_bitmap_skips_tiles_and_matches_dense_mask(ctx, kd):
     assert bits.shape == (n_qb, (n_kb + 7) // 8)
     q, k, v = dev(qf), op_tensor(kf, oracle.BF16), op_tensor(vf, oracle.BF16)
     outs = {}
-    want = expected_tile_counts(keep, Lq, Lk, H * N)
+    want = expected_tile_counts(keep, Lq, Lk, H * N, head_pairs=True)
     dense_counts = expected_tile_counts(np.ones_like(keep), Lq, Lk, H * N)
     for name, kw in (("dense", dict(mask=torch.from_numpy(dense).cuda())), ("bitmap", dict(tile_mask=bits)),
                      ("both", dict(mask=torch.from_numpy(dense).cuda(), tile_mask=bits)), ("none", {})):
@@ -315,7 +324,7 @@ def test_tile_bitmap_skips_tiles_and_matches_dense_mask(ctx, kd):
         ctx.device_status()
         outs[name] = (out.cpu(), lse.cpu())
         assert counts == (dense_counts if name == "none" else want), (name, counts)
-    assert want[0] < dense_counts[0]
+    assert want[1] < dense_counts[1]   # fewer products than dense (head pairs may load more tiles: per head)
     assert_gates(outs["bitmap"][0].numpy(), exact, lse=outs["bitmap"][1].numpy(), lse_ref=lse_ref, label="bitmap")
     for name in ("dense", "both"):
         assert torch.equal(outs[name][0], outs["bitmap"][0]) and torch.equal(outs[name][1], outs["bitmap"][1])
