@@ -38,7 +38,7 @@ extern "C" {
 #endif
 
 #define KD_ATTN_VERSION_MAJOR 0
-#define KD_ATTN_VERSION_MINOR 1
+#define KD_ATTN_VERSION_MINOR 2
 
 typedef enum {
     KD_ATTN_OK = 0,

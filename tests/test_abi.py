@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(kd):
 
 
 def test_version(kd):
-    assert kd.version() == (0, 1)
+    assert kd.version() == (0, 2)
 
 
 def test_create_without_gpu_fails_cleanly(kd):
