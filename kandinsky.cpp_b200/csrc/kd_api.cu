@@ -782,8 +782,17 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     int G = 1;
     for (int g = 1; g <= n_head; ++g)
         if (n_head % g == 0 && n_head / g >= want) G = g;
-    const int groups = n_head / G;
-    const size_t in_w = (size_t)G * kHeadDim * 4;                  // bytes per row of one input slab
+    // Group sizes: G heads each, except that the last G are split by halving (G/2, G/4, ..., 1, 1):
+    // only the last group's compute and copy-out are exposed behind the (PCIe-bound) copy-in.
+    std::vector<int> sizes;
+    for (int g = 0; g < n_head / G - 1; ++g) sizes.push_back(G);
+    for (int rest = n_head - (int)sizes.size() * G; rest > 0;) {
+        const int part = std::min(G, rest > 1 ? (rest + 1) / 2 : 1);  // never more than a slab holds
+        sizes.push_back(part);
+        rest -= part;
+    }
+    const int groups = (int)sizes.size();
+    const size_t in_w = (size_t)G * kHeadDim * 4;                  // bytes per row of one input slab (max)
     const size_t out_es = elt_size(out->type);
     const size_t out_w = (size_t)G * kHeadDim * out_es;
     const size_t in_slab = align256(in_w * (size_t)(L * N));
@@ -801,12 +810,16 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     KD_CUDA(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_start, 0));
     KD_CUDA(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_start, 0));
     const kd_tensor* ins[3] = {q_in, k_in, v_in};
-    for (int g = 0; g < groups; ++g) {
+    int head0 = 0;
+    for (int g = 0; g < groups; head0 += sizes[g], ++g) {
         const int b = g & 1;
+        const int gh = sizes[g];                                       // heads in this group
+        const size_t gin_w = (size_t)gh * kHeadDim * 4, gout_w = (size_t)gh * kHeadDim * out_es;
         // inputs of group g go into slab b once group g-2's compute has finished with it
         if (g >= 2) KD_CUDA(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_done[b], 0));
         for (int x = 0; x < 3; ++x)
-            if ((rc = copy_columns(ctx, ins[x], (size_t)g * in_w, in_w, in_buf(b, x), true, ctx->h2d))) return rc;
+            if ((rc = copy_columns(ctx, ins[x], (size_t)head0 * kHeadDim * 4, gin_w, in_buf(b, x), true, ctx->h2d)))
+                return rc;
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_in[b], ctx->h2d));
         // compute group g on the caller's stream; its output slab must have been copied out (group g-2)
         KD_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ev_in[b], 0));
@@ -815,24 +828,25 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
         for (int x = 0; x < 3; ++x) {
             xs[x] = *ins[x];
             xs[x].data = in_buf(b, x);
-            xs[x].ne[0] = (int64_t)G * kHeadDim;
-            xs[x].nb[1] = in_w;
-            xs[x].nb[2] = in_w * (size_t)L;
+            xs[x].ne[0] = (int64_t)gh * kHeadDim;
+            xs[x].nb[1] = gin_w;
+            xs[x].nb[2] = gin_w * (size_t)L;
             xs[x].nb[3] = xs[x].nb[2] * (size_t)N;
         }
         os = *out;
         os.data = out_buf(b);
-        os.ne[0] = (int64_t)G * kHeadDim;
-        os.nb[1] = out_w;
-        os.nb[2] = out_w * (size_t)L;
+        os.ne[0] = (int64_t)gh * kHeadDim;
+        os.nb[1] = gout_w;
+        os.nb[2] = gout_w * (size_t)L;
         os.nb[3] = os.nb[2] * (size_t)N;
-        if ((rc = attention_core(ctx, &xs[0], &xs[1], &xs[2], G, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
+        if ((rc = attention_core(ctx, &xs[0], &xs[1], &xs[2], gh, q_gain, k_gain, eps, rope, nullptr, nullptr, op_type,
                                  &os, nullptr, st)))
             return rc;
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_done[b], st));
         // copy group g's heads out into their columns of the host output
         KD_CUDA(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_done[b], 0));
-        if ((rc = copy_columns(ctx, out, (size_t)g * out_w, out_w, out_buf(b), false, ctx->d2h))) return rc;
+        if ((rc = copy_columns(ctx, out, (size_t)head0 * kHeadDim * out_es, gout_w, out_buf(b), false, ctx->d2h)))
+            return rc;
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_out[b], ctx->d2h));
     }
     // completion of the caller's stream covers the whole call (last copy-out included)
