@@ -3,8 +3,9 @@
 Runs oracle/_ref/kd_ref_pin -- the reference's src/rng.hpp (PhiloxRNG) and
 src/rope.hpp (get_freqs, compute_text_rope, compute_visual_rope) compiled from
 the reference sources by oracle/ref_pin/Makefile -- and stores its outputs.
-Needs the reference tree (default /root/reference, or $KD_REFERENCE_DIR); the
-committed .npz is what the tests read, so they run without it.
+Needs the reference tree (oracle/build_oracle.py's default location, or
+$KD_REFERENCE_DIR); the committed .npz is what the tests read, so they run
+without it.
 
     python tests/golden/make_golden.py
 """
