@@ -475,34 +475,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++it;
             return __all_sync(0xffffffffu, mbar_wait(&kv_full[s], ph, ctl, kErrTimeoutKVFull));
         };
+        // The whole warp runs the issue code (one elected lane issues each instruction).
         auto issue_s = [&](int i, int s) {
-            if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
-                           desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
-                }
+            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
+                       desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
             }
-            __syncwarp();
         };
         // O_i += P_i V for keys [64*half, 64*half + 64): P columns 32*half.., V rows 64*half..
         auto issue_pv = [&](int i, int s, bool acc, int half) {
-            if (lane == 0) {
 #pragma unroll
-                for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
-                    const int kk = half * (kBlockN / 32) + k4;
-                    mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
-                           desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
-                           (acc || kk > 0) ? 1u : 0u);
-                }
+            for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+                const int kk = half * (kBlockN / 32) + k4;
+                mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
+                       desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
+                       (acc || kk > 0) ? 1u : 0u);
             }
-            __syncwarp();
         };
-        auto commit = [&](uint64_t* bar) {
-            if (lane == 0) tc_commit(bar);
-            __syncwarp();
-        };
+        auto commit = [&](uint64_t* bar) { tc_commit(bar); };
         // wait for P_i of its needed tile number gi (both halves, or each half with the split hand-off), issue PV_i
         auto pv = [&](int i, int s, bool acc, uint32_t gi) -> bool {
             if (kSplitP) {
@@ -515,6 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             }
             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], gi & 1, ctl, kErrTimeoutP))) return false;
+            KD_TRACE(1, 1 + 2 * i, gi);
             tc_fence_after();
             issue_pv(i, s, acc, 0);
             issue_pv(i, s, acc, 1);
@@ -636,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!early0 && need(e_next, 0)) {
                             issue_s(0, sK2);
                             commit(&s_full[0]);
+                            KD_TRACE(1, 2, gq0);
                         }
                     }
                     if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV))) break;
@@ -644,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!early1 && need(e_next, 1)) {
                             issue_s(1, sK2);
                             commit(&s_full[1]);
+                            KD_TRACE(1, 4, gq1);
                         }
                         commit(&kv_empty[sK2]);
                         if (j + 2 == n_iter) commit(q_empty);
