@@ -815,14 +815,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m = m_new;
                 }
                 const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+                // Dense lists: scores of even and odd keys go through packed f32x2 FMA and add (the
+                // row sum kept as two partial sums, even keys and odd keys, exactly as the scalar
+                // form below).  The masked instantiation keeps the scalar form: its extra live
+                // state leaves no room for the register pairs.
+                const uint64_t sl2x2 = f2_pack(sl2, sl2), nmux2 = f2_pack(neg_mu, neg_mu);
+                uint64_t rs2 = f2_pack(0.f, 0.f);
                 float rs0 = 0.f, rs1 = 0.f;
                 // P for 32 keys -> 16 packed columns of S_i's TMEM
                 auto p_chunk = [&](int c) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float xa = fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu);
-                        const float xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
+                        float xa, xb;
+                        if constexpr (!kSparse) {
+                            f2_unpack(fma_f32x2(f2_pack(__uint_as_float(su[c * 32 + 2 * i]),
+                                                        __uint_as_float(su[c * 32 + 2 * i + 1])),
+                                                sl2x2, nmux2),
+                                      xa, xb);
+                        } else {
+                            xa = fmaf(__uint_as_float(su[c * 32 + 2 * i]), sl2, neg_mu);
+                            xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
+                        }
                         float a, bb;
                         if ((kPolyPairs >> i) & 1u) {
                             a = exp2_poly(xa);
@@ -831,8 +845,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             a = ex2_approx(xa);
                             bb = ex2_approx(xb);
                         }
-                        rs0 += a;
-                        rs1 += bb;
+                        if constexpr (!kSparse) {
+                            rs2 = add_f32x2(rs2, f2_pack(a, bb));
+                        } else {
+                            rs0 += a;
+                            rs1 += bb;
+                        }
                         pk[i] = Pack2<T>::pack(a, bb);
                     }
                     tmem_st16(tS + c * 16, pk);
@@ -860,6 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 p_chunk(2);
                 p_chunk(3);
                 tmem_wait_st();
+                if constexpr (!kSparse) f2_unpack(rs2, rs0, rs1);
                 l += rs0 + rs1;
                 tc_fence_before();
                 mbar_arrive(&p_full[wg]);
