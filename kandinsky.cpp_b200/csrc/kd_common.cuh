@@ -262,6 +262,23 @@ __host__ __device__ constexpr uint64_t make_sw128_desc(uint32_t saddr, uint32_t 
            ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 __host__ __device__ constexpr uint64_t desc_k_sw128(uint32_t saddr) { return make_sw128_desc(saddr, 16, 1024); }
+// The same descriptor as two words.  The low word holds the start address and the leading byte
+// offset; the descriptors of the K-steps of one tile differ only in the start address, so an MMA
+// loop builds the low word once and adds (byte offset >> 4) per step.  Shared-memory addresses
+// stay below 2^18, so the 14-bit address field never carries into the LBO field.
+__host__ __device__ constexpr uint32_t sw128_desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+    return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t sw128_desc_hi(uint32_t sbo_bytes) {
+    return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+__host__ __device__ constexpr uint64_t desc_join(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+static_assert(desc_join(sw128_desc_lo(0x1400u, 16) + (0x4020u >> 4), sw128_desc_hi(1024)) ==
+                  make_sw128_desc(0x1400u + 0x4020u, 16, 1024),
+              "split K-major descriptor");
+static_assert(desc_join(sw128_desc_lo(0x31C00u, 16384) + (0x3800u >> 4), sw128_desc_hi(1024)) ==
+                  make_sw128_desc(0x31C00u + 0x3800u, 16384, 1024),
+              "split MN-major descriptor");
 __host__ __device__ constexpr uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
     return make_sw128_desc(saddr, lbo, 1024);
 }

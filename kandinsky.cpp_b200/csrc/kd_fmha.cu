@@ -476,22 +476,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             return __all_sync(0xffffffffu, mbar_wait(&kv_full[s], ph, ctl, kErrTimeoutKVFull));
         };
         // The whole warp runs the issue code (one elected lane issues each instruction).
+        // Descriptors: low words built once per tile, a constant added per K-step.
+        constexpr uint32_t dhi = sw128_desc_hi(1024);
         auto issue_s = [&](int i, int s) {
+            const uint32_t alo = sw128_desc_lo(qa + i * kTileBytes, 16), blo = sw128_desc_lo(kva + s * kTileBytes, 16);
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                mma_ss(tmem + i * 128, desc_k_sw128(qa + i * kTileBytes + off),
-                       desc_k_sw128(kva + s * kTileBytes + off), idS, kk > 0 ? 1u : 0u);
+                const uint32_t o = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
+                mma_ss(tmem + i * 128, desc_join(alo + o, dhi), desc_join(blo + o, dhi), idS, kk > 0 ? 1u : 0u);
             }
         };
         // O_i += P_i V for keys [64*half, 64*half + 64): P columns 32*half.., V rows 64*half..
         auto issue_pv = [&](int i, int s, bool acc, int half) {
+            const uint32_t vlo = sw128_desc_lo(kva + s * kTileBytes, kBoxBytes);
 #pragma unroll
             for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
                 const int kk = half * (kBlockN / 32) + k4;
-                mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
-                       desc_mn_sw128(kva + s * kTileBytes + kk * 16 * 128, kBoxBytes), idPV,
-                       (acc || kk > 0) ? 1u : 0u);
+                mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, desc_join(vlo + ((kk * 16 * 128) >> 4), dhi),
+                       idPV, (acc || kk > 0) ? 1u : 0u);
             }
         };
         auto commit = [&](uint64_t* bar) { tc_commit(bar); };
