@@ -130,8 +130,8 @@ kd_attn_status check_tensor(kd_attn_ctx* ctx, const kd_tensor* t, const char* na
             return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: ne[%d] = %lld out of range", name, i,
                         (long long)t->ne[i]);
     if (t->nb[0] != es) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "%s: dim 0 must be contiguous", name);
-    const int64_t n = t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3];
-    if (n > 0 && !t->data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: data is NULL", name);
+    const bool empty = t->ne[0] == 0 || t->ne[1] == 0 || t->ne[2] == 0 || t->ne[3] == 0;
+    if (!empty && !t->data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: data is NULL", name);
     return KD_ATTN_OK;
 }
 
