@@ -83,3 +83,40 @@ def test_set_log_callback_roundtrip(kd):
     """The process-wide logger is callable without a GPU: set, then restore the default."""
     kd.set_log_callback(lambda lvl, txt: None)
     kd.set_log_callback(None)
+
+
+def test_noalloc_argument_checks_without_a_device(kd):
+    """kd_attn_flash_ext_noalloc rejects malformed calls with ggml_flash_attn_ext's error classes
+    before it touches a device: unsupported features and layouts -> ERR_UNSUPPORTED, inconsistent
+    shapes -> ERR_INVALID_ARGUMENT.  Host tensors stand in for the operands (only their shapes and
+    strides are read).  Skipped where a GPU is present, so that no launch could ever see them."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only check")
+    bf = torch.bfloat16
+    N, H, Lq, Lk = 1, 4, 64, 96
+    q = torch.zeros(N, H, Lq, 128, dtype=bf)
+    k = torch.zeros(N, H, Lk, 128, dtype=bf)
+    v = torch.zeros(N, H, Lk, 128, dtype=bf)
+    out = torch.zeros(N, Lq, H, 128, dtype=bf)
+
+    def status(q=q, k=k, v=v, out=out, mask=None, scale=0.088, max_bias=0.0, logit_softcap=0.0):
+        return kd.lib.kd_attn_flash_ext_noalloc(kd._ref(q), kd._ref(k), kd._ref(v), kd._ref(mask), float(scale),
+                                                float(max_bias), float(logit_softcap), None, None, kd._ref(out),
+                                                None, None)
+
+    assert status(max_bias=1.0) == kd.ERR_UNSUPPORTED                       # ALiBi
+    assert status(logit_softcap=30.0) == kd.ERR_UNSUPPORTED                 # soft-capping
+    assert status(scale=-1.0) == kd.ERR_UNSUPPORTED
+    assert status(q=torch.zeros(N, H, Lq, 64, dtype=bf)) == kd.ERR_UNSUPPORTED      # head_dim 64
+    assert status(k=k.float(), v=v.float()) == kd.ERR_UNSUPPORTED           # K/V must be f16 or bf16
+    assert status(k=k.half()) == kd.ERR_UNSUPPORTED                         # K and V types differ
+    assert status(v=torch.zeros(N, H, Lk + 1, 128, dtype=bf)) == kd.ERR_INVALID_ARGUMENT
+    assert status(k=torch.zeros(N, 3, Lk, 128, dtype=bf), v=torch.zeros(N, 3, Lk, 128, dtype=bf)) == \
+        kd.ERR_INVALID_ARGUMENT                                             # 4 heads over 3 K/V heads
+    assert status(out=torch.zeros(N, Lq, H + 1, 128, dtype=bf)) == kd.ERR_INVALID_ARGUMENT
+    assert status(mask=torch.zeros(1, 1, Lq, Lk, dtype=torch.float32)) == kd.ERR_UNSUPPORTED   # f32 mask
+    assert status(mask=torch.zeros(1, 1, Lq, Lk - 1, dtype=torch.float16)) == kd.ERR_INVALID_ARGUMENT
+    assert status(mask=torch.zeros(1, 3, Lq, Lk, dtype=torch.float16)) == kd.ERR_INVALID_ARGUMENT  # 3 planes, 4 heads
+    # a well-formed call passes every check and stops at the first device query
+    assert status() == kd.ERR_CUDA
