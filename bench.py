@@ -170,6 +170,18 @@ def dist_setup():
     return ws, rank, local
 
 
+def cpu_model():
+    """The host CPU's model name (first /proc/cpuinfo entry), or platform.processor()."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def sample_rows_for_cpu(L, budget_flop, d=128):
     """query rows of one (batch, head) pair so the CPU oracle does about budget_flop of work."""
     per_row = 4.0 * L * d
@@ -220,7 +232,7 @@ def cpu_reference(cfg, seconds_target=15.0, threads=None):
         what = f"{planes} whole (batch, head) planes of {cfg['N'] * cfg['H']}"
     full_flop = 4.0 * cfg["N"] * cfg["H"] * L * L * d
     ms_full = t * 1e3 * full_flop / flop_sample
-    return {"value": flop_sample / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": flop_sample / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
             "sample": f"{what} (prologue + ggml-faithful flash_attn_ext), {t:.1f} s on {threads} threads; "
                       f"scaled by the FLOP ratio to {ms_full / 1e3:.0f} s per full call",
             "ms_per_call_scaled": ms_full}
@@ -246,7 +258,7 @@ def run_reference(args, cfg):
             "data": "synthetic (seeded Philox4x32-10 N(0,1), the reference's generator)",
             "config": {"workload": cfg["name"], "global_batch": cfg["N"], "seq_len": L_of(cfg), "heads": cfg["H"],
                        "head_dim": 128, "parallelism": "cpu", "l2": "n/a"},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -354,6 +366,70 @@ def run_other(args, cfg, ctx, kd_attn, torch, q, k, v, rope, op, out_dt, stream)
             "flash_kernel_dense_mask_ms": fa_dense_ms}
 
 
+def exchange_check(ctx, torch, dist, proj, out_full, rope, op, out_dt, ws, rank, N, L, Hs, Cs, dev, stream):
+    """After the timed sharded steps, every rank's out_full must hold every rank's heads.  Each rank
+    recomputes, with the single-GPU kd_attn_self_attention, its own heads and those of the next rank
+    (from that rank's seed) and requires the columns of its out_full -- its own written locally,
+    the peer's written over NVLink by the peer's flash kernel -- to be bit-identical.  The verdict
+    is min-reduced over the ranks, so every rank reports the same one."""
+    checked = []
+    ok = True
+    for owner in (rank, (rank + 1) % ws):
+        ins = [proj(off, owner) for off in range(3)]
+        ref = torch.empty(N, L, Cs, device=dev, dtype=out_dt)
+        ctx.self_attention(*ins, Hs, ref, rope=rope, op_type=op, stream=stream)
+        torch.cuda.synchronize()
+        got = out_full[:, :, owner * Cs:(owner + 1) * Cs]
+        same = bool(torch.equal(got, ref))
+        ndiff = 0 if same else int((got != ref).sum().item())
+        checked.append({"heads_of_rank": owner, "rows": N * L, "bit_identical": same, "elements_differing": ndiff})
+        ok = ok and same
+        del ins, ref
+    flag = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return {"status": "pass" if int(flag.item()) == 1 else "fail", "ranks": ws, "rank0_checked": checked,
+            "how": "each rank recomputes its own and the next rank's heads (kd_attn_self_attention, single GPU) "
+                   "and compares them bit for bit with its out_full copy after the timed steps; min over ranks"}
+
+
+def extra_measurements(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
+    """Single-GPU side measurements printed with the headline line.
+    cfg2: the config-2 cross-attention call (the config-1 Q projections are config 2's Q: same shape,
+          N(0,1)) and its flash kernel alone, in HBM GB/s.
+    ggml_semantics: config 1 through kd_attn_flash_ext the way ops.hpp:176 feeds it -- f32 Q
+          (rounded to f16 inside the call), f16 K/V, f32 output -- beside the same call with Q
+          already f16, whose difference is the Q-rounding kernel's share."""
+    res = {}
+    cfg2 = dict(CONFIGS[2])
+    r2 = run_other(args, cfg2, ctx, kd_attn, torch, q, None, None, rope, kd_attn.BF16, torch.bfloat16, stream)
+    res["cfg2"] = {"workload": cfg2["name"], "kv_len": r2["config"]["kv_len"], "call_ms": r2["ms_per_step"],
+                   "flash_kernel_ms": r2["flash_kernel"]["ms"], "flash_kernel_gbs": r2["flash_kernel"]["gbs"],
+                   "flash_kernel_frac_of_hbm": r2["flash_kernel"]["frac_of_hbm"],
+                   "algorithmic_bytes": r2["flash_kernel"]["algorithmic_bytes"],
+                   "bytes": "Q + O (bf16) + K + V of the valid-length-independent padded shape"}
+    N, L, C = q.shape
+    H, d = C // 128, 128
+    qf = torch.empty(N, H, L, d, device=dev)
+    q16 = torch.empty(N, H, L, d, device=dev, dtype=torch.float16)
+    k16, v16 = torch.empty_like(q16), torch.empty_like(q16)
+    ctx.qk_prologue(q, k, v, q16, k16, v16, rope=rope, stream=stream)
+    ctx.prologue(q, H, qf, rope=rope, stream=stream)
+    of = torch.empty(N, L, H, d, device=dev)
+    ms_f32q = _timed(torch, stream, lambda: ctx.flash_attn_ext(qf, k16, v16, of, stream=stream), args.steps,
+                     args.warmup)
+    ms_f16q = _timed(torch, stream, lambda: ctx.flash_attn_ext(q16, k16, v16, of, stream=stream), args.steps,
+                     args.warmup)
+    ctx.device_status()
+    flop = 4.0 * N * H * L * L * d
+    res["ggml_semantics"] = {
+        "call": "kd_attn_flash_ext, Q f32 [128, L, H, N], K/V f16, out f32 [128, H, L, N] (ops.hpp:176)",
+        "ms": ms_f32q, "tflops": flop / (ms_f32q * 1e-3) / 1e12,
+        "ms_q_already_f16": ms_f16q, "q_rounding_ms": ms_f32q - ms_f16q,
+        "q_rounding_share": (ms_f32q - ms_f16q) / ms_f32q}
+    del qf, q16, k16, v16, of
+    return res
+
+
 def hbm_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -371,6 +447,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config-2 and ggml-semantics measurements of the single-GPU line")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (profiling runs)")
     ap.add_argument("--heads", type=int, default=None, help="override the config's head count (profiling runs)")
     ap.add_argument("--frames", type=int, default=None,
@@ -403,6 +481,9 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
+        # NCCL's init lines ("... nranks N ... Init COMPLETE") show every communicator's size
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", init_method="env://", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     N, H, d = cfg["N"], cfg["H"], 128
@@ -422,10 +503,11 @@ def main():
     stream = torch.cuda.current_stream()
 
     # inputs: this rank's column shard (heads [rank*Hs, (rank+1)*Hs)) of the Q/K/V projections
-    def proj(offset):
+    def proj(offset, owner=rank):
+        """rank `owner`'s column shard of one projection (seed 1 + owner)."""
         t = torch.empty(N, L, Cs, device=dev)
         full = torch.empty(N * L * Cs, device=dev)
-        ctx.fill_randn(full, seed=1 + rank, offset=offset)
+        ctx.fill_randn(full, seed=1 + owner, offset=offset)
         t.copy_(full.view(N, L, Cs))
         return t
 
@@ -504,6 +586,11 @@ def main():
     ms = float(t.item())
     flop = 4.0 * N * H * L * L * d
     value = flop / (ms * 1e-3) / 1e12
+
+    exchange = None
+    if ws > 1:
+        exchange = exchange_check(ctx, torch, dist, proj, out_full, rope, op, out_dt, ws, rank, N, L, Hs, Cs, dev,
+                                  stream)
 
     nccl_ms = None
     if ws > 1:  # the same job with the exchange as a separate ncclAllGather + permute, for comparison
@@ -606,15 +693,22 @@ def main():
         "gpu_launches": args.steps * 2,  # prologue + flash (the barriers are NCCL kernels)
         "clocks": clk.summary(),
     }
+    if exchange is not None:
+        line["exchange_check"] = exchange["status"]
+        line["exchange_check_detail"] = exchange
+    if ws == 1 and not args.no_extra:
+        line["extra"] = extra_measurements(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream)
     if rank == 0 and not args.no_cpu_baseline:
         cb = cpu_reference(cfg, seconds_target=args.ref_seconds)
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     ctx.close()
     if ws > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if exchange is not None and exchange["status"] != "pass":
+        raise SystemExit("exchange_check failed: " + json.dumps(exchange))
 
 
 if __name__ == "__main__":

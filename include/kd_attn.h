@@ -200,32 +200,51 @@ kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_
 
 /* ---------------------------------------------------------------------------
  * Allocation-free variant of kd_attn_flash_ext.  It has no counterpart in the
- * reference: it exists for callers that cannot allocate device memory at all
- * -- code running while a CUDA graph is being captured, or embedders whose
- * device memory is owned by another allocator (a ggml backend buffer, a
- * serving runtime's arena) and who may not call cudaMalloc behind its back.
- * It needs no kd_attn_ctx (whose creation allocates) and calls no cudaMalloc,
- * cudaFree or allocating library routine.
+ * reference.  It is for callers that may not allocate device memory: embedders
+ * whose device memory belongs to another allocator (a ggml backend buffer, a
+ * serving runtime's arena) and who may not call cudaMalloc behind its back, or
+ * code that runs where the CUDA runtime forbids allocation.  It needs no
+ * kd_attn_ctx (whose creation allocates) and calls no cudaMalloc, cudaFree or
+ * allocating library routine.
  *
  * Same arguments and semantics as kd_attn_flash_ext; it runs on the calling
- * thread's current CUDA device.  Its scratch (Q rounded to the operand type
- * when Q is f32 or strided, plus the mask's tile classes) lives in one
- * statically sized device array of KD_ATTN_NOALLOC_SCRATCH_BYTES per device,
- * held from the first call until the process exits.  Problems that need more
- * scratch than that are rejected with KD_ATTN_ERR_UNSUPPORTED before anything
- * is launched (Q already in K's type with 16-byte-aligned rows needs none).
+ * thread's current CUDA device, and every buffer it is given must be device
+ * memory of that device (else KD_ATTN_ERR_INVALID_ARGUMENT).  Its scratch (Q
+ * rounded to the operand type when Q is f32 or strided, plus the mask's tile
+ * classes) lives in one statically sized device array of
+ * KD_ATTN_NOALLOC_SCRATCH_BYTES that belongs to the library's device code: it
+ * is allocated on a device when that code is loaded there -- under CUDA's
+ * default lazy module loading at this entry point's first call on the device,
+ * with CUDA_MODULE_LOADING=EAGER as soon as the library's kernels are loaded,
+ * whichever entry point is used -- and it is held until the process exits.
+ * Problems that need more scratch than that are rejected with
+ * KD_ATTN_ERR_UNSUPPORTED before anything is launched (Q already in K's type
+ * with 16-byte-aligned rows needs none).
  *   - The first call on a device looks up that array's device address; make
  *     that first call before any stream capture begins.
  *   - Every call on a device shares the one array: calls that may overlap on
  *     the GPU (different streams without ordering) race and must not be issued.
- *   - Device-side wait timeouts are bounded as in the context path, but this
- *     entry point has no context to report them through. */
+ *   - A device-side wait that runs out (bounded as in the context path) sets
+ *     a sticky error word beside the array; kd_attn_noalloc_status reads it. */
 #define KD_ATTN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
                                          const kd_tensor* mask, float scale, float max_bias,
                                          float logit_softcap, const int32_t* kv_len,
                                          const uint8_t* tile_mask, kd_tensor* out, float* lse,
                                          void* stream);
+
+/* The allocation-free path's kd_attn_device_status (no reference counterpart):
+ * synchronises `stream`, then reads and clears the current device's sticky
+ * error word of kd_attn_flash_ext_noalloc.  KD_ATTN_ERR_DEVICE_TIMEOUT means a
+ * call since the last check gave up on a wait and its output is incomplete. */
+kd_attn_status kd_attn_noalloc_status(void* stream);
+
+/* Failure-detection self-test of the allocation-free path (no reference
+ * counterpart): one bounded device wait that nothing releases, on the current
+ * device, reporting through the same error word; after wait_ms (1..10000) it
+ * gives up, and the next kd_attn_noalloc_status returns
+ * KD_ATTN_ERR_DEVICE_TIMEOUT.  Nothing faults, traps or spins without a bound. */
+kd_attn_status kd_attn_noalloc_selftest_wait(uint32_t wait_ms, void* stream);
 
 /* ---------------------------------------------------------------------------
  * The two CrossDiT call sites end to end (prologue + flash), operands staged

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -181,10 +182,14 @@ kd_attn_status make_operand_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* 
 // ------------------------------------------------------------------ scratch
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-kd_attn_status ensure_scratch(kd_attn_ctx* ctx, size_t bytes) {
+// Grows the context's scratch to at least `bytes`.  Growing happens on the first calls only.  The
+// old buffer may still be read by work queued earlier: the context's calls are ordered on the
+// call's stream (or by the caller's events into it, and the host-buffer copy streams are joined
+// back into it), so draining that one stream is enough -- other streams of the device, such as a
+// concurrent NCCL barrier, are not waited for.
+kd_attn_status ensure_scratch(kd_attn_ctx* ctx, size_t bytes, cudaStream_t st) {
     if (bytes <= ctx->scratch_bytes) return KD_ATTN_OK;
-    // growing happens on the first calls only; make sure no queued work still reads the old buffer
-    KD_CUDA(ctx, cudaDeviceSynchronize());
+    if (ctx->scratch) KD_CUDA(ctx, cudaStreamSynchronize(st));
     if (ctx->scratch) cudaFree(ctx->scratch);
     ctx->scratch = nullptr;
     ctx->scratch_bytes = 0;
@@ -294,7 +299,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 static __device__ __align__(256) unsigned g_noalloc_words[4];  // [0] sticky error bits, [1] abort flag, [2] work counter
 
 struct NoAllocDevice {
-    bool ready = false;
+    std::atomic<bool> ready{false};
     char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
     unsigned* words = nullptr; // device address of g_noalloc_words on this device
     int num_sms = 0;
@@ -302,16 +307,21 @@ struct NoAllocDevice {
 std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
 
-// Once per device, with that device current: resolve the arrays' device addresses.
+// Once per device, with that device current: resolve the arrays' device addresses.  Later calls
+// take the lock-free path (the acquire load pairs with the release store that publishes them).
 kd_attn_status noalloc_setup(NoAllocDevice** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kNoAllocMaxDevices)
         return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
     NoAllocDevice& d = g_noalloc_dev[dev];
-    if (!d.ready) {
+    if (d.ready.load(std::memory_order_acquire)) {
+        *out = &d;
+        return KD_ATTN_OK;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready.load(std::memory_order_relaxed)) {
         int major = 0, minor = 0, sms = 0;
         if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
             cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
@@ -331,9 +341,31 @@ kd_attn_status noalloc_setup(NoAllocDevice** out) {
         d.scratch = static_cast<char*>(s);
         d.words = static_cast<unsigned*>(w);
         d.num_sms = sms;
-        d.ready = true;
+        d.ready.store(true, std::memory_order_release);
     }
     *out = &d;
+    return KD_ATTN_OK;
+}
+
+// The allocation-free entry point runs on the current device and has no context tying its
+// buffers to a device: every buffer it is given must be device (or managed) memory that the
+// current device owns.  cudaPointerGetAttributes allocates nothing.
+kd_attn_status noalloc_check_ptr(const void* p, const char* name) {
+    if (!p) return KD_ATTN_OK;
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    cudaPointerAttributes a{};
+    e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(nullptr, KD_ATTN_ERR_INVALID_ARGUMENT, "%s: not a CUDA pointer (%s)", name, cudaGetErrorString(e));
+    }
+    if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+        return fail(nullptr, KD_ATTN_ERR_INVALID_ARGUMENT, "%s is not device memory", name);
+    if (a.type == cudaMemoryTypeDevice && a.device != dev)
+        return fail(nullptr, KD_ATTN_ERR_INVALID_ARGUMENT, "%s lives on device %d but the current device is %d", name,
+                    a.device, dev);
     return KD_ATTN_OK;
 }
 
@@ -406,7 +438,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     int num_sms = 0;
     unsigned long long wait_ns = 2000000000ull;
     if (ctx) {
-        if ((rc = ensure_scratch(ctx, q_bytes + cls_bytes))) return rc;
+        if ((rc = ensure_scratch(ctx, q_bytes + cls_bytes, st))) return rc;
         scr = static_cast<char*>(ctx->scratch);
         words = ctx->d_words;
         stats = reinterpret_cast<unsigned long long*>(ctx->d_words + 4);
@@ -419,6 +451,12 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
                         "(KD_ATTN_NOALLOC_SCRATCH_BYTES); pass Q in K's type with 16-byte-aligned rows, or use "
                         "kd_attn_flash_ext",
                         q_bytes + cls_bytes, kNoAllocScratchBytes);
+        if ((rc = noalloc_check_ptr(q.data, "q")) || (rc = noalloc_check_ptr(k.data, "k")) ||
+            (rc = noalloc_check_ptr(v.data, "v")) || (rc = noalloc_check_ptr(o.data, "out")) ||
+            (rc = noalloc_check_ptr(a.mask ? a.mask->data : nullptr, "mask")) ||
+            (rc = noalloc_check_ptr(a.lse, "lse")) || (rc = noalloc_check_ptr(a.kv_len, "kv_len")) ||
+            (rc = noalloc_check_ptr(a.tile_mask, "tile_mask")))
+            return rc;
         NoAllocDevice* d = nullptr;
         if ((rc = noalloc_setup(&d))) return rc;
         scr = d->scratch;
@@ -691,7 +729,7 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     // operand scratch sits after the flash core's own scratch needs: reserve them up front
     const size_t flash_extra =
         mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
-    if ((rc = ensure_scratch(ctx, flash_extra + qb + 2 * kb))) return rc;
+    if ((rc = ensure_scratch(ctx, flash_extra + qb + 2 * kb, st))) return rc;
     // The flash core carves its scratch from the start of the buffer; operands go after it.
     char* base = static_cast<char*>(ctx->scratch) + flash_extra;
     kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N);
@@ -800,7 +838,7 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     const size_t opb = align256((size_t)N * G * L * kHeadDim * 2);  // one operand for one group
     const size_t core = 3 * opb;                                     // attention_core's operand scratch
     if ((rc = ensure_copy_streams(ctx))) return rc;
-    if ((rc = ensure_scratch(ctx, core + 2 * (3 * in_slab + out_slab)))) return rc;
+    if ((rc = ensure_scratch(ctx, core + 2 * (3 * in_slab + out_slab), st))) return rc;
     char* stage = static_cast<char*>(ctx->scratch) + core;
     auto in_buf = [&](int b, int x) { return stage + ((size_t)b * 3 + x) * in_slab; };
     auto out_buf = [&](int b) { return stage + 6 * in_slab + (size_t)b * out_slab; };
@@ -1264,7 +1302,7 @@ kd_attn_status kd_attn_allgather_heads(kd_attn_ctx* ctx, const kd_tensor* shard,
     }
     Nccl* n = nccl();
     if (!n || !ctx->nccl_comm) return fail(ctx, KD_ATTN_ERR_NCCL, "context has no NCCL communicator");
-    if ((rc = ensure_scratch(ctx, shard_bytes * R))) return rc;
+    if ((rc = ensure_scratch(ctx, shard_bytes * R, st))) return rc;
     const int r = n->allGather(shard->data, ctx->scratch, shard_bytes, kNcclUint8, ctx->nccl_comm, st);
     if (r != 0) return fail(ctx, KD_ATTN_ERR_NCCL, "ncclAllGather: %s", nccl_err(n, r));
     KD_CUDA(ctx, launch_unshard_heads(ctx->scratch, full->data, (long long)Lq * N, R, (long long)row, ctx->num_sms, st));
@@ -1292,4 +1330,31 @@ extern "C" kd_attn_status kd_attn_flash_ext_noalloc(const kd_tensor* q, const kd
     if (logit_softcap != 0.f) return fail(nullptr, KD_ATTN_ERR_UNSUPPORTED, "logit_softcap must be 0");
     FlashArgs fa{q, k, v, mask, scale, kv_len, out, lse, tile_mask};
     return flash_run(nullptr, fa, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" kd_attn_status kd_attn_noalloc_status(void* stream) {
+    NoAllocDevice* d = nullptr;
+    kd_attn_status rc;
+    if ((rc = noalloc_setup(&d))) return rc;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    unsigned word = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&word, d->words, sizeof word, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(d->words, 0, sizeof word);
+    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "reading the allocation-free error word: %s",
+                                      cudaGetErrorString(e));
+    if (word)
+        return fail(nullptr, KD_ATTN_ERR_DEVICE_TIMEOUT, "device-side wait expired in the allocation-free path "
+                    "(error bits 0x%x)", word);
+    return KD_ATTN_OK;
+}
+
+extern "C" kd_attn_status kd_attn_noalloc_selftest_wait(uint32_t wait_ms, void* stream) {
+    if (wait_ms == 0 || wait_ms > 10000) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    NoAllocDevice* d = nullptr;
+    kd_attn_status rc;
+    if ((rc = noalloc_setup(&d))) return rc;
+    const cudaError_t e = launch_wait_selftest(d->words, d->words + 1, (unsigned long long)wait_ms * 1000000ull,
+                                               static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(nullptr, KD_ATTN_ERR_CUDA, "self-test launch: %s", cudaGetErrorString(e));
+    return KD_ATTN_OK;
 }

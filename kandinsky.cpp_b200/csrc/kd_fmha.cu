@@ -51,25 +51,6 @@
 
 namespace kd {
 
-// Optional pipeline-event trace for studies of the schedule.  Only a build with
-// -DKD_FMHA_TRACE=<x> has it (the shipped library does not): lane 0 of the
-// producer, the MMA warp and the first warp of each softmax warpgroup of CTA
-// (x, 0, 0) store clock64() at named events, per K/V iteration (< 512), into
-// kd_fmha_trace[role][event][iteration]; kd_fmha_trace_read copies it out.
-#ifdef KD_FMHA_TRACE
-__device__ unsigned long long kd_fmha_trace[4][8][512];
-#define KD_TRACE(role, ev, it)                                                                   \
-    do {                                                                                         \
-        if (blockIdx.x == (KD_FMHA_TRACE) && blockIdx.y == 0 && blockIdx.z == 0 && lane == 0 && \
-            (it) < 512)                                                                          \
-            kd_fmha_trace[(role)][(ev)][(it)] = clock64();                                       \
-    } while (0)
-#else
-#define KD_TRACE(role, ev, it) \
-    do {                       \
-    } while (0)
-#endif
-
 namespace {
 
 constexpr int kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB: one 128 x 128 16-bit tile
@@ -435,7 +416,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t ph = (it / kStages) & 1u;
                         ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
                         if (!ok) break;
-                        KD_TRACE(0, w, j);
                         if (lane == 0) {
                             mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
                             const CUtensorMap* map = is_v ? &tmV : &tmK;
@@ -509,7 +489,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             }
             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[i], gi & 1, ctl, kErrTimeoutP))) return false;
-            KD_TRACE(1, 1 + 2 * i, gi);
             tc_fence_after();
             issue_pv(i, s, acc, 0);
             issue_pv(i, s, acc, 1);
@@ -604,7 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const bool more = j + 1 < n_iter;
                     if (more) e_next = entry(list, j + 1);
                     if (!(ok = next_stage(sV))) break;
-                    KD_TRACE(1, 0, gq0);
                     int sK2 = -1;
                     bool early0 = false, early1 = false;
                     // Masked lists: a Q tile with no PV at this K/V tile has nothing to wait for, so its
@@ -631,7 +609,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!early0 && need(e_next, 0)) {
                             issue_s(0, sK2);
                             commit(&s_full[0]);
-                            KD_TRACE(1, 2, gq0);
                         }
                     }
                     if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV))) break;
@@ -640,7 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!early1 && need(e_next, 1)) {
                             issue_s(1, sK2);
                             commit(&s_full[1]);
-                            KD_TRACE(1, 4, gq1);
                         }
                         commit(&kv_empty[sK2]);
                         if (j + 2 == n_iter) commit(q_empty);
@@ -741,7 +717,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kbase = (int)(e >> 16) * kBlockN;
                 const uint32_t c0 = (e >> (4 * g4)) & 3u, c1 = (e >> (4 * g4 + 2)) & 3u;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], g & 1, ctl, kErrTimeoutS)))) break;
-                if ((warp & 3) == 0) KD_TRACE(2 + wg, 0, g);
                 tc_fence_after();
 
                 // Mixed tiles: add the additive mask (divided by scale, so that scale*(s + m/scale) =
@@ -775,7 +750,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 uint32_t su[128];
                 tmem_ld128_sync(tS, su);
-                if ((warp & 3) == 0) KD_TRACE(2 + wg, 1, g);
                 // Skipped halves and keys past the valid length become -inf.
                 {
                     const int lim = lk_eff - kbase;
@@ -806,7 +780,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
 #endif
                 const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
-                if ((warp & 3) == 0) KD_TRACE(2 + wg, 2, g);
                 const float m_new = fmaxf(m, m_tile);
                 const bool resc = m_new > m + kRescaleThreshold;
                 const bool warp_resc = __any_sync(0xffffffffu, resc);
@@ -859,7 +832,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 };
                 p_chunk(0);
                 p_chunk(1);
-                if ((warp & 3) == 0) KD_TRACE(2 + wg, 3, g);
                 // Rescale O_i (PV_i of the previous tile is complete: its commit preceded S_i's).  It only
                 // has to precede the first PV_i MMA of this tile; the first 64 scores are dead here.
                 if (warp_resc && k > 0) {
@@ -884,7 +856,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l += rs0 + rs1;
                 tc_fence_before();
                 mbar_arrive(&p_full[wg]);
-                if ((warp & 3) == 0) KD_TRACE(2 + wg, 4, g);
                 ++g;
                 ++k;
             }
@@ -974,12 +945,6 @@ int regs_t() {
 
 int fmha_smem_bytes() { return Layout<true>::kSmemAlloc; }
 
-#ifdef KD_FMHA_TRACE
-extern "C" int kd_fmha_trace_read(unsigned long long* host, unsigned long long n) {
-    if (n > sizeof(kd_fmha_trace) / sizeof(unsigned long long)) n = sizeof(kd_fmha_trace) / sizeof(unsigned long long);
-    return (int)cudaMemcpyFromSymbol(host, kd_fmha_trace, n * sizeof(unsigned long long));
-}
-#endif
 
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                         const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st) {

@@ -42,7 +42,7 @@ EXPORTED = [
     "kd_attn_flash_ext_noalloc", "kd_attn_self_attention_host", "kd_attn_qk_prologue",
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
-    "kd_attn_selftest_wait",
+    "kd_attn_selftest_wait", "kd_attn_noalloc_status", "kd_attn_noalloc_selftest_wait",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -151,6 +151,10 @@ def _load():
     L.kd_attn_flash_ext_noalloc.argtypes = [T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P,
                                             P]
     L.kd_attn_flash_ext_noalloc.restype = st
+    L.kd_attn_noalloc_status.argtypes = [P]
+    L.kd_attn_noalloc_status.restype = st
+    L.kd_attn_noalloc_selftest_wait.argtypes = [ctypes.c_uint32, P]
+    L.kd_attn_noalloc_selftest_wait.restype = st
     L.kd_attn_symmetric_alloc.argtypes = [P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
     L.kd_attn_symmetric_alloc.restype = st
     L.kd_attn_symmetric_free.argtypes = [P, P, P]
@@ -418,10 +422,12 @@ def flash_attn_ext_noalloc(q, k, v, out, mask=None, scale=None, kv_len=None, lse
                            logit_softcap=0.0, tile_mask=None, stream=None):
     """kd_attn_flash_ext_noalloc: flash_attn_ext without a Context and without any device allocation.
 
-    For callers that may not allocate (graph capture, foreign memory arenas).  Runs on the current
-    CUDA device; its scratch is a fixed NOALLOC_SCRATCH_BYTES device array shared by every call on
-    that device, so calls must not overlap on the GPU.  Make the first call before any stream capture.
-    Problems needing more scratch are rejected with ERR_UNSUPPORTED.
+    For callers that may not allocate device memory (an embedder whose memory belongs to another
+    allocator).  Runs on the current CUDA device, whose memory every tensor must be in; its scratch
+    is a fixed NOALLOC_SCRATCH_BYTES device array shared by every call on that device, so calls must
+    not overlap on the GPU.  Make the first call on a device before any stream capture.  Problems
+    needing more scratch are rejected with ERR_UNSUPPORTED.  ``noalloc_status`` reports whether a
+    device-side wait ran out since the last check.
     """
     if scale is None:
         scale = 1.0 / (q.shape[-1] ** 0.5)
@@ -431,6 +437,20 @@ def flash_attn_ext_noalloc(q, k, v, out, mask=None, scale=None, kv_len=None, lse
     if rc != OK:
         raise KdAttnError(rc, "kd_attn_flash_ext_noalloc failed (details on stderr)")
     return out
+
+
+def noalloc_status(stream=None):
+    """kd_attn_noalloc_status: synchronise, read and clear the allocation-free path's error word."""
+    rc = lib.kd_attn_noalloc_status(_stream_ptr(stream))
+    if rc != OK:
+        raise KdAttnError(rc, "kd_attn_noalloc_status (details on stderr)")
+
+
+def noalloc_selftest_wait(wait_ms=50, stream=None):
+    """kd_attn_noalloc_selftest_wait: one bounded device wait that runs out on purpose."""
+    rc = lib.kd_attn_noalloc_selftest_wait(int(wait_ms), _stream_ptr(stream))
+    if rc != OK:
+        raise KdAttnError(rc, "kd_attn_noalloc_selftest_wait (details on stderr)")
 
 
 def attention(ctx: Context, q, k, v, n_head, mask=None, flash=True, op_type=F16, out_dtype=None, stream=None):

@@ -13,7 +13,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "_build", "libkd_oracle.so")
 PIN = os.path.join(HERE, "_ref", "kd_ref_pin")
-REF_DEFAULT = "/root/reference"
+# The reference checkout: $KD_REFERENCE_DIR, else a sibling directory of this repository named
+# "reference" (the layout in which the pin recipe is run); absent on machines without it.
+REF_SIBLING = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 
 def _stale(target, deps):
@@ -40,7 +42,7 @@ def build_oracle(force=False, verbose=False):
 
 def build_ref_pin(ref=None, verbose=False):
     """Compile oracle/_ref/kd_ref_pin when the reference tree is present; returns its path or None."""
-    ref = ref or os.environ.get("KD_REFERENCE_DIR", REF_DEFAULT)
+    ref = ref or os.environ.get("KD_REFERENCE_DIR") or REF_SIBLING
     if not os.path.isfile(os.path.join(ref, "src", "rope.hpp")):
         return PIN if os.path.exists(PIN) else None
     subprocess.run(["make", "-s", "-C", os.path.join(HERE, "ref_pin"), f"REF={ref}"], check=True,
