@@ -3,7 +3,7 @@
 Rank r runs kd_attn_self_attention on its column shard of the config-1-like projections and
 kd_attn_allgather_heads (one ncclAllGather + permute) rebuilds [C, L, N]; the result must equal
 the single-GPU call on the full projections bit for bit (heads are independent and the kernels
-are deterministic).  Child processes, one per GPU, 127.0.0.1 rendezvous, NVLS off.
+are deterministic).  The fused exchange's result is also checked against the fp64 CPU oracle.  Child processes, one per GPU, 127.0.0.1 rendezvous, NVLS off.
 """
 import os
 import socket
@@ -129,6 +129,8 @@ def _rank_main_fused(rank, world, port, out_dir):
                 single.device_status()
             res[str(dt) + " cross"] = (out_full.cpu(), ref.cpu())
             ctx.symmetric_free(out_full)
+        if rank == 0:
+            res["inputs"] = [x.cpu() for x in full_in]
     torch.save(res, os.path.join(out_dir, f"fused_r{rank}.pt"))
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
@@ -145,5 +147,15 @@ def test_two_gpu_fused_exchange_matches_single_gpu(tmp_path):
                        start_method="spawn")
     for r in range(2):
         res = torch.load(os.path.join(str(tmp_path), f"fused_r{r}.pt"))
+        inputs = res.pop("inputs", None)
         for got, ref in res.values():
             assert torch.equal(got, ref)
+        if inputs is not None:
+            # every rank's exchanged copy also against the fp64 CPU oracle (both ranks' heads)
+            import oracle
+            from helpers import assert_gates
+            q, k, v = (x.numpy() for x in inputs)
+            tab = oracle.visual_rope_table((4, 16, 16), scale=(1, 2, 2))
+            exact = oracle.self_attention(q, k, v, 8, rope_table=tab, kv_type=oracle.BF16, mode=oracle.EXACT)
+            got = res[str(torch.float32)][0].numpy()
+            assert_gates(got, exact, label="2-GPU fused exchange (f32 out) vs oracle")
