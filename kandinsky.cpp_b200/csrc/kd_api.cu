@@ -179,6 +179,22 @@ kd_attn_status make_operand_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* 
     return KD_ATTN_OK;
 }
 
+// The flash output [128, H, Lq, N] (16-bit) for TMA stores of 128-row O tiles: {64, 1, 128, 1} box,
+// 128-byte swizzle.  Returns false (and the kernel stores rows directly) if the driver rejects it.
+bool make_out_map(CUtensorMap* map, const void* data, int32_t type, int64_t H, int64_t Lq, int64_t N,
+                  const uint64_t nb[4]) {
+    PFN_encodeTiled_t enc = get_encode();
+    if (!enc || !aligned16(data)) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)H, (cuuint64_t)Lq, (cuuint64_t)N};
+    cuuint64_t strides[3] = {nb[1], nb[2], nb[3]};
+    cuuint32_t box[4] = {64, 1, (cuuint32_t)kBlockM, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(map, type == KD_ATTN_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+               const_cast<void*>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------------ scratch
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -552,9 +568,17 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     p.head_pairs = (tiled && mh == 1 && H % 2 == 0 && a.n_peers == 0) ? 1 : 0;
     p.out_v8 = (reinterpret_cast<uintptr_t>(o.data) % 32 == 0 && onb[1] % 32 == 0 && onb[2] % 32 == 0 &&
                 onb[3] % 32 == 0) ? 1 : 0;
+    // short-key calls (the kernel's double-buffered-Q instantiation) with a 16-bit output that is not
+    // exchanged with peers write their O tiles with TMA stores
+    CUtensorMap tmO = tmQ;  // never dereferenced unless p.tma_out
+    p.tma_out = 0;
+    if (!tiled && Lk > 0 && Lk <= kQ2MaxKeys && a.n_peers == 0 &&
+        (o.type == KD_ATTN_TYPE_BF16 || o.type == KD_ATTN_TYPE_F16) &&
+        make_out_map(&tmO, o.data, o.type, H, Lq, N, onb))
+        p.tma_out = 1;
     // abort flag and work counter start at zero for every launch
     KD_CUDA(ctx, cudaMemsetAsync(words + 1, 0, 2 * sizeof(unsigned), st));
-    KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
+    KD_CUDA(ctx, launch_fmha(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, tmO, p, st));
     return KD_ATTN_OK;
 }
 

@@ -61,20 +61,26 @@ constexpr int kOutSlots = 4;  // units published to the copy-out warp and not ye
 // Shared-memory layout of one instantiation.  The K/V ring gets every byte the 227 KB allow: the
 // masked kernel keeps two kept-tile lists (16 KB) and 4 stages; the dense kernel visits every tile
 // in order, needs no lists, and gets a 5th stage (its measured bottleneck was waiting for K/V
-// tiles to land with only 2 tiles of lookahead per Q tile pair).
-template <bool kSparse>
+// tiles to land with only 2 tiles of lookahead per Q tile pair).  The short-key instantiation
+// (kQ2: unmasked, a few K/V tiles per unit, as in cross-attention against text states) trades two
+// ring stages for a second Q buffer and publishes units two ahead instead of one, so the next
+// unit's Q streams in from HBM while this unit computes rather than after its last S MMA.
+template <bool kSparse, bool kQ2 = false>
 struct Layout {
-    static constexpr int kStages = kSparse ? 4 : 5;
+    static constexpr int kQBufs = kQ2 ? 2 : 1;
+    static constexpr int kListBufs = kQ2 ? 3 : 2;   // unit descriptors in flight
+    static constexpr int kStages = kSparse ? 4 : (kQ2 ? 3 : 5);
     static constexpr int kSmemQ = 0;
-    static constexpr int kSmemKV = kSmemQ + kQTiles * kTileBytes;
+    static constexpr int kSmemKV = kSmemQ + kQBufs * kQTiles * kTileBytes;
     static constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
-    // q_full, q_empty, kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full,
-    // o_free, list_full, list_empty, drain, then kOutSlots each of out_full, out_empty
-    static constexpr int kNumBars = 2 + 2 * kStages + 14 + 1 + 2 * kOutSlots;
+    // q_full[2], q_empty[2], kv_full[S], kv_empty[S], then 2 each of s_full, p_full, p_half, o_full,
+    // o_free, then drain, kOutSlots each of out_full, out_empty, then 3 each of list_full, list_empty
+    static constexpr int kNumBars = 4 + 2 * kStages + 10 + 1 + 2 * kOutSlots + 6;
     static constexpr int kSmemTmemSlot = kSmemBar + kNumBars * 8;
-    // unit, n_kept, lk_eff, last0, last1 per list buffer, then the copy-out ring's unit per slot
+    // unit, n_kept, lk_eff per list buffer (3 each), last0/last1 per list buffer (6), then the
+    // copy-out ring's unit per slot
     static constexpr int kSmemUnit = kSmemTmemSlot + 16;
-    static constexpr int kSmemList = (kSmemUnit + (10 + kOutSlots) * 4 + 15) & ~15;  // 2 lists (masked only)
+    static constexpr int kSmemList = (kSmemUnit + (15 + kOutSlots) * 4 + 15) & ~15;  // 2 lists (masked only)
     static constexpr int kSmemTotal = kSmemList + (kSparse ? 2 * kMaxKvTiles * 4 : 0);
     static constexpr int kSmemAlloc = kSmemTotal + 1024;  // slack to align the tiles to 1024 bytes
     static_assert(kSmemAlloc <= 232448, "shared memory budget");
@@ -101,6 +107,7 @@ constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8 between r
 #define KD_FMHA_MAX3 1
 #endif
 constexpr uint32_t kPolyPairs = KD_FMHA_POLY_PAIRS;
+
 
 // A list entry's class bits cover the unit's four 64-row groups, two per Q tile: Q tile i needs
 // the K/V tile unless all four of its (row group, key half) classes are "skip".
@@ -165,14 +172,18 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v
                           Pack2<__half>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
 
-template <typename T, typename TO, bool kSparse, bool kPairs>
+template <typename T, typename TO, bool kSparse, bool kPairs, bool kQ2>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const FmhaParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    const FmhaParams p) {
+    static_assert(!(kQ2 && (kSparse || kPairs)), "the double-buffered Q layout is a dense-list instantiation");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    using L = Layout<kSparse>;
+    using L = Layout<kSparse, kQ2>;
     constexpr int kStages = L::kStages;
+    constexpr int kQBufs = L::kQBufs;
+    constexpr int kLB = L::kListBufs;
     constexpr int kSmemQ = L::kSmemQ;
     constexpr int kSmemKV = L::kSmemKV;
 
@@ -203,26 +214,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kSmemBar);
-    uint64_t* q_full = bars + 0;
-    uint64_t* q_empty = bars + 1;
-    uint64_t* kv_full = bars + 2;
+    uint64_t* q_full = bars + 0;             // [kQBufs] Q tiles of a unit landed
+    uint64_t* q_empty = bars + 2;            // [kQBufs] the last S MMA of the unit using it completed
+    uint64_t* kv_full = bars + 4;
     uint64_t* kv_empty = kv_full + kStages;
     uint64_t* s_full = kv_empty + kStages;   // [2]
     uint64_t* p_full = s_full + 2;           // [2]
     uint64_t* p_half = s_full + 4;           // [2] first 64 keys of P_i written (split hand-off only)
     uint64_t* o_full = s_full + 6;           // [2] last PV_i of a unit complete
     uint64_t* o_free = s_full + 8;           // [2] epilogue has read O_i out of TMEM
-    uint64_t* list_full = s_full + 10;       // [2] unit descriptor + kept-tile list published
-    uint64_t* list_empty = s_full + 12;      // [2] every consumer is done with that list buffer
-    uint64_t* drain = s_full + 14;
-    uint64_t* out_full = s_full + 15;        // [kOutSlots] a unit's rows are stored locally (256 arrivals)
+    uint64_t* drain = s_full + 10;
+    uint64_t* out_full = s_full + 11;        // [kOutSlots] a unit's rows are stored locally (256 arrivals)
     uint64_t* out_empty = out_full + kOutSlots;  // [kOutSlots] the copy-out warp is done with the slot
+    uint64_t* list_full = out_empty + kOutSlots;  // [kLB] unit descriptor + kept-tile list published
+    uint64_t* list_empty = list_full + 3;         // [kLB] every consumer is done with that list buffer
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kSmemTmemSlot);
-    int* s_unit = reinterpret_cast<int*>(smem + L::kSmemUnit);  // [2] unit index, -1 = no more work
-    int* s_nkept = s_unit + 2;                                   // [2] kept K/V tiles of the unit
-    int* s_lkeff = s_unit + 4;                                   // [2] valid keys of the unit's sequence
-    int* s_last = s_unit + 6;                                    // [2][2] last list entry Q tile i needs, -1: none
-    int* s_out_unit = s_unit + 10;                               // [kOutSlots] unit to copy out, -1 = finished
+    int* s_unit = reinterpret_cast<int*>(smem + L::kSmemUnit);  // [kLB] unit index, -1 = no more work
+    int* s_nkept = s_unit + 3;                                   // [kLB] kept K/V tiles of the unit
+    int* s_lkeff = s_unit + 6;                                   // [kLB] valid keys of the unit's sequence
+    int* s_last = s_unit + 9;                                    // [kLB][2] last list entry Q tile i needs, -1: none
+    int* s_out_unit = s_unit + 15;                               // [kOutSlots] unit to copy out, -1 = finished
     // [2][kMaxKvTiles] kept-tile lists, masked kernel only; the dense kernel's entry j is tile j, all full
     uint32_t* lists = kSparse ? reinterpret_cast<uint32_t*>(smem + L::kSmemList) : nullptr;
     auto entry = [](const uint32_t* list, int j) -> uint32_t {
@@ -230,8 +241,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
+        // kQ2 with TMA output stores: a unit's Q buffer doubles as the staging area of its two O tiles,
+        // so it is free again once the last S MMA has completed AND both warpgroups' stores have read it
+        const uint32_t q_empty_count = (kQ2 && p.tma_out) ? 3u : 1u;
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], q_empty_count);
+        }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
@@ -242,6 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&p_half[i], kBlockM);
             mbar_init(&o_full[i], 1);
             mbar_init(&o_free[i], kBlockM);
+        }
+        for (int i = 0; i < 3; ++i) {
             mbar_init(&list_full[i], 32);
             mbar_init(&list_empty[i], kListConsumers);
         }
@@ -278,6 +296,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
 
+    // Loads a unit's two Q tiles into the next Q buffer, once the last S MMA of the unit that used that
+    // buffer before has completed (q_uses counts the units whose Q was loaded so far).  The producer
+    // warp does this; in the short-key instantiation the scheduler warp does it right after publishing
+    // the unit, about one unit ahead of its use, so the HBM latency of Q overlaps a whole unit.
+    auto load_q = [&](const UnitGeo& ug, uint32_t& q_uses) -> bool {
+        const int qb = (int)(q_uses % kQBufs);
+        if (q_uses >= (uint32_t)kQBufs &&
+            !__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], (q_uses / kQBufs - 1) & 1, ctl, kErrTimeoutQ)))
+            return false;
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&q_full[qb], kQTiles * kTileBytes);
+#pragma unroll
+            for (int i = 0; i < kQTiles; ++i)
+#pragma unroll
+                for (int bx = 0; bx < 2; ++bx)
+                    tma_load_4d(smem + kSmemQ + (qb * kQTiles + i) * kTileBytes + bx * kBoxBytes, &tmQ, &q_full[qb],
+                                bx * 64, ug.row0[i], ug.head[i], ug.n);
+        }
+        __syncwarp();
+        ++q_uses;
+        return true;
+    };
+    // Abort path: bounded wait (ignoring the abort flag) for the Q copies still in flight.
+    auto drain_q = [&](uint32_t q_uses) {
+        for (uint32_t k = (q_uses > (uint32_t)kQBufs ? q_uses - kQBufs : 0u); k < q_uses; ++k)
+            mbar_wait(&q_full[k % kQBufs], (k / kQBufs) & 1u, ctl, kErrTimeoutDrain, false);
+    };
+
     if (warp == 2) {
         // ------------------------------------------------------------ work scheduler + list builder
         // Takes units (256 query rows of one head and sequence) from the global counter in increasing
@@ -285,11 +331,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // it publishes the list of K/V tiles to visit: entry = (tile << 16) | 2-bit class per
         // (64-row group g, 64-key half hh) at bit 4g + 2hh; without a mask every tile is FULL and the
         // kv_len / Lk tail is masked by index.  Double-buffered: unit t+1's list is built while unit t runs.
+        uint32_t q_uses = 0;  // kQ2: units whose Q this warp loaded
+        bool q_ok = true;
         for (int t = 0;; ++t) {
-            const int b = t & 1;
-            // one unit ahead of the consumers: poll slowly so the softmax warps keep the issue slots
-            if (t >= 2 && !__all_sync(0xffffffffu, mbar_wait(&list_empty[b], ((t >> 1) - 1) & 1, ctl,
-                                                               kErrTimeoutList, true, 2000)))
+            const int b = t % kLB;
+            // ahead of the consumers: poll slowly so the softmax warps keep the issue slots (faster
+            // when this warp also issues the Q loads)
+            if (t >= kLB && !__all_sync(0xffffffffu, mbar_wait(&list_empty[b], ((t / kLB) - 1) & 1, ctl,
+                                                               kErrTimeoutList, true, kQ2 ? 200 : 2000)))
                 break;
             int u = 0;
             if (lane == 0) u = (int)atomicAdd(p.work_counter, 1u);
@@ -367,7 +416,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
             mbar_arrive(&list_full[b]);  // every lane: releases its own list writes
+            if constexpr (kQ2) {
+                if (count > 0 && !(q_ok = load_q(ug, q_uses))) break;
+            }
         }
+        if (!q_ok) drain_q(q_uses);
     } else if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -379,8 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t q_uses = 0;  // units whose Q was loaded
         bool ok = true;
         for (int t = 0; ok; ++t) {
-            const int b = t & 1;
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int b = t % kLB;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t / kLB) & 1, ctl, kErrTimeoutList)))) break;
             const int u = s_unit[b];
             if (u < 0) break;
             const int n_iter = s_nkept[b];
@@ -389,21 +442,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int hk0 = ug.head[0] / p.rk2, hk1 = ug.head[1] / p.rk2;
             const uint32_t* list = kSparse ? lists + b * kMaxKvTiles : nullptr;
             if (n_iter > 0) {
-                // Q buffer is free once the previous unit's last S MMA has completed
-                if (q_uses > 0 &&
-                    !(ok = __all_sync(0xffffffffu, mbar_wait(q_empty, (q_uses - 1) & 1, ctl, kErrTimeoutQ))))
-                    break;
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
-#pragma unroll
-                    for (int i = 0; i < kQTiles; ++i)
-#pragma unroll
-                        for (int bx = 0; bx < 2; ++bx)
-                            tma_load_4d(smem + kSmemQ + i * kTileBytes + bx * kBoxBytes, &tmQ, q_full, bx * 64,
-                                        ug.row0[i], ug.head[i], n);
+                if constexpr (!kQ2) {  // (the scheduler warp loads Q in the short-key instantiation)
+                    if (!(ok = load_q(ug, q_uses))) break;
                 }
-                __syncwarp();
-                ++q_uses;
                 for (int j = 0; j < n_iter && ok; ++j) {
                     const int kt = (int)(entry(list, j) >> 16);
                     // ring order per entry: K, V -- or for head-pair units K(head 0), K(head 1),
@@ -435,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) {
             // Abort path: wait (bounded, ignoring the abort flag) until every copy this warp issued has
             // landed, so no TMA write targets shared memory after the CTA exits.
-            if (q_uses > 0) mbar_wait(q_full, (q_uses - 1) & 1, ctl, kErrTimeoutDrain, false);
+            drain_q(q_uses);
             for (uint32_t k = (it > (uint32_t)kStages ? it - kStages : 0u); k < it; ++k)
                 mbar_wait(&kv_full[k % kStages], (k / kStages) & 1u, ctl, kErrTimeoutDrain, false);
         }
@@ -446,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
         constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
         uint32_t it = 0;       // K/V ring position
-        uint32_t units = 0;    // units with at least one tile: phase of q_full
+        uint32_t units = 0;    // units with at least one tile: Q buffer units % kQBufs and its phase
         bool issued = false;
 
         auto next_stage = [&](int& s) -> bool {
@@ -458,8 +499,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The whole warp runs the issue code (one elected lane issues each instruction).
         // Descriptors: low words built once per tile, a constant added per K-step.
         constexpr uint32_t dhi = sw128_desc_hi(1024);
-        auto issue_s = [&](int i, int s) {
-            const uint32_t alo = sw128_desc_lo(qa + i * kTileBytes, 16), blo = sw128_desc_lo(kva + s * kTileBytes, 16);
+        uint32_t qbuf = 0;     // Q buffer of the current unit
+        auto issue_s = [&](int i, int s, uint32_t qb) {
+            const uint32_t alo = sw128_desc_lo(qa + (qb * kQTiles + i) * kTileBytes, 16),
+                           blo = sw128_desc_lo(kva + s * kTileBytes, 16);
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
                 const uint32_t o = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
@@ -500,10 +543,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S_i(next) is always issued after PV_i(now), so P_i's TMEM is read before S_i overwrites it.
         uint32_t gq0 = 0, gq1 = 0;   // needed tiles so far, per Q tile: phase of p_full[i]
         uint32_t uq0 = 0, uq1 = 0;   // units in which Q tile i had work: phase of o_free[i]
+        bool pre = false;            // kQ2: S0(0) and S1(0) of this unit were issued by the previous unit
         bool ok = true;
         for (int t = 0; ok; ++t) {
-            const int b = t & 1;
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int b = t % kLB;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t / kLB) & 1, ctl, kErrTimeoutList)))) break;
             const int u = s_unit[b];
             if (u < 0) break;
             const int n_iter = s_nkept[b];
@@ -513,7 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&list_empty[b]);
                 continue;
             }
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(q_full, units & 1, ctl, kErrTimeoutQ)))) break;
+            qbuf = units % kQBufs;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qbuf], (units / kQBufs) & 1, ctl, kErrTimeoutQ))))
+                break;
             bool first0 = true, first1 = true;
             // PV_i for K/V tile j when Q tile i needs it; the first one of a unit overwrites O_i, so
             // the previous unit's epilogue must have read O_i first (o_free)
@@ -533,13 +579,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int sK0 = 0, sK1 = 0;
                 if (!(ok = next_stage(sK0)) || !(ok = next_stage(sK1))) break;
                 tc_fence_after();
-                issue_s(0, sK0);
+                issue_s(0, sK0, qbuf);
                 commit(&s_full[0]);
-                issue_s(1, sK1);
+                issue_s(1, sK1, qbuf);
                 commit(&s_full[1]);
                 commit(&kv_empty[sK0]);
                 commit(&kv_empty[sK1]);
-                if (n_iter == 1) commit(q_empty);
+                if (n_iter == 1) commit(&q_empty[qbuf]);
                 issued = true;
                 for (int j = 0; j < n_iter; ++j) {
                     const bool more = j + 1 < n_iter;
@@ -548,35 +594,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!(ok = pv_tile(0, j, first0, gq0, uq0, last0, sV0))) break;
                     if (more) {
                         if (!(ok = next_stage(sK0n)) || !(ok = next_stage(sK1n))) break;
-                        issue_s(0, sK0n);
+                        issue_s(0, sK0n, qbuf);
                         commit(&s_full[0]);
                     }
                     if (!(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV1))) break;
                     commit(&kv_empty[sV0]);
                     commit(&kv_empty[sV1]);
                     if (more) {
-                        issue_s(1, sK1n);
+                        issue_s(1, sK1n, qbuf);
                         commit(&s_full[1]);
                         commit(&kv_empty[sK0n]);
                         commit(&kv_empty[sK1n]);
-                        if (j + 2 == n_iter) commit(q_empty);
+                        if (j + 2 == n_iter) commit(&q_empty[qbuf]);
                     }
                 }
             } else {
                 int sK = 0, sV = 0;
-                if (!(ok = next_stage(sK))) break;
-                tc_fence_after();
                 uint32_t e_next = entry(list, 0);
-                if (need(e_next, 0)) {
-                    issue_s(0, sK);
-                    commit(&s_full[0]);
+                if (!pre) {
+                    if (!(ok = next_stage(sK))) break;
+                    tc_fence_after();
+                    if (need(e_next, 0)) {
+                        issue_s(0, sK, qbuf);
+                        commit(&s_full[0]);
+                    }
+                    if (need(e_next, 1)) {
+                        issue_s(1, sK, qbuf);
+                        commit(&s_full[1]);
+                    }
+                    commit(&kv_empty[sK]);
+                    if (n_iter == 1) commit(&q_empty[qbuf]);  // the unit's last S MMA is issued: Q may be replaced
                 }
-                if (need(e_next, 1)) {
-                    issue_s(1, sK);
-                    commit(&s_full[1]);
-                }
-                commit(&kv_empty[sK]);
-                if (n_iter == 1) commit(q_empty);  // the unit's last S MMA is issued: Q may be replaced
+                pre = false;
                 issued = true;
                 for (int j = 0; j < n_iter; ++j) {
                     const uint32_t e = e_next;
@@ -594,11 +643,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (early0 || early1) {
                             if (!(ok = next_stage(sK2))) break;
                             if (early0) {
-                                issue_s(0, sK2);
+                                issue_s(0, sK2, qbuf);
                                 commit(&s_full[0]);
                             }
                             if (early1) {
-                                issue_s(1, sK2);
+                                issue_s(1, sK2, qbuf);
                                 commit(&s_full[1]);
                             }
                         }
@@ -607,19 +656,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (more) {
                         if (sK2 < 0 && !(ok = next_stage(sK2))) break;
                         if (!early0 && need(e_next, 0)) {
-                            issue_s(0, sK2);
+                            issue_s(0, sK2, qbuf);
+                            commit(&s_full[0]);
+                        }
+                    }
+                    // Short-key instantiation, last tile of the unit: the next unit's Q is already
+                    // loading (the scheduler warp issued it a unit ahead), so its S0(0) goes out right
+                    // after PV0(last) -- softmax warpgroup 0 then starts the next unit as soon as its
+                    // epilogue ends instead of waiting for warpgroup 1's last P.  S1(0) follows PV1(last).
+                    int sKn = -1;
+                    uint32_t qbn = 0;
+                    int nn = 0;
+                    if (kQ2 && !more) {
+                        const int bn = (t + 1) % kLB;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[bn], ((t + 1) / kLB) & 1, ctl,
+                                                                     kErrTimeoutList))))
+                            break;
+                        nn = s_unit[bn] >= 0 ? s_nkept[bn] : 0;
+                        if (nn > 0) {
+                            qbn = (units + 1) % kQBufs;
+                            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qbn], ((units + 1) / kQBufs) & 1,
+                                                                         ctl, kErrTimeoutQ))))
+                                break;
+                            if (!(ok = next_stage(sKn))) break;
+                            tc_fence_after();
+                            issue_s(0, sKn, qbn);
                             commit(&s_full[0]);
                         }
                     }
                     if (need(e, 1) && !(ok = pv_tile(1, j, first1, gq1, uq1, last1, sV))) break;
                     commit(&kv_empty[sV]);
+                    if (sKn >= 0) {
+                        issue_s(1, sKn, qbn);
+                        commit(&s_full[1]);
+                        commit(&kv_empty[sKn]);
+                        if (nn == 1) commit(&q_empty[qbn]);
+                        pre = true;
+                    }
                     if (more) {
                         if (!early1 && need(e_next, 1)) {
-                            issue_s(1, sK2);
+                            issue_s(1, sK2, qbuf);
                             commit(&s_full[1]);
                         }
                         commit(&kv_empty[sK2]);
-                        if (j + 2 == n_iter) commit(q_empty);
+                        if (j + 2 == n_iter) commit(&q_empty[qbuf]);
                     }
                 }
             }
@@ -698,8 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         int t = 0;  // units taken (the last, u < 0, ends the loop): also the copy-out ring position
         for (; ok; ++t) {
-            const int b = t & 1;
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t >> 1) & 1, ctl, kErrTimeoutList)))) break;
+            const int b = t % kLB;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&list_full[b], (t / kLB) & 1, ctl, kErrTimeoutList)))) break;
             const int u = s_unit[b];
             if (u < 0) break;
             const int n_iter = s_nkept[b];
@@ -751,15 +831,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t su[128];
                 tmem_ld128_sync(tS, su);
                 // Skipped halves and keys past the valid length become -inf.
-                {
-                    const int lim = lk_eff - kbase;
-                    const int lim0 = c0 == kTileSkip ? 0 : lim;
-                    const int lim1 = c1 == kTileSkip ? 0 : lim;
-                    if (lim0 < 64 || lim1 < 128) {
+                const int lim = lk_eff - kbase;
+                const int lim0 = c0 == kTileSkip ? 0 : lim;
+                const int lim1 = c1 == kTileSkip ? 0 : lim;
+                if (lim0 < 64 || lim1 < 128) {
 #pragma unroll
-                        for (int c = 0; c < 128; ++c)
-                            if (c >= (c < 64 ? lim0 : lim1)) su[c] = __float_as_uint(-INFINITY);
-                    }
+                    for (int c = 0; c < 128; ++c)
+                        if (c >= (c < 64 ? lim0 : lim1)) su[c] = __float_as_uint(-INFINITY);
                 }
                 float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #if KD_FMHA_MAX3
@@ -800,6 +878,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // P for 32 keys -> 16 packed columns of S_i's TMEM
                 auto p_chunk = [&](int c) {
                     uint32_t pk[16];
+                    // Short-key instantiation: a 32-key chunk wholly past the valid keys (the padded
+                    // tail of a text sequence) is all zeros -- no exponentials.  The warp-uniform
+                    // branch stays out of the long-key kernel, whose chunks the compiler interleaves.
+                    if constexpr (kQ2) {
+                        if (32 * c >= (c < 2 ? lim0 : lim1)) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+                            tmem_st16(tS + c * 16, pk);
+                            return;
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         float xa, xb;
@@ -874,8 +963,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld128_sync(tO, ov);
                 tc_fence_before();
                 mbar_arrive(&o_free[wg]);  // the next unit's PV_i may overwrite O_i now
+                const uint32_t qb_unit = units % kQBufs;  // the unit's Q buffer (dense lists: every unit has work)
                 ++units;
                 const float inv = l > 0.f ? 1.0f / l : 0.f;
+                if constexpr (kQ2 && !std::is_same<TO, float>::value) {
+                    if (p.tma_out) {
+                        // Short-key epilogue: the O tile goes to shared memory (this unit's Q tile wg, no
+                        // longer read once o_full fired) in the swizzled layout of a TMA tile, and one thread
+                        // writes it with two tensor stores -- whole 128-byte lines instead of 32-byte pieces
+                        // of 32 rows per instruction, whose drain held up the warpgroup's next unit.
+                        const uint32_t stg = smem_u32(smem + kSmemQ + (qb_unit * kQTiles + wg) * kTileBytes);
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                w[i] = Pack2<TO>::pack(__uint_as_float(ov[8 * c + 2 * i]) * inv,
+                                                       __uint_as_float(ov[8 * c + 2 * i + 1]) * inv);
+                            st_shared_v4(stg + (c >> 3) * kBoxBytes + (uint32_t)r * 128u +
+                                             ((uint32_t)((c & 7) ^ (r & 7)) << 4),
+                                         w[0], w[1], w[2], w[3]);
+                        }
+                        fence_proxy_async_smem();
+                        named_bar_sync(1 + wg, kBlockM);
+                        if (r == 0) {
+                            const int row0 = wg ? ug.row0[1] : ug.row0[0];
+#pragma unroll
+                            for (int bx = 0; bx < 2; ++bx) tma_store_4d(&tmO, stg + bx * kBoxBytes, bx * 64, h, row0, n);
+                            bulk_commit_group();
+                            bulk_wait_group_read0();  // the staging tile has been read: the Q buffer may refill
+                            mbar_arrive(&q_empty[qb_unit]);
+                        }
+                        orow = nullptr;
+                    }
+                }
                 if (orow) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -902,6 +1023,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // tell the copy-out warp there are no more units (after an abort it leaves on its own)
         if (ok && p.n_peer_out) publish_out(t, -1);
+        if (kQ2 && p.tma_out && r == 0) bulk_wait_group0();  // this thread's tensor stores have completed
     }
 
     tc_fence_before();
@@ -913,14 +1035,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <typename T, typename TO>
-cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const FmhaParams& p,
-                     cudaStream_t st) {
+cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const CUtensorMap& tmO,
+                     const FmhaParams& p, cudaStream_t st) {
     // a mask (tile classes) selects the instantiation that skips K/V tiles per Q tile
     // head-pair units when every head shares one mask plane (p.head_pairs, set by the host)
-    auto kern = !p.tile_cls ? fmha_fwd_kernel<T, TO, false, false>
-                            : (p.head_pairs ? fmha_fwd_kernel<T, TO, true, true> : fmha_fwd_kernel<T, TO, true, false>);
+    // without a mask, a short key sequence selects the double-buffered-Q instantiation
+    const bool q2 = !p.tile_cls && p.Lk <= kQ2MaxKeys;
+    auto kern = p.tile_cls ? (p.head_pairs ? fmha_fwd_kernel<T, TO, true, true, false>
+                                           : fmha_fwd_kernel<T, TO, true, false, false>)
+                           : (q2 ? fmha_fwd_kernel<T, TO, false, false, true> : fmha_fwd_kernel<T, TO, false, false, false>);
     // set on every launch: the attribute belongs to the current device, and the call is cheap
-    const int smem_bytes = p.tile_cls ? Layout<true>::kSmemAlloc : Layout<false>::kSmemAlloc;
+    const int smem_bytes = p.tile_cls ? Layout<true>::kSmemAlloc
+                                      : (q2 ? Layout<false, true>::kSmemAlloc : Layout<false>::kSmemAlloc);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     // Persistent: one CTA per SM (never more CTAs than units); units are handed out by p.work_counter,
@@ -930,14 +1056,14 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
                                 : (long long)((p.Lq + kRowsPerCta - 1) / kRowsPerCta) * p.H * p.N;
     const int grid = (int)(units < p.num_ctas ? units : p.num_ctas);
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, kThreads, smem_bytes, st>>>(tmQ, tmK, tmV, p);
+    kern<<<grid, kThreads, smem_bytes, st>>>(tmQ, tmK, tmV, tmO, p);
     return cudaGetLastError();
 }
 
 template <typename T, typename TO>
 int regs_t() {
     cudaFuncAttributes a{};
-    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false, false>) != cudaSuccess) return -1;
+    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false, false, false>) != cudaSuccess) return -1;
     return a.numRegs;
 }
 
@@ -947,15 +1073,15 @@ int fmha_smem_bytes() { return Layout<true>::kSmemAlloc; }
 
 
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                        const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st) {
+                        const CUtensorMap& tmV, const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st) {
     if (op == OpType::BF16) {
-        if (ot == OutType::F32) return launch_t<__nv_bfloat16, float>(tmQ, tmK, tmV, p, st);
-        if (ot == OutType::BF16) return launch_t<__nv_bfloat16, __nv_bfloat16>(tmQ, tmK, tmV, p, st);
-        return launch_t<__nv_bfloat16, __half>(tmQ, tmK, tmV, p, st);
+        if (ot == OutType::F32) return launch_t<__nv_bfloat16, float>(tmQ, tmK, tmV, tmO, p, st);
+        if (ot == OutType::BF16) return launch_t<__nv_bfloat16, __nv_bfloat16>(tmQ, tmK, tmV, tmO, p, st);
+        return launch_t<__nv_bfloat16, __half>(tmQ, tmK, tmV, tmO, p, st);
     }
-    if (ot == OutType::F32) return launch_t<__half, float>(tmQ, tmK, tmV, p, st);
-    if (ot == OutType::BF16) return launch_t<__half, __nv_bfloat16>(tmQ, tmK, tmV, p, st);
-    return launch_t<__half, __half>(tmQ, tmK, tmV, p, st);
+    if (ot == OutType::F32) return launch_t<__half, float>(tmQ, tmK, tmV, tmO, p, st);
+    if (ot == OutType::BF16) return launch_t<__half, __nv_bfloat16>(tmQ, tmK, tmV, tmO, p, st);
+    return launch_t<__half, __half>(tmQ, tmK, tmV, tmO, p, st);
 }
 
 int fmha_num_regs(OpType op, OutType ot) {

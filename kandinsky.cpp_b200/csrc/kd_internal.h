@@ -19,6 +19,13 @@ constexpr int kRowsPerCta = kBlockM * kQTiles;
 constexpr int kBlockN = 128;   // keys per K/V tile
 constexpr int kMaxKvTiles = 2048;  // per-unit kept-tile list capacity (Lk <= 262144)
 constexpr int kMaxPeers = 7;       // other ranks an output row is also written to (8 GPUs)
+// Unmasked calls with at most this many keys (padded length) run the short-key instantiation:
+// double-buffered Q, units published two ahead, Q loads issued by the scheduler warp, and (16-bit
+// outputs, no peer exchange) the O tiles written with TMA stores from shared memory.
+#ifndef KD_FMHA_Q2_MAX_KEYS
+#define KD_FMHA_Q2_MAX_KEYS 1024
+#endif
+constexpr int kQ2MaxKeys = KD_FMHA_Q2_MAX_KEYS;
 
 struct FmhaParams {
     int Lq, Lk, H, N;        // query rows, keys, heads, sequences
@@ -47,6 +54,7 @@ struct FmhaParams {
     int out_v8;              // 1: out rows are 32-byte aligned (256-bit stores in the epilogue)
     int head_pairs;          // masked kernel: units of 128 rows x heads (2hp, 2hp+1) -- needs one mask
                              // plane for all heads (mh == 1), an even head count and no peers
+    int tma_out;             // short-key kernel: tmO describes `out` (16-bit, no peers); O tiles go out by TMA
 };
 
 enum class OpType { F16, BF16 };
@@ -54,9 +62,10 @@ enum class OutType { F32, F16, BF16 };
 
 // Launches the tcgen05 flash-attention forward.  tmQ/tmK/tmV are 4-D tiled
 // tensor maps over [128, L, heads, seqs] with a {64, 128, 1, 1} box and
-// 128-byte swizzle.
+// 128-byte swizzle; tmO (read only when p.tma_out) maps `out` as [128, H, Lq, N]
+// with a {64, 1, 128, 1} box (the same 128 rows of 128 bytes in shared memory) and swizzle.
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                        const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st);
+                        const CUtensorMap& tmV, const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st);
 int fmha_smem_bytes();
 // Register count the compiler gave the kernel (the host refuses to launch if it is not the expected one).
 int fmha_num_regs(OpType op, OutType ot);
