@@ -481,9 +481,12 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        # NCCL's init lines ("... nranks N ... Init COMPLETE") show every communicator's size
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # NCCL's init lines ("... nranks N ... Init COMPLETE") show every communicator's size; they go to
+        # stderr so that stdout keeps the one JSON line
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", init_method="env://", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     N, H, d = cfg["N"], cfg["H"], 128
@@ -693,6 +696,9 @@ def main():
         "gpu_launches": args.steps * 2,  # prologue + flash (the barriers are NCCL kernels)
         "clocks": clk.summary(),
     }
+    if ws > 1:
+        line["comm"] = {"backend": "nccl", "world_size": dist.get_world_size(), "gpus_active": ws,
+                        "library_communicator_ranks": ws}
     if exchange is not None:
         line["exchange_check"] = exchange["status"]
         line["exchange_check_detail"] = exchange
