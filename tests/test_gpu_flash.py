@@ -425,3 +425,53 @@ def test_text_block_self_attention_with_1d_rope(ctx, kd, Lt):
     ctx.self_attention(dev(q), dev(k), dev(v), H, out, rope=rope, op_type=kd.BF16, lse=lse)
     ctx.device_status()
     assert_gates(out.cpu().numpy(), exact, lse=lse.cpu().numpy(), lse_ref=lse_ref, label=f"text L{Lt}")
+
+
+# ------------------------------------------------------------------ batched CFG over two separate buffers
+def test_cfg_halves_in_separate_buffers_as_one_batch2_call(ctx, kd):
+    """The reference runs classifier-free guidance as two batch-1 DiT forwards (pipeline.cpp:1571-1592);
+    integration/kd_ggml_bridge.hpp pairs the two forwards' tensors into ONE batch-2 call by giving the
+    sequence dimension the address difference of the two buffers.  That call must equal the two
+    batch-1 calls bit for bit.  Here each role's two halves sit 4 KB apart (not packed), cond first."""
+    L, H, d = 1280, 8, 128
+    C = H * d
+    gap = 1024                                   # floats between the halves (4 KB)
+    rope = kd.Rope3D.make((5, 16, 16), scale=(1, 2, 2))
+
+    def pair_buffers(dtype):
+        buf = torch.empty(2, L * C + gap, device="cuda", dtype=dtype)
+        return buf, [buf[i, :L * C].view(1, L, C) for i in range(2)]
+
+    ins = []
+    for off in range(3):
+        buf, halves = pair_buffers(torch.float32)
+        for i, h in enumerate(halves):      # cond, uncond
+            t = torch.empty(L * C, device="cuda")
+            ctx.fill_randn(t, seed=11 + i, offset=off)
+            h.copy_(t.view(1, L, C))
+        ins.append((buf, halves))
+    obuf, outs = pair_buffers(torch.bfloat16)
+    refs = []
+    for i in range(2):
+        r = torch.empty(1, L, C, device="cuda", dtype=torch.bfloat16)
+        ctx.self_attention(*(x[1][i] for x in ins), H, r, rope=rope, op_type=kd.BF16)
+        refs.append(r)
+
+    def paired(halves):
+        t = kd.KdTensor.of(halves[0])
+        diff = halves[1].data_ptr() - halves[0].data_ptr()
+        assert diff > 0 and diff % 16 == 0 and diff > halves[0].numel() * halves[0].element_size()
+        t.ne[2] = 2
+        t.nb[2] = diff
+        t.nb[3] = 2 * diff
+        return t
+
+    tq, tk, tv = (paired(x[1]) for x in ins)
+    to = paired(outs)
+    rc = kd.lib.kd_attn_self_attention(ctx.handle, kd.ctypes.byref(tq), kd.ctypes.byref(tk), kd.ctypes.byref(tv), H,
+                                       None, None, kd.ctypes.c_float(1e-6), kd.ctypes.byref(rope), kd.BF16,
+                                       kd.ctypes.byref(to), None, None)
+    assert rc == kd.OK, kd.lib.kd_attn_last_error(ctx.handle)
+    ctx.device_status()
+    for i in range(2):
+        assert torch.equal(outs[i], refs[i])
