@@ -59,11 +59,19 @@ inline bool kd_from_ggml(const ggml_tensor* t, kd_tensor* out) {
 }
 
 // Would kd_attn_attention accept ops::attention(q, k, v, n_head, mask, flash = true)?  q [C, Lq, N],
-// k/v [C_kv, Lk, N] f32, head_dim 128, GQA ratio integral, f16 mask [Lk, >=Lq] or none.
+// k/v [C_kv, Lk, N] f32 with head_dim 128, GQA ratio integral, f16 mask [Lk, >=Lq] or none -- or the
+// VAE mid block's single head of 512 channels (vae.hpp:89): packed rows, no mask.
 inline bool supports_attention(const ggml_tensor* q, const ggml_tensor* k, const ggml_tensor* v, int64_t n_head,
                                const ggml_tensor* mask) {
     if (!q || !k || !v || n_head <= 0 || q->ne[0] % n_head) return false;
     const int64_t d = q->ne[0] / n_head;
+    if (d == 512 && n_head == 1) {
+        const ggml_tensor* t[3] = {q, k, v};
+        for (const ggml_tensor* x : t)
+            if (x->type != GGML_TYPE_F32 || x->ne[0] != 512 || x->nb[0] != 4 || x->nb[1] != 512 * 4 || x->ne[3] != 1)
+                return false;
+        return !mask && k->ne[1] == v->ne[1] && k->ne[2] == q->ne[2] && v->ne[2] == q->ne[2];
+    }
     if (d != 128 || k->ne[0] % d || v->ne[0] != k->ne[0] || q->ne[3] != 1 || k->ne[3] != 1 || v->ne[3] != 1)
         return false;
     const int64_t n_kv = k->ne[0] / d;

@@ -161,16 +161,17 @@ PFN_encodeTiled_t get_encode() {
     return fn;
 }
 
-// [128, L, heads, seqs] 16-bit operand, {64, 128, 1, 1} box, 128-byte swizzle, zero fill out of range.
+// [d, L, heads, seqs] 16-bit operand, {64, box_rows, 1, 1} box, 128-byte swizzle, zero fill out of range.
 kd_attn_status make_operand_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, bool bf16, int64_t L,
-                                int64_t heads, int64_t seqs, const uint64_t nb[4]) {
+                                int64_t heads, int64_t seqs, const uint64_t nb[4], int64_t d = kHeadDim,
+                                uint32_t box_rows = kBlockM) {
     PFN_encodeTiled_t enc = get_encode();
     if (!enc) return fail(ctx, KD_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     if (!aligned16(data)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "operand base address is not 16-byte aligned");
-    cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)(L > 0 ? L : 1), (cuuint64_t)(heads > 0 ? heads : 1),
+    cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)(L > 0 ? L : 1), (cuuint64_t)(heads > 0 ? heads : 1),
                           (cuuint64_t)(seqs > 0 ? seqs : 1)};
     cuuint64_t strides[3] = {nb[1], nb[2], nb[3]};
-    cuuint32_t box[4] = {64, (cuuint32_t)kBlockM, 1, 1};
+    cuuint32_t box[4] = {64, box_rows, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                      const_cast<void*>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -395,9 +396,14 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         (rc = check_tensor(ctx, a.v, "v")) || (rc = check_tensor(ctx, a.out, "out")))
         return rc;
     const kd_tensor &q = *a.q, &k = *a.k, &v = *a.v, &o = *a.out;
-    if (q.ne[0] != kHeadDim || k.ne[0] != kHeadDim || v.ne[0] != kHeadDim)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128 (q %lld, k %lld, v %lld)",
+    // head_dim 128 (CrossDiT) or 512 (the VAE mid block, kd_fmha512.cu: no mask, no kv_len, no peers)
+    const int64_t D = q.ne[0];
+    if ((D != kHeadDim && D != kHeadDim512) || k.ne[0] != D || v.ne[0] != D)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128 or 512 (q %lld, k %lld, v %lld)",
                     (long long)q.ne[0], (long long)k.ne[0], (long long)v.ne[0]);
+    const bool d512 = D == kHeadDim512;
+    if (d512 && (a.mask || a.kv_len || a.tile_mask || a.n_peers))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim 512 takes no mask, kv_len, tile mask or peers");
     if (k.type != v.type || (k.type != KD_ATTN_TYPE_F16 && k.type != KD_ATTN_TYPE_BF16))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k and v must share type f16 or bf16");
     const int64_t Lq = q.ne[1], H = q.ne[2], N = q.ne[3];
@@ -407,8 +413,10 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     if (Hkv <= 0 || Nkv <= 0 || H % Hkv || N % Nkv)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q heads/sequences (%lld, %lld) are not multiples of k's (%lld, %lld)",
                     (long long)H, (long long)N, (long long)Hkv, (long long)Nkv);
-    if (o.ne[0] != kHeadDim || o.ne[1] != H || o.ne[2] != Lq || o.ne[3] != N)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [128, H, Lq, N]");
+    if (o.ne[0] != D || o.ne[1] != H || o.ne[2] != Lq || o.ne[3] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [D, H, Lq, N]");
+    if (d512 && Lk == 0 && Lq > 0)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim 512 needs at least one key");
     if (!(a.scale > 0.f) || !std::isfinite(a.scale))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "scale must be positive and finite");
     if (Lk > (int64_t)kMaxKvTiles * kBlockN)
@@ -428,7 +436,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
 
     // scratch plan: [Q rounded to the operand type][tile classes]
     const bool q_direct = q.type == k.type && strides16(qnb) && aligned16(q.data);
-    const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * kHeadDim * 2);
+    const size_t q_bytes = q_direct ? 0 : align256((size_t)N * H * Lq * D * 2);
     const bool tiled = a.mask || a.tile_mask;
     const int n_qb = tiled ? (int)((Lq + 63) / 64) : 0, n_kb = tiled ? (int)((Lk + 63) / 64) : 0;
     int mh = 1, mn = 1;
@@ -492,9 +500,10 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         cp.L = (int)Lq;
         cp.H = (int)H;
         cp.N = (int)N;
+        cp.sub = (int)(D / kHeadDim);
         KD_CUDA(ctx, launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, num_sms, st));
         qdata = scr;
-        qnb[1] = kHeadDim * 2;
+        qnb[1] = (uint64_t)D * 2;
         qnb[2] = qnb[1] * Lq;
         qnb[3] = qnb[2] * H;
     }
@@ -520,6 +529,31 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     }
 
     CUtensorMap tmQ, tmK, tmV;
+    if (d512) {
+        if ((rc = make_operand_map(ctx, &tmQ, qdata, bf16, Lq, H, N, qnb, D, 128)) ||
+            (rc = make_operand_map(ctx, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb, D, 64)) ||
+            (rc = make_operand_map(ctx, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb, D, 64)))
+            return rc;
+        FmhaParams p{};
+        p.Lq = (int)Lq;
+        p.Lk = (int)Lk;
+        p.H = (int)H;
+        p.N = (int)N;
+        p.rk2 = (int)(H / Hkv);
+        p.rk3 = (int)(N / Nkv);
+        p.scale_log2 = a.scale * 1.4426950408889634f;
+        p.out = o.data;
+        p.o_nb1 = (long long)onb[1];
+        p.o_nb2 = (long long)onb[2];
+        p.o_nb3 = (long long)onb[3];
+        p.lse = a.lse;
+        p.err = words;
+        p.abort_flag = words + 1;
+        p.wait_ns = wait_ns;
+        KD_CUDA(ctx, cudaMemsetAsync(words + 1, 0, sizeof(unsigned), st));
+        KD_CUDA(ctx, launch_fmha512(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
+        return KD_ATTN_OK;
+    }
     if ((rc = make_operand_map(ctx, &tmQ, qdata, bf16, Lq, H, N, qnb))) return rc;
     if (Lk > 0) {
         if ((rc = make_operand_map(ctx, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb))) return rc;
@@ -724,12 +758,70 @@ kd_attn_status out_view(kd_attn_ctx* ctx, const kd_tensor* out, int32_t n_head, 
     return KD_ATTN_OK;
 }
 
+// ops::attention with ONE head of 512 channels: VAEAttnBlock::forward (vae.hpp:89) on the H*W latent
+// positions, no RMSNorm or RoPE.  The prologue (permute + rounding, 128-wide rows) takes each packed
+// 512-wide row as four consecutive 128-wide rows, which lays the operands out as [512, L, 1, N];
+// then the head_dim-512 flash kernel with scale 1/sqrt(512) (ops.hpp:161).
+kd_attn_status attention512_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
+                                 const kd_tensor* mask, int32_t op_type, kd_tensor* out, float* lse, cudaStream_t st) {
+    kd_attn_status rc;
+    if (mask) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim 512 takes no mask");
+    const kd_tensor* ins[3] = {q_in, k_in, v_in};
+    for (const kd_tensor* t : ins)
+        if (t->ne[0] != kHeadDim512 || t->type != KD_ATTN_TYPE_F32 || t->nb[1] != (size_t)kHeadDim512 * 4 ||
+            t->ne[3] != 1)
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim 512 needs packed f32 rows [512, L, N]");
+    const int64_t Lq = q_in->ne[1], N = q_in->ne[2], Lk = k_in->ne[1];
+    if (k_in->ne[2] != N || v_in->ne[1] != Lk || v_in->ne[2] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
+    if ((rc = check_tensor(ctx, out, "out"))) return rc;
+    if (out->ne[0] != kHeadDim512 || out->ne[1] != Lq || out->ne[2] != N || out->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [512, Lq, N]");
+    const size_t qb = align256((size_t)N * Lq * kHeadDim512 * 2);
+    const size_t kb = align256((size_t)N * Lk * kHeadDim512 * 2);
+    if ((rc = ensure_scratch(ctx, qb + 2 * kb, st))) return rc;
+    char* base = static_cast<char*>(ctx->scratch);
+    char* dst[3] = {base, base + qb, base + qb + kb};
+    const int64_t len[3] = {Lq, Lk, Lk};
+    kd_tensor x4[3], y4[3], ops[3];
+    PrologueReq req[3];
+    for (int i = 0; i < 3; ++i) {
+        x4[i] = *ins[i];  // [128, 4L, N]: row pieces 512 bytes apart
+        x4[i].ne[0] = kHeadDim;
+        x4[i].ne[1] = 4 * len[i];
+        x4[i].nb[1] = (size_t)kHeadDim * 4;
+        y4[i] = operand_view(dst[i], op_type, 4 * len[i], 1, N);
+        ops[i] = y4[i];  // the same bytes as [512, L, 1, N]
+        ops[i].ne[0] = kHeadDim512;
+        ops[i].ne[1] = len[i];
+        ops[i].nb[1] = (size_t)kHeadDim512 * 2;
+        req[i] = PrologueReq{&x4[i], 0, nullptr, false, &y4[i]};
+    }
+    if ((rc = prologue_multi(ctx, req, 3, 1, 0.f, nullptr, st))) return rc;
+    kd_tensor ov = *out;  // [512, Lq, N] as the flash dst [512, 1, Lq, N]
+    ov.ne[1] = 1;
+    ov.ne[2] = Lq;
+    ov.ne[3] = N;
+    ov.nb[1] = out->nb[0] * kHeadDim512;
+    ov.nb[2] = out->nb[1];
+    ov.nb[3] = out->nb[2];
+    FlashArgs fa{&ops[0], &ops[1], &ops[2], nullptr, 1.0f / std::sqrt((float)kHeadDim512), nullptr, &ov, lse};
+    return flash_run(ctx, fa, st);
+}
+
 kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in, const kd_tensor* v_in,
                               int32_t n_head, const float* q_gain, const float* k_gain, float eps,
                               const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
                               kd_tensor* out, float* lse, cudaStream_t st, const char* out_base = nullptr,
                               char* const* peer_base = nullptr, int n_peers = 0, bool norm_qk = true) {
     kd_attn_status rc;
+    if (n_head == 1 && q_in && q_in->ne[0] == kHeadDim512 && !norm_qk && !rope && !kv_len && !n_peers &&
+        (op_type == KD_ATTN_TYPE_F16 || op_type == KD_ATTN_TYPE_BF16)) {
+        if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
+            (rc = check_tensor(ctx, v_in, "v_in")))
+            return rc;
+        return attention512_core(ctx, q_in, k_in, v_in, mask, op_type, out, lse, st);
+    }
     if ((rc = check_tensor(ctx, q_in, "q_in")) || (rc = check_tensor(ctx, k_in, "k_in")) ||
         (rc = check_tensor(ctx, v_in, "v_in")))
         return rc;

@@ -13,6 +13,7 @@ enum : uint8_t { kTileSkip = 0, kTileFull = 1, kTileMixed = 2 };
 
 // Flash-attention forward geometry (sm_100a kernel in kd_fmha.cu).
 constexpr int kHeadDim = 128;
+constexpr int kHeadDim512 = 512;  // the VAE mid-block head (kd_fmha512.cu)
 constexpr int kBlockM = 128;   // query rows per Q tile = one M=128 tcgen05 MMA
 constexpr int kQTiles = 2;     // Q tiles per CTA, one softmax warpgroup each
 constexpr int kRowsPerCta = kBlockM * kQTiles;
@@ -67,6 +68,10 @@ enum class OutType { F32, F16, BF16 };
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                         const CUtensorMap& tmV, const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st);
 int fmha_smem_bytes();
+// head_dim 512, no mask (kd_fmha512.cu): tmQ over [512, Lq, H, N] with a {64, 128, 1, 1} box,
+// tmK/tmV over [512, Lk, Hkv, Nkv] with a {64, 64, 1, 1} box, all 128-byte swizzled.
+cudaError_t launch_fmha512(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                           const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st);
 // Register count the compiler gave the kernel (the host refuses to launch if it is not the expected one).
 int fmha_num_regs(OpType op, OutType ot);
 
@@ -105,8 +110,9 @@ cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cu
 struct ConvertParams {
     const void* src; int src_type;   // kd_attn_type id
     long long nb1, nb2, nb3;
-    void* dst;                       // contiguous [128, L, H, N]
+    void* dst;                       // contiguous [128 * sub, L, H, N]
     int L, H, N;
+    int sub;                         // 128-element pieces per row (1, or 4 for head_dim 512)
 };
 cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st);
 

@@ -116,24 +116,26 @@ __device__ __forceinline__ float load_elt(const void* base, long long idx, int t
     return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
-// One warp per 128-element row; the source row is contiguous (nb0 = element size).
+// One warp per 128-element piece of a row (p.sub pieces per row); the source row is contiguous
+// (nb0 = element size), so piece j of row l starts 128 * j elements into it.
 template <typename TD>
 __global__ void __launch_bounds__(256) convert_q_kernel(const ConvertParams p) {
     const int lane = threadIdx.x & 31;
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    const long long rows = (long long)p.N * p.H * p.L;
+    const long long lsub = (long long)p.L * p.sub;
+    const long long rows = (long long)p.N * p.H * lsub;
     const int esz = p.src_type == 0 ? 4 : 2;
     for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
          row += warps) {
-        const int l = (int)(row % p.L);
-        const long long nh = row / p.L;
+        const long long lj = row % lsub;
+        const int l = (int)(lj / p.sub), j = (int)(lj % p.sub);
+        const long long nh = row / lsub;
         const int h = (int)(nh % p.H);
         const int n = (int)(nh / p.H);
         const char* src = reinterpret_cast<const char*>(p.src) + (long long)n * p.nb3 + (long long)h * p.nb2 +
-                          (long long)l * p.nb1;
+                          (long long)l * p.nb1 + (long long)j * kHeadDim * esz;
         float a = load_elt(src, 4 * lane + 0, p.src_type), b = load_elt(src, 4 * lane + 1, p.src_type);
         float c = load_elt(src, 4 * lane + 2, p.src_type), d = load_elt(src, 4 * lane + 3, p.src_type);
-        (void)esz;
         char* dst = reinterpret_cast<char*>(p.dst) + (row * kHeadDim + 4 * lane) * (long long)sizeof(TD);
         store4<TD>(dst, a, b, c, d);
     }
@@ -298,7 +300,7 @@ cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned l
 }
 
 cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st) {
-    const long long rows = (long long)p.N * p.H * p.L;
+    const long long rows = (long long)p.N * p.H * p.L * p.sub;
     if (rows == 0) return cudaSuccess;
     const int grid = grid_for(rows, num_sms);
     if (dt == OpType::BF16)

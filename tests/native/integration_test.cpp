@@ -133,7 +133,12 @@ int main() {
     CHECK(kd_bridge::supports_attention(&q, &kg, &vg, H, nullptr));       // GQA 32 : 8
     ggml_tensor qh = make(GGML_TYPE_F16, C, L, N, 0x100000);
     CHECK(!kd_bridge::supports_attention(&qh, &k, &v, H, nullptr));       // ops::attention feeds f32
+    ggml_tensor vq = make(GGML_TYPE_F32, 512, 4096, 1, 0x500000), vk = make(GGML_TYPE_F32, 512, 4096, 1, 0x600000),
+                vv = make(GGML_TYPE_F32, 512, 4096, 1, 0x700000);
+    CHECK(kd_bridge::supports_attention(&vq, &vk, &vv, 1, nullptr));      // VAE mid block: one head of 512
+    CHECK(!kd_bridge::supports_attention(&vq, &vk, &vv, 2, nullptr));     // two heads of 256
     ggml_tensor mf = make(GGML_TYPE_F32, L, L, 1, 0x400000), mh = make(GGML_TYPE_F16, L, L, 1, 0x400000);
+    CHECK(!kd_bridge::supports_attention(&vq, &vk, &vv, 1, &mh));
     CHECK(!kd_bridge::supports_attention(&q, &k, &v, H, &mf));
     CHECK(kd_bridge::supports_attention(&q, &k, &v, H, &mh));
 

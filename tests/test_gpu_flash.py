@@ -475,3 +475,46 @@ def test_cfg_halves_in_separate_buffers_as_one_batch2_call(ctx, kd):
     ctx.device_status()
     for i in range(2):
         assert torch.equal(outs[i], refs[i])
+
+
+# ------------------------------------------------------------------ head_dim 512: the VAE mid-block attention
+@pytest.mark.parametrize("N,H,L,kv_type,out_dtype", [
+    (1, 1, 64 * 64, oracle.F16, torch.float32),      # 512 x 512 image: 64 x 64 latent, ggml types
+    (2, 2, 37 * 41, oracle.BF16, torch.bfloat16),    # ragged: partial Q tile and partial 64-key tile
+])
+def test_flash_ext_head_dim_512(ctx, N, H, L, kv_type, out_dtype):
+    """VAEAttnBlock::forward (vae.hpp:89) attends with one head of the full channel count (512) through
+    ops::attention's flash branch; kd_attn_flash_ext takes it with f32 Q (rounded to K's type on the
+    device), 16-bit K/V, f32 or 16-bit output and the LSE."""
+    D = 512
+    qf = seeded((N, H, L, D), 512 + L, 0)
+    kf = seeded((N, H, L, D), 512 + L, 1)
+    vf = seeded((N, H, L, D), 512 + L, 2)
+    kb, vb = oracle.to_type(kf, kv_type), oracle.to_type(vf, kv_type)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, mode=oracle.EXACT, lse=True)
+    out = torch.empty(N, L, H, D, device="cuda", dtype=out_dtype)
+    lse = torch.empty(N, H, L, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, kv_type), op_tensor(vf, kv_type), out, lse=lse)
+    ctx.device_status()
+    ot = None if out_dtype == torch.float32 else "bf16"
+    ggml = oracle.flash_attn_ext(qf, kb, vb, mode=oracle.GGML) if ot is None else None
+    assert_gates(out.float().cpu().numpy(), exact, ggml, lse.cpu().numpy(), lse_ref, label=f"d512 {N,H,L}", out_type=ot)
+
+
+def test_ops_attention_vae_mid_block(ctx, kd):
+    """ops::attention as VAEAttnBlock::forward calls it (vae.hpp:89): one head over the 64 x 64 latent
+    positions of a 512 x 512 image with the full 512 channels, f32 q/k/v [512, H*W, 1], f16 operands
+    (ggml's flash branch), f32 output -- through the C ABI entry point that mirrors ops::attention."""
+    N, L, C = 1, 64 * 64, 512
+    q = seeded((N, L, C), 77, 0)
+    k = seeded((N, L, C), 77, 1)
+    v = seeded((N, L, C), 77, 2)
+    out = torch.empty(N, L, C, device="cuda")
+    lse = torch.empty(N, 1, L, device="cuda")
+    ctx.ops_attention(dev(q), dev(k), dev(v), 1, out, op_type=kd.F16, lse=lse)
+    ctx.device_status()
+    q4, k4, v4 = (x.reshape(N, 1, L, C) for x in (q, k, v))
+    kb, vb = oracle.to_type(k4, oracle.F16), oracle.to_type(v4, oracle.F16)
+    exact, lse_ref = oracle.flash_attn_ext(q4, kb, vb, mode=oracle.EXACT, lse=True)
+    ggml = oracle.flash_attn_ext(q4, kb, vb, mode=oracle.GGML)
+    assert_gates(out.cpu().numpy().reshape(N, L, 1, C), exact, ggml, lse.cpu().numpy(), lse_ref, label="VAE mid block")
