@@ -192,7 +192,8 @@ kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
  * lse  : NULL or device f32 [N, H, Lq], natural-log softmax denominator
  *        (ln sum_j exp(scale*q.k_j + mask_j)); -inf for fully masked rows.
  * max_bias and logit_softcap must be 0 (the only values ops.hpp:176 passes).
- * Rows whose keys are all masked produce 0.  D must be 128. */
+ * Rows whose keys are all masked produce 0.  D is 128, or 512 -- one head of a VAE mid block
+ * (src/models/vae.hpp:89) -- with no mask, kv_len or tile_mask and at least one key. */
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k,
                                  const kd_tensor* v, const kd_tensor* mask, float scale,
                                  float max_bias, float logit_softcap, const int32_t* kv_len,
@@ -263,7 +264,9 @@ kd_attn_status kd_attn_noalloc_selftest_wait(uint32_t wait_ms, void* stream);
  * rounded to op_type (ops.hpp:122-131,167-169, f16 in ggml), then flash attention
  * with scale 1/sqrt(128).  mask: NULL or f16 in ggml's flash orientation
  * [>=Lk, >=Lq, mh, mn] (ops.hpp:171-174 transposes an [N, Lq, Lk] mask first; that
- * branch is never reached by the CrossDiT call sites).  out [n_head*128, Lq, N]. */
+ * branch is never reached by the CrossDiT call sites).  out [n_head*128, Lq, N].
+ * n_head = 1 with 512 channels (packed rows, no mask) is the VAE mid-block call (vae.hpp:89):
+ * head_dim 512, scale 1/sqrt(512). */
 kd_attn_status kd_attn_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
                                  const kd_tensor* v_in, int32_t n_head, const kd_tensor* mask,
                                  int32_t op_type, kd_tensor* out, float* lse, void* stream);
