@@ -169,6 +169,42 @@ kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
                                    kd_tensor* k_out, kd_tensor* v_out, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * QKV projection with the prologue as its epilogue.
+ * Replaces, for one attention block, the three Linear layers and everything up to
+ * the flash operands:
+ *   q, k, v = to_query/to_key/to_value(x)       crossdit.hpp:123-125 (ops::linear, ops.hpp:27-42:
+ *                                               ggml_mul_mat(w, x) + bias)
+ *   + the prologue of kd_attn_qk_prologue        crossdit.hpp:132-141, ops.hpp:122-131,167-169
+ * as one tensor-core GEMM whose epilogue adds the bias, RMS-normalises Q and K
+ * per head (q_gain / k_gain, NULL = unit gain), applies the 3D RoPE when `rope`
+ * is given, casts, and stores [d, L, H, N] operands: the f32 projections are
+ * never written to memory.  The GEMM runs in bf16 with fp32 accumulation; quantized
+ * weights are expanded to bf16 first (q8_0: value d*q; q4_0: value d*(q-8), element
+ * j in the low nibble and j+16 in the high one -- ggml's block formats, as
+ * scripts/convert_to_gguf.py:90-146 writes them).
+ * x     : [K, L, N] f32, rows 16-byte aligned; K a multiple of 32
+ * wq/wk/wv : weights in ggml layout [K, C] (row r = output feature r); any of the
+ *         three may be NULL together with its output (e.g. the Q projection of
+ *         cross-attention alone, or its K/V projection of the text states)
+ * q_out/k_out/v_out : [128, L, H, N] f16 or bf16 (= out_dtype), H*128 = C a
+ *         multiple of 256, rows 16-byte aligned.  Q and K are normalised (and
+ *         rotated), V only cast. */
+#define KD_ATTN_TYPE_Q4_0 2 /* ggml.h GGML_TYPE_Q4_0: 18-byte blocks of 32 (f16 scale, 16 bytes of nibbles) */
+#define KD_ATTN_TYPE_Q8_0 8 /* ggml.h GGML_TYPE_Q8_0: 34-byte blocks of 32 (f16 scale, 32 int8) */
+typedef struct {
+    const void* data;   /* device pointer to C rows of K elements of `type` */
+    int32_t type;       /* KD_ATTN_TYPE_F32 / F16 / BF16 / Q4_0 / Q8_0 */
+    int64_t ne[2];      /* {K, C} (ggml ne of the weight tensor) */
+    size_t nb1;         /* bytes between rows (ggml nb[1]) */
+    const float* bias;  /* device f32 [C] or NULL */
+} kd_linear;
+
+kd_attn_status kd_attn_qkv_projection(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                      const kd_linear* wk, const kd_linear* wv, const float* q_gain,
+                                      const float* k_gain, float eps, const kd_rope3d* rope, int32_t out_dtype,
+                                      kd_tensor* q_out, kd_tensor* k_out, kd_tensor* v_out, void* stream);
+
+/* ---------------------------------------------------------------------------
  * ggml_flash_attn_ext semantics (called at ops.hpp:176):
  *   out[:, h, i, n] = softmax_j(scale * q[:, i, h, n] . k[:, j, hk, nk] + mask[j, i, h%mh, n%mn]) v[:, j, hk, nk]
  * q    : [D, Lq, H, N]      f32 | f16 | bf16 (f32 is rounded to K's type first,

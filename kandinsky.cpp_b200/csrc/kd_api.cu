@@ -1009,6 +1009,141 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     return KD_ATTN_OK;
 }
 
+// ------------------------------------------------------------------ QKV projection
+// Bytes of one weight row of K elements (ggml_row_size).
+int64_t weight_row_bytes(int32_t type, int64_t K) {
+    switch (type) {
+        case KD_ATTN_TYPE_F32: return K * 4;
+        case KD_ATTN_TYPE_F16:
+        case KD_ATTN_TYPE_BF16: return K * 2;
+        case KD_ATTN_TYPE_Q8_0: return K / 32 * 34;
+        case KD_ATTN_TYPE_Q4_0: return K / 32 * 18;
+        default: return -1;
+    }
+}
+
+// bf16 [inner, rows] with a {64, box_rows} box, 128-byte swizzle, zero fill past the ends.
+kd_attn_status make_gemm_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, int64_t inner, int64_t rows,
+                             uint32_t box_rows) {
+    PFN_encodeTiled_t enc = get_encode();
+    if (!enc) return fail(ctx, KD_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(data), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled rejected a GEMM operand (%d)", (int)r);
+    return KD_ATTN_OK;
+}
+
+// Launch sequence: each given weight expanded to bf16 rows of one B operand [K, nslots*C]; x rounded to
+// bf16 token rows [K, L*N]; the RoPE (cos, sin) table when rotating; then the persistent GEMM whose
+// epilogue writes the operands.  Scratch: [B operand][A operand][RoPE table].
+kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* const w[3],
+                                   const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
+                                   int32_t out_dtype, kd_tensor* const outs[3], cudaStream_t st) {
+    kd_attn_status rc;
+    if ((rc = check_tensor(ctx, x, "x"))) return rc;
+    if (x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x must be f32");
+    if (x->ne[3] != 1) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x must be [K, L, N] (ne[3] == 1)");
+    if (out_dtype != KD_ATTN_TYPE_F16 && out_dtype != KD_ATTN_TYPE_BF16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "the projection writes f16 or bf16 operands");
+    const int64_t K = x->ne[0], L = x->ne[1], N = x->ne[2];
+    if (K <= 0 || K % 32)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "in_features %lld is not a positive multiple of 32", (long long)K);
+    uint64_t xnb[4];
+    packed_strides(x, xnb);
+    if (!aligned16(x->data) || xnb[1] % 16 || xnb[2] % 16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x rows must be 16-byte aligned");
+    if (L * N > INT32_MAX - 128) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than 2^31 tokens");
+
+    QkvParams p{};
+    p.K = (int)K;
+    p.L = (int)L;
+    p.M = (int)(L * N);
+    p.eps = eps;
+    int64_t C = -1;
+    int slot_of[3] = {-1, -1, -1};
+    for (int i = 0; i < 3; ++i) {
+        if (!w[i] && !outs[i]) continue;
+        if (!w[i] || !outs[i]) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "a weight and its output must both be given");
+        const kd_linear& W = *w[i];
+        const kd_tensor& o = *outs[i];
+        if ((rc = check_tensor(ctx, &o, "projection output"))) return rc;
+        if (o.type != out_dtype) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must have type out_dtype");
+        const int64_t rb = weight_row_bytes(W.type, K);
+        if (rb < 0) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "weight type %d is not f32/f16/bf16/q4_0/q8_0", W.type);
+        if (W.ne[0] != K) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight ne[0] %lld != in_features %lld",
+                                      (long long)W.ne[0], (long long)K);
+        if (W.ne[1] <= 0 || W.ne[1] % 256)
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features %lld is not a positive multiple of 256",
+                        (long long)W.ne[1]);
+        if (C >= 0 && W.ne[1] != C) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the weights disagree on out_features");
+        C = W.ne[1];
+        if ((int64_t)W.nb1 < rb) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight nb1 smaller than a row");
+        if (!W.data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight data is NULL");
+        if ((W.type == KD_ATTN_TYPE_F32 || W.type == KD_ATTN_TYPE_F16 || W.type == KD_ATTN_TYPE_BF16) &&
+            (!aligned16(W.data) || W.nb1 % 16))
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "f32/f16/bf16 weight rows must be 16-byte aligned");
+        if (W.type == KD_ATTN_TYPE_F32 && ((reinterpret_cast<uintptr_t>(W.data) | W.nb1) & 3))
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "f32 weight rows must be 4-byte aligned");
+        if (o.ne[0] != kHeadDim || o.ne[1] != L || o.ne[2] * kHeadDim != C || o.ne[3] != N)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must be [128, L, C/128, N]");
+        uint64_t onb[4];
+        packed_strides(&o, onb);
+        if (!aligned16(o.data) || !strides16(onb))
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "output rows must be 16-byte aligned");
+        QkvSlot& S = p.slot[p.nslots];
+        S.out = o.data;
+        S.o_nb1 = (long long)onb[1];
+        S.o_nb2 = (long long)onb[2];
+        S.o_nb3 = (long long)onb[3];
+        S.bias = W.bias;
+        S.norm = i < 2;
+        S.gain = i == 0 ? q_gain : (i == 1 ? k_gain : nullptr);
+        S.rope = (i < 2 && rope) ? 1 : 0;
+        slot_of[i] = p.nslots++;
+    }
+    if (p.nslots == 0) return KD_ATTN_OK;
+    if (C > (1 << 20)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features beyond 2^20");
+    p.C = (int)C;
+    RopeTab tab{};
+    const bool rot = rope && (p.slot[0].rope || (p.nslots > 1 && p.slot[1].rope));
+    if (rot && (rc = fill_rope(ctx, rope, L, &tab))) return rc;
+    if (p.M == 0) return KD_ATTN_OK;
+
+    const size_t b_bytes = align256((size_t)p.nslots * C * K * 2);
+    const size_t a_bytes = align256((size_t)p.M * K * 2);
+    const size_t cs_bytes = rot ? align256((size_t)L * 64 * sizeof(float2)) : 0;
+    if ((rc = ensure_scratch(ctx, b_bytes + a_bytes + cs_bytes, st))) return rc;
+    char* scr = static_cast<char*>(ctx->scratch);
+    __nv_bfloat16* wb = reinterpret_cast<__nv_bfloat16*>(scr);
+    __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(scr + b_bytes);
+    for (int i = 0; i < 3; ++i)
+        if (slot_of[i] >= 0)
+            KD_CUDA(ctx, launch_expand_weights(w[i]->data, w[i]->type, (long long)w[i]->nb1, (int)K, (int)C,
+                                               slot_of[i] * (int)C, wb, ctx->num_sms, st));
+    KD_CUDA(ctx, launch_to_bf16_rows(x->data, (long long)xnb[1], (long long)xnb[2], (int)K, (int)L, p.M, xb,
+                                     ctx->num_sms, st));
+    if (rot) {
+        float2* cs = reinterpret_cast<float2*>(scr + b_bytes + a_bytes);
+        KD_CUDA(ctx, launch_rope_table(tab, (int)L, cs, ctx->num_sms, st));
+        p.rope_cs = cs;
+    }
+    CUtensorMap tmX, tmW;
+    if ((rc = make_gemm_map(ctx, &tmX, xb, K, p.M, 128)) ||
+        (rc = make_gemm_map(ctx, &tmW, wb, K, (int64_t)p.nslots * C, 256)))
+        return rc;
+    p.err = ctx->d_words;
+    p.abort_flag = ctx->d_words + 1;
+    p.wait_ns = ctx->wait_ns;
+    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, sizeof(unsigned), st));
+    KD_CUDA(ctx, launch_qkv_gemm(out_type_of(out_dtype), tmX, tmW, p, ctx->num_sms, st));
+    return KD_ATTN_OK;
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1198,6 +1333,17 @@ kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_dtype must be f32, f16 or bf16");
     if (n_head <= 0 || n_head > (1 << 20)) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "bad head count");
     return prologue_multi(ctx, req, count, (int32_t)n_head, eps, rope, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_qkv_projection(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq, const kd_linear* wk,
+                                      const kd_linear* wv, const float* q_gain, const float* k_gain, float eps,
+                                      const kd_rope3d* rope, int32_t out_dtype, kd_tensor* q_out, kd_tensor* k_out,
+                                      kd_tensor* v_out, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    const kd_linear* w[3] = {wq, wk, wv};
+    kd_tensor* outs[3] = {q_out, k_out, v_out};
+    return qkv_projection_core(ctx, x, w, q_gain, k_gain, eps, rope, out_dtype, outs, static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,

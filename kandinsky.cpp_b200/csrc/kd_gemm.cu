@@ -1,0 +1,379 @@
+// kd_gemm.cu -- the QKV projection of DiTSelfAttention::forward with the attention prologue fused
+// into its epilogue, on sm_100a (B200).
+//
+// The reference computes q, k, v = Linear(x) (src/models/crossdit.hpp:123-125: ggml_mul_mat on
+// q4_0 / q8_0 / f16 weights plus a bias, ops::linear), writes them as f32 [C, L, N], then the
+// graph reads them back for the per-head RMSNorm (crossdit.hpp:135-136), rope::apply (:140-141)
+// and the permute + cast to the flash operands (ops.hpp:122-131,167-169).  Here one GEMM produces
+// the three projections and its epilogue applies bias, RMSNorm, RoPE and the cast and stores the
+// flash-attention operands [128, L, H, N] directly: the f32 projections never reach HBM.
+//
+//   expand_weights_kernel  ggml weight [C_in, C_out] (q8_0: 34-byte blocks of an f16 scale and 32
+//                          int8, value d*q; q4_0: 18-byte blocks of an f16 scale and 16 bytes,
+//                          element j in the low nibble and j+16 in the high one, value d*(q-8) --
+//                          the layout scripts/convert_to_gguf.py:90-146 writes; f16 / bf16 / f32)
+//                          -> bf16 rows of the concatenated [C_in, 3*C_out] B operand
+//   to_bf16_rows_kernel    x f32 [C_in, L, N] -> bf16 [C_in, L*N] (the A operand, token rows)
+//   rope_table_kernel      cos/sin of every (token, rotary pair), the prologue's angle formula
+//   qkv_gemm_kernel        persistent tcgen05 GEMM, 128 tokens x 256 output features per tile
+//                          (two heads of one projection), K = C_in in steps of 64 through a 4-stage
+//                          TMA ring, fp32 accumulators double-buffered in TMEM so one tile's
+//                          epilogue overlaps the next tile's MMAs
+//
+// Every wait is bounded (kd_common.cuh: mbar_wait).
+#include "kd_common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+namespace {
+
+constexpr int kBM = 128;                 // tokens per tile (MMA M)
+constexpr int kBN = 256;                 // output features per tile (MMA N): two heads
+constexpr int kBK = 64;                  // K per stage (one 128-byte swizzled row)
+constexpr int kABytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kGStages = 4;
+constexpr int kGSmemBar = kGStages * kStageBytes;
+// full[S], empty[S], acc_full[2], acc_empty[2]
+constexpr int kGNumBars = 2 * kGStages + 4;
+constexpr int kGSmemSlot = kGSmemBar + kGNumBars * 8;
+constexpr int kGSmemAlloc = kGSmemSlot + 16 + 1024;
+static_assert(kGSmemAlloc <= 232448, "shared memory budget");
+constexpr int kGThreads = 256;
+constexpr int kGroupM = 16;  // m-tiles per raster band: the tiles in flight share 16 A row blocks and ~10 B column blocks
+
+// Tile t of the persistent loop -> (m-tile, n-tile).  Bands of kGroupM m-tiles are swept n-tile by n-tile,
+// m fastest, so the CTAs running at one time read a few MB of A and B that stay in L2.
+__device__ __forceinline__ void tile_coords(long long t, int m_tiles, int n_tiles_n, int& mt, int& nt) {
+    const long long band = t / ((long long)kGroupM * n_tiles_n);
+    const int first = (int)band * kGroupM;
+    const int gm = min(kGroupM, m_tiles - first);
+    const int within = (int)(t - band * kGroupM * n_tiles_n);
+    mt = first + within % gm;
+    nt = within / gm;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+template <typename TO>
+__device__ __forceinline__ void store_chunk(TO* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        d[i] = make_uint4(Pack2<TO>::pack(v[8 * i], v[8 * i + 1]), Pack2<TO>::pack(v[8 * i + 2], v[8 * i + 3]),
+                          Pack2<TO>::pack(v[8 * i + 4], v[8 * i + 5]), Pack2<TO>::pack(v[8 * i + 6], v[8 * i + 7]));
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(kGThreads, 1)
+    qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ QkvParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
+    const int n_tiles_n = p.nslots * p.C / kBN;
+    const int m_tiles = (p.M + kBM - 1) / kBM;
+    const long long n_tiles = (long long)m_tiles * n_tiles_n;
+    const int k_steps = (p.K + kBK - 1) / kBK;  // a ragged last step reads zeros past K (TMA fill)
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGSmemBar);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kGStages;
+    uint64_t* acc_full = bars + 2 * kGStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kGSmemSlot);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kBM);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmX);
+            tma_prefetch_desc(&tmW);
+        }
+        uint32_t it = 0;
+        bool ok = true;
+        for (long long t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles_n, mt, nt);
+            for (int kb = 0; kb < k_steps; ++kb) {
+                const int s = it % kGStages;
+                if (!(ok = __all_sync(0xffffffffu,
+                                      mbar_wait(&empty[s], ((it / kGStages) & 1u) ^ 1u, ctl, kErrTimeoutKVEmpty))))
+                    break;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    uint8_t* st = smem + s * kStageBytes;
+                    tma_load_2d(st, &tmX, &full[s], kb * kBK, mt * kBM);
+                    tma_load_2d(st + kABytes, &tmW, &full[s], kb * kBK, nt * kBN);
+                }
+                __syncwarp();
+                ++it;
+            }
+        }
+        if (!ok)
+            for (uint32_t k = (it > (uint32_t)kGStages ? it - kGStages : 0u); k < it; ++k)
+                mbar_wait(&full[k % kGStages], (k / kGStages) & 1u, ctl, kErrTimeoutDrain, false);
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = idesc_f16_f32acc(true, kBM, kBN, false);
+        constexpr uint32_t dhi = sw128_desc_hi(1024);
+        const uint32_t base = smem_u32(smem);
+        uint32_t it = 0, tc = 0;
+        bool ok = true, issued = false;
+        for (long long t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++tc) {
+            const uint32_t ab = tc & 1u;
+            if (tc >= 2 &&
+                !(ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[ab], ((tc >> 1) - 1) & 1u, ctl, kErrTimeoutO))))
+                break;
+            tc_fence_after();
+            for (int kb = 0; kb < k_steps; ++kb) {
+                const int s = it % kGStages;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / kGStages) & 1u, ctl, kErrTimeoutKVFull))))
+                    break;
+                ++it;
+                tc_fence_after();
+                const uint32_t alo = sw128_desc_lo(base + s * kStageBytes, 16);
+                const uint32_t blo = sw128_desc_lo(base + s * kStageBytes + kABytes, 16);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                    mma_ss(tmem + ab * kBN, desc_join(alo + ((kk * 32) >> 4), dhi), desc_join(blo + ((kk * 32) >> 4), dhi),
+                           idesc, (kb | kk) ? 1u : 0u);
+                tc_commit(&empty[s]);
+                issued = true;
+            }
+            if (ok) tc_commit(&acc_full[ab]);
+        }
+        if (issued) {
+            tc_commit(&acc_full[tc & 1u]);  // a further arrival after the last tile: every MMA has retired
+            mbar_wait(&acc_full[tc & 1u], (tc >> 1) & 1u, ctl, kErrTimeoutDrain, false);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ epilogue: bias, RMSNorm, RoPE, cast
+        const int r = ((warp & 3) << 5) + lane;
+        const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+        uint32_t tc = 0;
+        for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+            const uint32_t ab = tc & 1u;
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles_n, mt, nt);
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (tc >> 1) & 1u, ctl, kErrTimeoutO))) break;
+            tc_fence_after();
+            const long long m = (long long)mt * kBM + r;
+            const bool valid = m < p.M;
+            const int l = valid ? (int)(m % p.L) : 0, n = valid ? (int)(m / p.L) : 0;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                const int col0 = nt * kBN + hh * 128;
+                const QkvSlot& S = p.slot[col0 / p.C];
+                const int h = (col0 % p.C) / 128;
+                const uint32_t taddr = tmem + lane_addr + ab * kBN + hh * 128;
+                const float* bias = S.bias ? S.bias + h * 128 : nullptr;
+                // Pass 1 (RMSNorm heads): ggml's CPU rms_norm -- float squares summed in double, the mean
+                // rounded to float, scale = 1/sqrt(mean + eps).  The row is read from TMEM in 32-column
+                // chunks twice rather than held whole, which keeps the epilogue at ~64 live registers.
+                float scale = 1.0f;
+                if (S.norm) {
+                    double ss = 0.0;
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t xr[32];
+                        tmem_ld32_sync(taddr + c * 32, xr);
+#pragma unroll
+                        for (int d = 0; d < 32; ++d) {
+                            float x = __uint_as_float(xr[d]);
+                            if (bias) x = __fadd_rn(x, __ldg(bias + c * 32 + d));
+                            ss += (double)__fmul_rn(x, x);
+                        }
+                    }
+                    scale = __frcp_rn(__fsqrt_rn(__fadd_rn((float)(ss * (1.0 / 128.0)), p.eps)));
+                }
+                // Pass 2: bias, x * scale * gain, RoPE, cast, 64 bytes stored per chunk.
+                TO* dst = reinterpret_cast<TO*>(static_cast<char*>(S.out) + (long long)n * S.o_nb3 +
+                                                (long long)h * S.o_nb2 + (long long)l * S.o_nb1);
+                const float2* cs = S.rope ? p.rope_cs + (long long)l * 64 : nullptr;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t xr[32];
+                    tmem_ld32_sync(taddr + c * 32, xr);
+                    if (hh == 1 && c == 3) {  // the whole tile has been read: the next tile's MMAs may overwrite it
+                        tc_fence_before();
+                        mbar_arrive(&acc_empty[ab]);
+                    }
+                    float x[32];
+#pragma unroll
+                    for (int d = 0; d < 32; ++d) {
+                        x[d] = __uint_as_float(xr[d]);
+                        if (bias) x[d] = __fadd_rn(x[d], __ldg(bias + c * 32 + d));
+                        if (S.norm) x[d] = __fmul_rn(__fmul_rn(x[d], scale), S.gain ? __ldg(S.gain + c * 32 + d) : 1.0f);
+                    }
+                    if (cs) {
+                        // rope::apply (rope.hpp:140-141): (x0 c - x1 s, x0 s + x1 c), products rounded apart
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 a = __ldg(cs + c * 16 + i);  // (cos, sin)
+                            const float x0 = x[2 * i], x1 = x[2 * i + 1];
+                            x[2 * i] = __fsub_rn(__fmul_rn(x0, a.x), __fmul_rn(x1, a.y));
+                            x[2 * i + 1] = __fadd_rn(__fmul_rn(x0, a.y), __fmul_rn(x1, a.x));
+                        }
+                    }
+                    if (valid) store_chunk<TO>(dst + c * 32, x);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// One thread per 32-element block of one output-feature row: ggml weight -> bf16 row of B.
+__global__ void expand_weights_kernel(const uint8_t* w, int type, long long row_bytes, int K, int rows, int row0,
+                                      __nv_bfloat16* dst) {
+    const long long blocks_per_row = K / 32;
+    const long long total = blocks_per_row * rows;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int o = (int)(i / blocks_per_row), b = (int)(i % blocks_per_row);
+        const uint8_t* src = w + (long long)o * row_bytes;
+        float v[32];
+        if (type == 8) {  // q8_0: f16 d, int8 q[32]
+            const uint8_t* blk = src + (long long)b * 34;
+            const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = d * (float)(int8_t)blk[2 + j];
+        } else if (type == 2) {  // q4_0: f16 d, 16 bytes; element j low nibble, j+16 high nibble, value d*(q-8)
+            const uint8_t* blk = src + (long long)b * 18;
+            const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                v[j] = d * (float)((int)(blk[2 + j] & 0x0F) - 8);
+                v[j + 16] = d * (float)((int)(blk[2 + j] >> 4) - 8);
+            }
+        } else if (type == 0) {
+            const float* f = reinterpret_cast<const float*>(src) + b * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = f[j];
+        } else {
+            const unsigned short* u = reinterpret_cast<const unsigned short*>(src) + b * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                v[j] = type == 1 ? __half2float(__ushort_as_half(u[j])) : __bfloat162float(__ushort_as_bfloat16(u[j]));
+        }
+        uint4* d = reinterpret_cast<uint4*>(dst + (long long)(row0 + o) * K + b * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            d[q] = make_uint4(Pack2<__nv_bfloat16>::pack(v[8 * q], v[8 * q + 1]),
+                              Pack2<__nv_bfloat16>::pack(v[8 * q + 2], v[8 * q + 3]),
+                              Pack2<__nv_bfloat16>::pack(v[8 * q + 4], v[8 * q + 5]),
+                              Pack2<__nv_bfloat16>::pack(v[8 * q + 6], v[8 * q + 7]));
+    }
+}
+
+// x f32 [K, L, N] (rows 16-byte aligned) -> bf16 [K, L*N] contiguous; 8 elements per thread.
+__global__ void to_bf16_rows_kernel(const char* x, long long nb1, long long nb2, int K, int L, long long M,
+                                    __nv_bfloat16* dst) {
+    const long long per_row = K / 8;
+    const long long total = per_row * M;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long m = i / per_row;
+        const int c = (int)(i % per_row) * 8;
+        const float4* s = reinterpret_cast<const float4*>(x + (m / L) * nb2 + (m % L) * nb1 + (long long)c * 4);
+        const float4 a = s[0], b = s[1];
+        *reinterpret_cast<uint4*>(dst + m * K + c) =
+            make_uint4(Pack2<__nv_bfloat16>::pack(a.x, a.y), Pack2<__nv_bfloat16>::pack(a.z, a.w),
+                       Pack2<__nv_bfloat16>::pack(b.x, b.y), Pack2<__nv_bfloat16>::pack(b.z, b.w));
+    }
+}
+
+// (cos, sin) of every (token l, rotary pair i): angle = pos_axis(l) * freq_i / scale_axis, the
+// prologue's formula (rope.hpp:78-95 order of operations, correctly rounded float ops).
+__global__ void rope_table_kernel(const RopeTab tab, int L, float2* cs) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)L * 64;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int l = (int)(i / 64), pi = (int)(i % 64);
+        const int w = l % tab.grid_w, hh = (l / tab.grid_w) % tab.grid_h, t = l / (tab.grid_w * tab.grid_h);
+        const int ax = tab.axis[pi];
+        const float pos = (float)(ax == 0 ? t : (ax == 1 ? hh : w));
+        float s, c;
+        sincosf(__fdiv_rn(__fmul_rn(pos, tab.freq[pi]), tab.div[pi]), &s, &c);
+        cs[i] = make_float2(c, s);
+    }
+}
+
+int grid_1d(long long work, int num_sms) {
+    long long b = (work + 255) / 256;
+    const long long cap = (long long)num_sms * 8;
+    if (b > cap) b = cap;
+    return (int)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+cudaError_t launch_expand_weights(const void* w, int type, long long row_bytes, int K, int rows, int row0,
+                                  __nv_bfloat16* dst, int num_sms, cudaStream_t st) {
+    const long long total = (long long)(K / 32) * rows;
+    if (total == 0) return cudaSuccess;
+    expand_weights_kernel<<<grid_1d(total, num_sms), 256, 0, st>>>(static_cast<const uint8_t*>(w), type, row_bytes, K,
+                                                                    rows, row0, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int K, int L, long long M,
+                                __nv_bfloat16* dst, int num_sms, cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    to_bf16_rows_kernel<<<grid_1d(M * (K / 8), num_sms), 256, 0, st>>>(static_cast<const char*>(x), nb1, nb2, K, L, M,
+                                                                       dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms, cudaStream_t st) {
+    if (L == 0) return cudaSuccess;
+    rope_table_kernel<<<grid_1d((long long)L * 64, num_sms), 256, 0, st>>>(tab, L, cs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
+                            cudaStream_t st) {
+    auto kern = ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16> : qkv_gemm_kernel<__half>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemAlloc);
+    if (e != cudaSuccess) return e;
+    const long long tiles = (long long)((p.M + kBM - 1) / kBM) * (p.nslots * p.C / kBN);
+    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+    if (grid <= 0) return cudaSuccess;
+    kern<<<grid, kGThreads, kGSmemAlloc, st>>>(tmX, tmW, p);
+    return cudaGetLastError();
+}
+
+}  // namespace kd

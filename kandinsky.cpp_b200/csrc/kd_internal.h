@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -130,6 +131,42 @@ struct MaskClassParams {
     int n_qb, n_kb;
 };
 cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st);
+
+// ---------------------------------------------------------------- QKV projection (kd_gemm.cu)
+// One projection of the fused GEMM: C output features = C/128 heads, written as [128, L, H, N].
+struct QkvSlot {
+    void* out;
+    long long o_nb1, o_nb2, o_nb3;  // byte strides of out (row, head, sequence)
+    const float* bias;              // [C] or null
+    const float* gain;              // [128] or null (unit gain); read when norm
+    int norm;                       // 1: RMSNorm per head
+    int rope;                       // 1: rotate with QkvParams::rope_cs
+};
+struct QkvParams {
+    QkvSlot slot[3];
+    int nslots;              // projections concatenated along the B operand's rows (slot s = rows [s*C, (s+1)*C))
+    int C;                   // output features per projection, a multiple of 256
+    int K;                   // input features
+    int M;                   // tokens = L * N
+    int L;                   // tokens per sequence (token m is l = m % L of sequence n = m / L)
+    float eps;
+    const float2* rope_cs;   // [L][64] (cos, sin) or null
+    unsigned* err;
+    unsigned* abort_flag;
+    unsigned long long wait_ns;
+};
+// tmX: bf16 [K, M] with a {64, 128} box; tmW: bf16 [K, nslots*C] with a {64, 256} box; both 128-byte swizzled.
+cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
+                            cudaStream_t st);
+// ggml weight rows [rows][row_bytes] of type f32 (0), f16 (1), q4_0 (2), q8_0 (8), bf16 (30) -> bf16 rows
+// row0 .. row0+rows-1 of dst [*, K]; K a multiple of 32.
+cudaError_t launch_expand_weights(const void* w, int type, long long row_bytes, int K, int rows, int row0,
+                                  __nv_bfloat16* dst, int num_sms, cudaStream_t st);
+// f32 x [K, L, N] (byte strides nb1, nb2; K a multiple of 8, rows 16-byte aligned) -> bf16 [M = L*N][K].
+cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int K, int L, long long M,
+                                __nv_bfloat16* dst, int num_sms, cudaStream_t st);
+// (cos, sin) of every token and rotary pair of the 3D RoPE table: cs[l * 64 + i].
+cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms, cudaStream_t st);
 
 // One bounded wait that nothing releases (sets the self-test error bit after wait_ns).
 cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned long long wait_ns, cudaStream_t st);

@@ -32,8 +32,9 @@ ERR_OUT_OF_MEMORY = -4
 ERR_DEVICE_TIMEOUT = -5
 ERR_NCCL = -6
 
-# ggml type ids (kd_attn_type)
+# ggml type ids (kd_attn_type; Q4_0 / Q8_0 for Linear weights)
 F32, F16, BF16 = 0, 1, 30
+Q4_0, Q8_0 = 2, 8
 
 EXPORTED = [
     "kd_attn_create", "kd_attn_destroy", "kd_attn_last_error", "kd_attn_device_status",
@@ -43,6 +44,7 @@ EXPORTED = [
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
     "kd_attn_selftest_wait", "kd_attn_noalloc_status", "kd_attn_noalloc_selftest_wait",
+    "kd_attn_qkv_projection",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -82,6 +84,25 @@ class KdTensor(ctypes.Structure):
                 k.ne[i] = 1
                 k.nb[i] = k.nb[i - 1] * k.ne[i - 1] if i > 0 else es
         return k
+
+
+class KdLinear(ctypes.Structure):
+    """kd_linear: a Linear layer's weight in ggml layout [K, C] (C rows of K elements of `type`) + f32 bias."""
+    _fields_ = [("data", ctypes.c_void_p), ("type", ctypes.c_int32), ("ne", ctypes.c_int64 * 2),
+                ("nb1", ctypes.c_size_t), ("bias", ctypes.c_void_p)]
+
+    @staticmethod
+    def of(weight, type, in_features, out_features, bias=None):
+        """weight: device tensor holding the rows (uint8 bytes of ggml blocks for q4_0/q8_0, or
+        f32/f16/bf16 elements) shaped (out_features, row) -- one row per output feature."""
+        w = KdLinear()
+        w.data = weight.data_ptr()
+        w.type = int(type)
+        w.ne[0] = int(in_features)
+        w.ne[1] = int(out_features)
+        w.nb1 = weight.stride(0) * weight.element_size()
+        w.bias = None if bias is None else bias.data_ptr()
+        return w
 
 
 class Rope3D(ctypes.Structure):
@@ -131,6 +152,10 @@ def _load():
     L.kd_attn_qk_prologue.argtypes = [P, T, T, T, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), ctypes.c_int32,
                                       T, T, T, P]
     L.kd_attn_qk_prologue.restype = st
+    W = ctypes.POINTER(KdLinear)
+    L.kd_attn_qkv_projection.argtypes = [P, T, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D),
+                                         ctypes.c_int32, T, T, T, P]
+    L.kd_attn_qkv_projection.restype = st
     L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
@@ -310,6 +335,21 @@ class Context:
                                            _ptr(k_gain), float(eps), None if rope is None else ctypes.byref(rope),
                                            int(out_dtype), _ref(q_out), _ref(k_out), _ref(v_out),
                                            _stream_ptr(stream)))
+        return q_out, k_out, v_out
+
+    def qkv_projection(self, x, wq, wk, wv, q_out, k_out, v_out, q_gain=None, k_gain=None, eps=1e-6, rope=None,
+                       stream=None):
+        """to_query/to_key/to_value + prologue as one GEMM: x (N, L, K) f32; wq/wk/wv KdLinear or None;
+        q_out/k_out/v_out (N, H, L, 128) f16/bf16 (ggml [128, L, H, N]) or None with their weight."""
+        outs = [t for t in (q_out, k_out, v_out) if t is not None]
+        if len({t.dtype for t in outs}) > 1:
+            raise ValueError("outputs must share one dtype")
+        out_dtype = KdTensor.of(outs[0]).type if outs else BF16
+        ref_w = lambda w: None if w is None else ctypes.byref(w)
+        self.check(lib.kd_attn_qkv_projection(self.handle, _ref(x), ref_w(wq), ref_w(wk), ref_w(wv), _ptr(q_gain),
+                                              _ptr(k_gain), float(eps), None if rope is None else ctypes.byref(rope),
+                                              int(out_dtype), _ref(q_out), _ref(k_out), _ref(v_out),
+                                              _stream_ptr(stream)))
         return q_out, k_out, v_out
 
     def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,

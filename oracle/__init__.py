@@ -227,3 +227,98 @@ def parity_metrics(got, ref):
     rms = float(np.sqrt(np.mean(r * r)))
     mae = float(np.max(np.abs(g - r))) if g.size else 0.0
     return {"cos": cos, "maxabs_over_rms": mae / (rms + 1e-300), "maxabs": mae, "rms": rms}
+
+
+# ---------------------------------------------------------------- Linear weights (ggml block formats)
+# A Linear weight of ggml shape [K, C] is C rows of K elements; the quantized types store each row as
+# K/32 blocks.  The quantizers restate the reference converter (scripts/convert_to_gguf.py:90-146), the
+# dequantizers ggml's published block formats:
+#   q8_0: 34 bytes = f16 d, 32 x int8 q;                        value = d * q
+#   q4_0: 18 bytes = f16 d, 16 bytes, element j low nibble,
+#         element j+16 high nibble;                              value = d * (nibble - 8)
+Q4_0, Q8_0 = 2, 8
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34}
+
+
+def quantize_q8_0(w):
+    """(rows, K) float -> (rows, K/32*34) uint8.  d = amax/127 (1 for an all-zero block), q = round-half-even
+    (x / d) clipped to int8 -- numpy's round, as the converter uses; d is computed in f32 and stored as f16."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, K = w.shape
+    b = w.reshape(rows, K // 32, 32)
+    d = (np.abs(b).max(axis=2) / np.float32(127.0)).astype(np.float32)
+    d[d == 0] = 1.0
+    q = np.clip(np.round(b / d[..., None]), -128, 127).astype(np.int8)
+    out = np.empty((rows, K // 32, 34), dtype=np.uint8)
+    out[..., :2] = d.astype(np.float16)[..., None].view(np.uint8)
+    out[..., 2:] = q.view(np.uint8)
+    return out.reshape(rows, -1)
+
+
+def quantize_q4_0(w):
+    """(rows, K) float -> (rows, K/32*18) uint8.  d = (the element of largest magnitude, with its sign) / -8,
+    nibble = trunc(x / d + 8.5) clipped to [0, 15] (x / d taken as x * (1/d) in f32; 1/d = 0 for an
+    all-zero block); d stored as f16."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, K = w.shape
+    b = w.reshape(rows, K // 32, 32)
+    idx = np.abs(b).argmax(axis=2)
+    signed_max = np.take_along_axis(b, idx[..., None], axis=2)[..., 0]
+    d = (signed_max / np.float32(-8.0)).astype(np.float32)
+    inv = np.zeros_like(d)
+    nz = np.abs(b).max(axis=2) > 0
+    inv[nz] = np.float32(1.0) / d[nz]
+    lo = np.clip((b[..., :16] * inv[..., None] + np.float32(8.5)).astype(np.int32), 0, 15).astype(np.uint8)
+    hi = np.clip((b[..., 16:] * inv[..., None] + np.float32(8.5)).astype(np.int32), 0, 15).astype(np.uint8)
+    out = np.empty((rows, K // 32, 18), dtype=np.uint8)
+    out[..., :2] = d.astype(np.float16)[..., None].view(np.uint8)
+    out[..., 2:] = lo | (hi << 4)
+    return out.reshape(rows, -1)
+
+
+def dequantize(wq, type_, K):
+    """ggml weight rows -> (rows, K) float32: q8_0 / q4_0 bytes, or f32 / f16 / bf16 (uint16 bits) elements."""
+    if type_ == F32:
+        return np.asarray(wq, np.float32).reshape(-1, K)
+    if type_ in (F16, BF16):
+        return to_f32(np.asarray(wq).reshape(-1, K), type_)
+    wq = np.ascontiguousarray(wq, dtype=np.uint8)
+    blocks = wq.reshape(wq.shape[0], K // 32, BLOCK_BYTES[type_])
+    d = blocks[..., :2].copy().view(np.float16)[..., 0].astype(np.float32)
+    if type_ == Q8_0:
+        q = blocks[..., 2:].view(np.int8).astype(np.float32)
+    elif type_ == Q4_0:
+        p = blocks[..., 2:]
+        q = np.concatenate([(p & 0x0F), (p >> 4)], axis=2).astype(np.float32) - 8.0
+    else:
+        raise ValueError(f"unknown weight type {type_}")
+    return (d[..., None] * q).reshape(-1, K)
+
+
+def linear(x, w, bias=None):
+    """ops::linear (ops.hpp:27-42): ggml_mul_mat(w, x) + bias, in float64 on the given float32 operands.
+    x: (..., K); w: (C, K) float32 (dequantized rows); bias: (C,) or None.  Returns (..., C) float64."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y
+
+
+def qkv_projection(x, w, bias, n_head, q_gain=None, k_gain=None, rope_table=None, eps=1e-6):
+    """to_query/to_key/to_value (crossdit.hpp:123-125) followed by the prologue of each projection.
+
+    x: (N, L, K) float32; w / bias: 3-lists (q, k, v) of (C, K) float32 rows and (C,) or None -- an entry
+    may be None to skip that projection.  Returns 3 arrays [d, L, H, N] = numpy (N, H, L, d) float32 (the
+    f32 projections rounded to float32 before the prologue, as ggml stores them)."""
+    outs = []
+    for i in range(3):
+        if w[i] is None:
+            outs.append(None)
+            continue
+        y = linear(x, w[i], bias[i]).astype(np.float32)
+        if i < 2:
+            outs.append(prologue(y, n_head, q_gain if i == 0 else k_gain, rope_table, eps))
+        else:
+            N, L, C = y.shape
+            outs.append(np.ascontiguousarray(y.reshape(N, L, n_head, C // n_head).transpose(0, 2, 1, 3)))
+    return outs

@@ -1,0 +1,177 @@
+"""kd_attn_qkv_projection: to_query/to_key/to_value (crossdit.hpp:123-125) as one tcgen05 GEMM whose
+epilogue is the prologue (bias, per-head RMSNorm, 3D RoPE, cast, operand layout).
+
+Every case is checked twice against the fp64 oracle (oracle.qkv_projection: numpy dequantization of the
+ggml blocks, float64 matmul + bias, rounded to f32, then the prologue restatement):
+  - on the exact operands (f32 x, dequantized weights) with the north-star gates -- the GEMM rounds x and
+    the weights to bf16, which these gates absorb;
+  - on the operands rounded to bf16 as the GEMM reads them, where only the fp32 accumulation order and the
+    output rounding remain: max-abs beyond the output format's half ulp <= 2e-3 x RMS.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_gates, seeded
+
+pytestmark = pytest.mark.gpu
+
+TIGHT = 2e-3
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def make_weight(kd, seed, off, C, K, wtype, bias=True):
+    """Seeded N(0, 1/K) weight stored as `wtype` on the device; returns (KdLinear, keep-alive, dequantized
+    f32 rows (C, K), bias f32 or None)."""
+    w = seeded((C, K), seed, off) / np.float32(np.sqrt(K))
+    b = (0.5 * seeded((C,), seed, off + 1)).astype(np.float32) if bias else None
+    if wtype == kd.Q8_0:
+        raw = oracle.quantize_q8_0(w)
+    elif wtype == kd.Q4_0:
+        raw = oracle.quantize_q4_0(w)
+    elif wtype == kd.F16:
+        raw = w.astype(np.float16)
+    elif wtype == kd.BF16:
+        raw = oracle.to_type(w, oracle.BF16).view(np.int16)
+    else:
+        raw = w
+    deq = oracle.dequantize(raw.view(np.uint16) if wtype == kd.BF16 else raw, wtype, K)
+    t = dev(raw)
+    if wtype == kd.BF16:
+        t = t.view(torch.bfloat16)
+    bt = None if b is None else dev(b)
+    return kd.KdLinear.of(t, wtype, K, C, bt), (t, bt), deq, b
+
+
+def bf16_round(a):
+    return oracle.to_f32(oracle.to_type(np.ascontiguousarray(a, np.float32), oracle.BF16), oracle.BF16)
+
+
+def check(got, x, w, b, H, q_gain, k_gain, tab, out_type, label):
+    """got: 3 device tensors (or None) (N, H, L, 128)."""
+    exact = oracle.qkv_projection(x, w, b, H, q_gain, k_gain, tab)
+    wr = [None if a is None else bf16_round(a) for a in w]
+    rounded = oracle.qkv_projection(bf16_round(x), wr, b, H, q_gain, k_gain, tab)
+    half = 2.0 ** -8 if out_type == "bf16" else 2.0 ** -11
+    for name, g, e, r in zip("qkv", got, exact, rounded):
+        if g is None:
+            continue
+        gn = g.float().cpu().numpy()
+        assert_gates(gn, e, label=f"{label} {name} vs exact operands", out_type=out_type)
+        rms = float(np.sqrt(np.mean(np.asarray(r, np.float64) ** 2)))
+        excess = float(np.max(np.abs(gn - r) - np.abs(r) * half)) / rms
+        assert excess <= TIGHT, f"{label} {name}: {excess:.3e} x RMS beyond {out_type} rounding vs bf16-rounded operands"
+
+
+WTYPES = {"q8_0": 8, "q4_0": 2, "f16": 1, "bf16": 30, "f32": 0}
+
+
+@pytest.mark.parametrize("wname", list(WTYPES))
+def test_self_attention_projection_matches_oracle(ctx, kd, wname):
+    """Q, K, V of self-attention from one x, every weight type, bias, gains, RoPE with scale (1, 2, 2);
+    600 tokens = 4 full 128-row tiles and a ragged fifth."""
+    N, grid, K, H = 2, (3, 10, 10), 1024, 8
+    L, C = int(np.prod(grid)), H * 128
+    x = seeded((N, L, K), 71, 0)
+    lin = [make_weight(kd, 72, 10 * i, C, K, WTYPES[wname], bias=(i != 1)) for i in range(3)]
+    q_gain = (1.0 + 0.1 * seeded((128,), 73, 0)).astype(np.float32)
+    k_gain = (1.0 + 0.1 * seeded((128,), 73, 1)).astype(np.float32)
+    tab = oracle.visual_rope_table(grid, scale=(1.0, 2.0, 2.0))
+    outs = [torch.full((N, H, L, 128), float("nan"), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(dev(x), lin[0][0], lin[1][0], lin[2][0], *outs, q_gain=dev(q_gain), k_gain=dev(k_gain),
+                       rope=kd.Rope3D.make(grid, scale=(1.0, 2.0, 2.0)))
+    ctx.device_status()
+    check(outs, x, [l[2] for l in lin], [l[3] for l in lin], H, q_gain, k_gain, tab, "bf16", wname)
+
+
+def test_model_width_q8_0_f16_operands(ctx, kd):
+    """The Kandinsky 5 Pro width (4096 = 32 heads of 128) with q8_0 weights and f16 operands; unit gains."""
+    N, grid, K, H = 1, (2, 10, 11), 4096, 32
+    L, C = int(np.prod(grid)), H * 128
+    x = seeded((N, L, K), 81, 0) * 2.0
+    lin = [make_weight(kd, 82, 10 * i, C, K, kd.Q8_0) for i in range(3)]
+    tab = oracle.visual_rope_table(grid)
+    outs = [torch.empty((N, H, L, 128), device="cuda", dtype=torch.float16) for _ in range(3)]
+    ctx.qkv_projection(dev(x), lin[0][0], lin[1][0], lin[2][0], *outs, rope=kd.Rope3D.make(grid))
+    ctx.device_status()
+    check(outs, x, [l[2] for l in lin], [l[3] for l in lin], H, None, None, tab, "f16", "width 4096")
+
+
+def test_ragged_k_and_strided_x(ctx, kd):
+    """in_features 544 (not a multiple of the 64-wide K step: the last step is zero-filled) and x given as a
+    strided view (rows of a wider buffer)."""
+    N, L, K, H = 2, 77, 544, 2
+    C = H * 128
+    wide = seeded((N, L, K + 32), 91, 0)
+    x = wide[:, :, :K]
+    lin = [make_weight(kd, 92, 10 * i, C, K, kd.F16) for i in range(3)]
+    outs = [torch.empty((N, H, L, 128), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(dev(wide)[:, :, :K], lin[0][0], lin[1][0], lin[2][0], *outs)
+    ctx.device_status()
+    check(outs, x, [l[2] for l in lin], [l[3] for l in lin], H, None, None, None, "bf16", "K=544")
+
+
+def test_cross_attention_projections(ctx, kd):
+    """Cross-attention (crossdit.hpp:174-200): Q alone from the visual tokens (RMSNorm, no RoPE), then K and
+    V from 77 text tokens in a second call -- slots left out of the GEMM."""
+    N, Lq, Lt, K, H = 2, 256, 77, 512, 4
+    C = H * 128
+    xv, xt = seeded((N, Lq, K), 95, 0), seeded((N, Lt, K), 95, 1)
+    lq, lk, lv = (make_weight(kd, 96, 10 * i, C, K, kd.Q4_0) for i in range(3))
+    q = torch.empty((N, H, Lq, 128), device="cuda", dtype=torch.bfloat16)
+    k = torch.empty((N, H, Lt, 128), device="cuda", dtype=torch.bfloat16)
+    v = torch.empty_like(k)
+    ctx.qkv_projection(dev(xv), lq[0], None, None, q, None, None)
+    ctx.qkv_projection(dev(xt), None, lk[0], lv[0], None, k, v)
+    ctx.device_status()
+    check([q, None, None], xv, [lq[2], None, None], [lq[3], None, None], H, None, None, None, "bf16", "cross q")
+    check([None, k, v], xt, [None, lk[2], lv[2]], [None, lk[3], lv[3]], H, None, None, None, "bf16", "cross kv")
+
+
+def test_projection_feeds_flash_attention(ctx, kd):
+    """x -> kd_attn_qkv_projection -> kd_attn_flash_ext (bf16 operands, no copies between them) against
+    the oracle's linear + self_attention on the exact operands."""
+    N, grid, K, H = 1, (2, 8, 16), 512, 4
+    L, C = int(np.prod(grid)), H * 128
+    x = seeded((N, L, K), 101, 0)
+    lin = [make_weight(kd, 102, 10 * i, C, K, kd.Q8_0) for i in range(3)]
+    outs = [torch.empty((N, H, L, 128), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(dev(x), lin[0][0], lin[1][0], lin[2][0], *outs, rope=kd.Rope3D.make(grid))
+    o = torch.empty(N, L, H, 128, device="cuda")
+    ctx.flash_attn_ext(*outs, o)
+    ctx.device_status()
+    proj = [oracle.linear(x, l[2], l[3]).astype(np.float32) for l in lin]
+    ref = oracle.self_attention(*proj, H, rope_table=oracle.visual_rope_table(grid), kv_type=oracle.BF16,
+                                q_type=oracle.BF16, mode=oracle.EXACT)
+    m = oracle.parity_metrics(o.cpu().numpy().reshape(N, L, C), ref)
+    assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m
+
+
+def test_rejected_shapes(ctx, kd):
+    K, C = 256, 256
+    x = torch.zeros(1, 8, K, device="cuda")
+    w = torch.zeros(C, K, device="cuda", dtype=torch.float16)
+    lin = kd.KdLinear.of(w, kd.F16, K, C)
+    out = torch.empty(1, 2, 8, 128, device="cuda", dtype=torch.bfloat16)
+    for bad_out, status in ((torch.empty(1, 2, 8, 128, device="cuda"), kd.ERR_UNSUPPORTED),      # f32 operands
+                            (torch.empty(1, 2, 9, 128, device="cuda", dtype=torch.bfloat16), kd.ERR_INVALID_ARGUMENT)):
+        with pytest.raises(kd.KdAttnError) as e:
+            ctx.qkv_projection(x, None, None, lin, None, None, bad_out)
+        assert e.value.status == status
+    w128 = torch.zeros(128, K, device="cuda", dtype=torch.float16)        # 128 output features: one head
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.qkv_projection(x, None, None, kd.KdLinear.of(w128, kd.F16, K, 128), None, None, out[:, :1])
+    assert e.value.status == kd.ERR_UNSUPPORTED
+    with pytest.raises(kd.KdAttnError) as e:                               # q4_1 is not a supported block type
+        ctx.qkv_projection(x, None, None, kd.KdLinear.of(w, 3, K, C), None, None, out)
+    assert e.value.status == kd.ERR_UNSUPPORTED
+    with pytest.raises(kd.KdAttnError) as e:                               # a weight without its output
+        ctx.qkv_projection(x, lin, None, None, None, None, None)
+    assert e.value.status == kd.ERR_INVALID_ARGUMENT
+    ctx.qkv_projection(x, None, None, lin, None, None, out)
+    ctx.device_status()
+    assert torch.count_nonzero(out.float()) == 0

@@ -198,3 +198,60 @@ def test_ggml_mode_f16_accumulator_is_the_only_difference():
 def test_f16_conversion_round_trip_matches_numpy():
     x = np.concatenate([_rand((10000,), 13) * 1000, np.array([65504, 65519.99, 65520, 1e-8, 6e-5, -0.0, 3e-8], np.float32)])
     np.testing.assert_array_equal(oracle.to_type(x, oracle.F16), x.astype(np.float16))
+
+
+# ------------------------------------------------------------------ Linear weight formats
+QUANT_GOLD = os.path.join(os.path.dirname(__file__), "golden", "quant_pin.npz")
+
+
+@pytest.mark.parametrize("case", ["rand", "heavy", "edge"])
+def test_quantizers_match_reference_converter(case):
+    """q8_0 / q4_0 bytes equal those of the reference converter (scripts/convert_to_gguf.py:90-146),
+    stored by tests/golden/make_quant_golden.py, including round-half-even ties and all-zero blocks."""
+    g = np.load(QUANT_GOLD)
+    w = g[f"{case}_w"]
+    np.testing.assert_array_equal(oracle.quantize_q8_0(w), g[f"{case}_q8_0"])
+    np.testing.assert_array_equal(oracle.quantize_q4_0(w), g[f"{case}_q4_0"])
+
+
+def test_dequantize_known_blocks():
+    """Hand-built blocks: q8_0 d = 0.5 with q = -128..127 pattern; q4_0 d = -0.25 with element j in the low
+    nibble and j + 16 in the high nibble."""
+    q8 = np.zeros((1, 34), np.uint8)
+    q8[0, :2] = np.array([0.5], np.float16).view(np.uint8)
+    q = (np.arange(32) * 8 - 128).astype(np.int8)
+    q8[0, 2:] = q.view(np.uint8)
+    np.testing.assert_array_equal(oracle.dequantize(q8, oracle.Q8_0, 32)[0], q.astype(np.float32) * 0.5)
+    q4 = np.zeros((1, 18), np.uint8)
+    q4[0, :2] = np.array([-0.25], np.float16).view(np.uint8)
+    lo, hi = np.arange(16, dtype=np.uint8), (15 - np.arange(16)).astype(np.uint8)
+    q4[0, 2:] = lo | (hi << 4)
+    want = np.concatenate([lo, hi]).astype(np.float32) - 8.0
+    np.testing.assert_array_equal(oracle.dequantize(q4, oracle.Q4_0, 32)[0], want * -0.25)
+
+
+def test_quantize_dequantize_error_bounds():
+    """Round trip within half a step, plus the f16 rounding of the stored scale (the quantizers divide by
+    the f32 scale): q8_0 |w - deq| <= d/2 + 127 d 2^-11; q4_0 within one step (the +8 end clips to 7)."""
+    w = (np.random.default_rng(5).standard_normal((16, 256)) * 0.05).astype(np.float32)
+    b = np.abs(w.reshape(16, 8, 32)).max(axis=2)
+    e8 = np.abs(oracle.dequantize(oracle.quantize_q8_0(w), oracle.Q8_0, 256) - w).reshape(16, 8, 32).max(axis=2)
+    assert np.all(e8 <= b / 127 * (0.5 + 127 * 2.0 ** -11) * (1 + 1e-3))
+    e4 = np.abs(oracle.dequantize(oracle.quantize_q4_0(w), oracle.Q4_0, 256) - w).reshape(16, 8, 32).max(axis=2)
+    assert np.all(e4 <= b / 8 * (1 + 8 * 2.0 ** -11) * (1 + 1e-3))
+
+
+def test_qkv_projection_oracle_is_linear_then_prologue():
+    """The projection oracle = f64 matmul + bias, rounded to f32, then the prologue (Q, K) or a permute (V)."""
+    rng = np.random.default_rng(3)
+    N, L, K, H = 1, 12, 64, 2
+    x = rng.standard_normal((N, L, K)).astype(np.float32)
+    w = [rng.standard_normal((H * 128, K)).astype(np.float32) * 0.1 for _ in range(3)]
+    b = [rng.standard_normal(H * 128).astype(np.float32), None, rng.standard_normal(H * 128).astype(np.float32)]
+    tab = oracle.visual_rope_table((1, 3, 4))
+    q, k, v = oracle.qkv_projection(x, w, b, H, rope_table=tab)
+    yq = (x.astype(np.float64) @ w[0].T.astype(np.float64) + b[0]).astype(np.float32)
+    np.testing.assert_array_equal(q, oracle.prologue(yq, H, rope_table=tab))
+    yv = (x.astype(np.float64) @ w[2].T.astype(np.float64) + b[2]).astype(np.float32)
+    np.testing.assert_array_equal(v, yv.reshape(N, L, H, 128).transpose(0, 2, 1, 3))
+    assert k.shape == (N, H, L, 128)
