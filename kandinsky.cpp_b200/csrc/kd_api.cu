@@ -1133,8 +1133,8 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         p.rope_cs = cs;
     }
     CUtensorMap tmX, tmW;
-    if ((rc = make_gemm_map(ctx, &tmX, xb, K, p.M, 128)) ||
-        (rc = make_gemm_map(ctx, &tmW, wb, K, (int64_t)p.nslots * C, 256)))
+    if ((rc = make_gemm_map(ctx, &tmX, xb, K, p.M, kGemmBoxRowsA)) ||
+        (rc = make_gemm_map(ctx, &tmW, wb, K, (int64_t)p.nslots * C, kGemmBoxRowsB)))
         return rc;
     p.err = ctx->d_words;
     p.abort_flag = ctx->d_words + 1;

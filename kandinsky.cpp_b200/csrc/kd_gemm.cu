@@ -15,9 +15,9 @@
 //                          -> bf16 rows of the concatenated [C_in, 3*C_out] B operand
 //   to_bf16_rows_kernel    x f32 [C_in, L, N] -> bf16 [C_in, L*N] (the A operand, token rows)
 //   rope_table_kernel      cos/sin of every (token, rotary pair), the prologue's angle formula
-//   qkv_gemm_kernel        persistent tcgen05 GEMM, 128 tokens x 256 output features per tile
-//                          (two heads of one projection), K = C_in in steps of 64 through a 4-stage
-//                          TMA ring, fp32 accumulators double-buffered in TMEM so one tile's
+//   qkv_gemm_kernel        persistent tcgen05 GEMM on CTA pairs, 256 tokens x 256 output features
+//                          per tile (two heads of one projection), K = C_in in steps of 64 through a
+//                          6-stage TMA ring, fp32 accumulators double-buffered in TMEM so one tile's
 //                          epilogue overlaps the next tile's MMAs
 //
 // Every wait is bounded (kd_common.cuh: mbar_wait).
@@ -27,13 +27,22 @@
 namespace kd {
 namespace {
 
-constexpr int kBM = 128;                 // tokens per tile (MMA M)
+// Tiles of 256 tokens x 256 output features are computed by a CTA pair (a cluster of 2 on neighbouring
+// SMs) with tcgen05.mma.cta_group::2: each CTA stages its 128 token rows of A and its 128 feature rows of B,
+// the MMA (M = 256, N = 256, issued by the pair's rank-0 CTA) reads both CTAs' halves, and each CTA's TMEM
+// receives the 128 x 256 accumulator of its own token rows.  Per SM that is 16 KB of A and 16 KB of B per
+// 64-wide K step -- two thirds of the shared-memory traffic of a one-CTA 128 x 256 tile, whose TMA writes
+// plus MMA operand reads exceed the SM's shared-memory bandwidth (measured: tensor pipe 56 % active).
+constexpr int kBM = kGemmBoxRowsA;       // token rows per CTA (the pair covers 256)
+constexpr int kPairM = 2 * kBM;
 constexpr int kBN = 256;                 // output features per tile (MMA N): two heads
+constexpr int kHalfN = kGemmBoxRowsB;    // B rows staged by each CTA
+static_assert(kBM == 128 && 2 * kHalfN == kBN, "pair tile geometry");
 constexpr int kBK = 64;                  // K per stage (one 128-byte swizzled row)
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kBBytes = kHalfN * kBK * 2;  // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kGStages = 4;
+constexpr int kGStages = 6;
 constexpr int kGSmemBar = kGStages * kStageBytes;
 // full[S], empty[S], acc_full[2], acc_empty[2]
 constexpr int kGNumBars = 2 * kGStages + 4;
@@ -41,10 +50,10 @@ constexpr int kGSmemSlot = kGSmemBar + kGNumBars * 8;
 constexpr int kGSmemAlloc = kGSmemSlot + 16 + 1024;
 static_assert(kGSmemAlloc <= 232448, "shared memory budget");
 constexpr int kGThreads = 256;
-constexpr int kGroupM = 16;  // m-tiles per raster band: the tiles in flight share 16 A row blocks and ~10 B column blocks
+constexpr int kGroupM = 8;  // 256-row m-tiles per raster band: the pairs in flight share 8 A blocks and ~9 B blocks
 
 // Tile t of the persistent loop -> (m-tile, n-tile).  Bands of kGroupM m-tiles are swept n-tile by n-tile,
-// m fastest, so the CTAs running at one time read a few MB of A and B that stay in L2.
+// m fastest, so the pairs running at one time read a few MB of A and B that stay in L2.
 __device__ __forceinline__ void tile_coords(long long t, int m_tiles, int n_tiles_n, int& mt, int& nt) {
     const long long band = t / ((long long)kGroupM * n_tiles_n);
     const int first = (int)band * kGroupM;
@@ -54,11 +63,64 @@ __device__ __forceinline__ void tile_coords(long long t, int m_tiles, int n_tile
     nt = within / gm;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+// ------------------------------------------------------------------ CTA-pair primitives
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the variable at shared::cta address `saddr` in the pair's CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Tile load into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of
+// the pair (here always rank 0's): .cta_group::2, no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A[smem of both CTAs] * B[smem of both CTAs], issued by one lane of rank 0.
+__device__ __forceinline__ void mma_pair_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at the same offset in both CTAs when the pair's MMAs issued so far complete.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}\n" ::"r"(
+            smem_u32(bar)),
+        "h"((unsigned short)0x3)
         : "memory");
 }
 
@@ -71,6 +133,8 @@ __device__ __forceinline__ void store_chunk(TO* dst, const float (&v)[32]) {
                           Pack2<TO>::pack(v[8 * i + 4], v[8 * i + 5]), Pack2<TO>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
 
+// Launched as clusters of 2 (blockIdx.x = 2 * pair + rank).  Warps: 0 TMA producer (both CTAs), 1 TMEM
+// allocation (both) and MMA issue (rank 0), 4-7 epilogue (both, each on its CTA's 128 token rows).
 template <typename TO>
 __global__ void __launch_bounds__(kGThreads, 1)
     qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
@@ -79,17 +143,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const long long pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
     const int n_tiles_n = p.nslots * p.C / kBN;
-    const int m_tiles = (p.M + kBM - 1) / kBM;
+    const int m_tiles = (p.M + kPairM - 1) / kPairM;
     const long long n_tiles = (long long)m_tiles * n_tiles_n;
     const int k_steps = (p.K + kBK - 1) / kBK;  // a ragged last step reads zeros past K (TMA fill)
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGSmemBar);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + kGStages;
+    uint64_t* full = bars;              // rank 0's count both CTAs' bytes of a stage
+    uint64_t* empty = bars + kGStages;  // each CTA's: its stage may be refilled
     uint64_t* acc_full = bars + 2 * kGStages;
-    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* acc_empty = acc_full + 2;  // rank 0's: both CTAs' epilogues have read the accumulator
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kGSmemSlot);
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGStages; ++s) {
@@ -98,28 +164,32 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kBM);
+            mbar_init(&acc_empty[i], 2 * kBM);
         }
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
     }
+    // both CTAs' barriers exist before either CTA's copies or MMAs can signal them
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t full0 = map_to_rank(smem_u32(full), 0);
+    const uint32_t acc_empty0 = map_to_rank(smem_u32(acc_empty), 0);
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
             tma_prefetch_desc(&tmX);
             tma_prefetch_desc(&tmW);
         }
+        const uint32_t base = smem_u32(smem);
         uint32_t it = 0;
         bool ok = true;
-        for (long long t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        for (long long t = pair; t < n_tiles && ok; t += npairs) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles_n, mt, nt);
             for (int kb = 0; kb < k_steps; ++kb) {
@@ -128,26 +198,29 @@ __global__ void __launch_bounds__(kGThreads, 1)
                                       mbar_wait(&empty[s], ((it / kGStages) & 1u) ^ 1u, ctl, kErrTimeoutKVEmpty))))
                     break;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    uint8_t* st = smem + s * kStageBytes;
-                    tma_load_2d(st, &tmX, &full[s], kb * kBK, mt * kBM);
-                    tma_load_2d(st + kABytes, &tmW, &full[s], kb * kBK, nt * kBN);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
+                    const uint32_t st = base + s * kStageBytes;
+                    tma_load_2d_pair(st, &tmX, full0 + 8u * s, kb * kBK, mt * kPairM + (int)rank * kBM);
+                    tma_load_2d_pair(st + kABytes, &tmW, full0 + 8u * s, kb * kBK, nt * kBN + (int)rank * kHalfN);
                 }
                 __syncwarp();
                 ++it;
             }
         }
-        if (!ok)
+        // Producer tail: the MMA's releases of the last stages arrive on this CTA's barriers from the pair's
+        // commits; wait for them so that nothing is still addressed to this CTA when it leaves.
+        if (ok)
             for (uint32_t k = (it > (uint32_t)kGStages ? it - kGStages : 0u); k < it; ++k)
-                mbar_wait(&full[k % kGStages], (k / kGStages) & 1u, ctl, kErrTimeoutDrain, false);
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_f16_f32acc(true, kBM, kBN, false);
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[k % kGStages], (k / kGStages) & 1u, ctl, kErrTimeoutDrain)))
+                    break;
+    } else if (warp == 1 && rank == 0) {
+        // ------------------------------------------------------------ MMA issuer (rank 0 of the pair)
+        constexpr uint32_t idesc = idesc_f16_f32acc(true, kPairM, kBN, false);
         constexpr uint32_t dhi = sw128_desc_hi(1024);
         const uint32_t base = smem_u32(smem);
         uint32_t it = 0, tc = 0;
         bool ok = true, issued = false;
-        for (long long t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++tc) {
+        for (long long t = pair; t < n_tiles && ok; t += npairs, ++tc) {
             const uint32_t ab = tc & 1u;
             if (tc >= 2 &&
                 !(ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[ab], ((tc >> 1) - 1) & 1u, ctl, kErrTimeoutO))))
@@ -163,29 +236,31 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 const uint32_t blo = sw128_desc_lo(base + s * kStageBytes + kABytes, 16);
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
-                    mma_ss(tmem + ab * kBN, desc_join(alo + ((kk * 32) >> 4), dhi), desc_join(blo + ((kk * 32) >> 4), dhi),
-                           idesc, (kb | kk) ? 1u : 0u);
-                tc_commit(&empty[s]);
+                    mma_pair_ss(tmem + ab * kBN, desc_join(alo + ((kk * 32) >> 4), dhi),
+                                desc_join(blo + ((kk * 32) >> 4), dhi), idesc, (kb | kk) ? 1u : 0u);
+                tc_commit_pair(&empty[s]);
                 issued = true;
             }
-            if (ok) tc_commit(&acc_full[ab]);
+            if (ok) tc_commit_pair(&acc_full[ab]);
         }
-        if (issued) {
-            tc_commit(&acc_full[tc & 1u]);  // a further arrival after the last tile: every MMA has retired
+        if (!ok && issued) {
+            // gave up mid-way: a further arrival once every MMA issued so far has retired
+            tc_commit_pair(&acc_full[tc & 1u]);
             mbar_wait(&acc_full[tc & 1u], (tc >> 1) & 1u, ctl, kErrTimeoutDrain, false);
         }
+        // (otherwise both epilogues have waited for the last tile's accumulator, which retires every MMA)
     } else if (warp >= 4) {
         // ------------------------------------------------------------ epilogue: bias, RMSNorm, RoPE, cast
         const int r = ((warp & 3) << 5) + lane;
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         uint32_t tc = 0;
-        for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+        for (long long t = pair; t < n_tiles; t += npairs, ++tc) {
             const uint32_t ab = tc & 1u;
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles_n, mt, nt);
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (tc >> 1) & 1u, ctl, kErrTimeoutO))) break;
             tc_fence_after();
-            const long long m = (long long)mt * kBM + r;
+            const long long m = (long long)mt * kPairM + (long long)rank * kBM + r;
             const bool valid = m < p.M;
             const int l = valid ? (int)(m % p.L) : 0, n = valid ? (int)(m / p.L) : 0;
 #pragma unroll 1
@@ -224,7 +299,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
                     tmem_ld32_sync(taddr + c * 32, xr);
                     if (hh == 1 && c == 3) {  // the whole tile has been read: the next tile's MMAs may overwrite it
                         tc_fence_before();
-                        mbar_arrive(&acc_empty[ab]);
+                        mbar_arrive_remote(acc_empty0 + 8u * ab);
                     }
                     float x[32];
 #pragma unroll
@@ -249,11 +324,18 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
     }
 
+    // After a bounded wait gave up, copies this CTA issued may still be landing: give them time before the
+    // pair's shared memory is released.  (Without an abort every copy was consumed by an MMA.)
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile unsigned*>(p.abort_flag)) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 50000ull) {
+        }
+    }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while its partner may still signal its barriers
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc_pair(tmem, 512);
     }
 }
 
@@ -369,11 +451,28 @@ cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMa
     auto kern = ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16> : qkv_gemm_kernel<__half>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemAlloc);
     if (e != cudaSuccess) return e;
-    const long long tiles = (long long)((p.M + kBM - 1) / kBM) * (p.nslots * p.C / kBN);
-    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-    if (grid <= 0) return cudaSuccess;
-    kern<<<grid, kGThreads, kGSmemAlloc, st>>>(tmX, tmW, p);
-    return cudaGetLastError();
+    const long long tiles = (long long)((p.M + kPairM - 1) / kPairM) * (p.nslots * p.C / kBN);
+    if (tiles <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = kGSmemAlloc;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // one persistent CTA pair per pair of SMs that can hold one at the same time
+    cfg.gridDim = dim3((unsigned)(2 * ((num_sms + 1) / 2)));
+    int pairs = 0;
+    e = cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (pairs <= 0) return cudaErrorInvalidConfiguration;
+    if (pairs > tiles) pairs = (int)tiles;
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    return cudaLaunchKernelEx(&cfg, kern, tmX, tmW, p);
 }
 
 }  // namespace kd

@@ -155,7 +155,12 @@ struct QkvParams {
     unsigned* abort_flag;
     unsigned long long wait_ns;
 };
-// tmX: bf16 [K, M] with a {64, 128} box; tmW: bf16 [K, nslots*C] with a {64, 256} box; both 128-byte swizzled.
+// Rows of one TMA box of each GEMM operand: each CTA of a pair stages 128 token rows of A and 128 feature
+// rows of B per K step (the kernel's shared-memory slots are sized from these).
+constexpr int kGemmBoxRowsA = 128;
+constexpr int kGemmBoxRowsB = 128;
+// tmX: bf16 [K, M] with a {64, kGemmBoxRowsA} box; tmW: bf16 [K, nslots*C] with a {64, kGemmBoxRowsB} box;
+// both 128-byte swizzled.
 cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
                             cudaStream_t st);
 // ggml weight rows [rows][row_bytes] of type f32 (0), f16 (1), q4_0 (2), q8_0 (8), bf16 (30) -> bf16 rows
