@@ -1022,24 +1022,26 @@ int64_t weight_row_bytes(int32_t type, int64_t K) {
     }
 }
 
-// bf16 [inner, rows] with a {64, box_rows} box, 128-byte swizzle, zero fill past the ends.
-kd_attn_status make_gemm_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, int64_t inner, int64_t rows,
+// bf16 rows [rows][Kp] (Kp a multiple of kGemmKChunk) viewed as {64, rows, Kp/64}: a {64, box_rows,
+// kGemmBoxChunks} box brings kGemmBoxChunks 64-wide K slices of box_rows rows, 128-byte swizzled; rows past
+// the end read as zeros.
+kd_attn_status make_gemm_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, int64_t Kp, int64_t rows,
                              uint32_t box_rows) {
     PFN_encodeTiled_t enc = get_encode();
     if (!enc) return fail(ctx, KD_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(data), dims, strides, box, estr,
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(Kp / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)Kp * 2, 128};
+    cuuint32_t box[3] = {64, box_rows, (cuuint32_t)kGemmBoxChunks};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(data), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled rejected a GEMM operand (%d)", (int)r);
     return KD_ATTN_OK;
 }
 
-// Launch sequence: each given weight expanded to bf16 rows of one B operand [K, nslots*C]; x rounded to
-// bf16 token rows [K, L*N]; the RoPE (cos, sin) table when rotating; then the persistent GEMM whose
+// Launch sequence: each given weight expanded to bf16 rows of one B operand [Kp, nslots*C]; x rounded to
+// bf16 token rows [Kp, L*N] (Kp: K rounded up to the GEMM's K step, zero-padded); the RoPE (cos, sin) table when rotating; then the persistent GEMM whose
 // epilogue writes the operands.  Scratch: [B operand][A operand][RoPE table].
 kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* const w[3],
                                    const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
@@ -1095,6 +1097,7 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         packed_strides(&o, onb);
         if (!aligned16(o.data) || !strides16(onb))
             return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "output rows must be 16-byte aligned");
+        if (!aligned16(W.bias)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "bias must be 16-byte aligned");
         QkvSlot& S = p.slot[p.nslots];
         S.out = o.data;
         S.o_nb1 = (long long)onb[1];
@@ -1107,6 +1110,8 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         slot_of[i] = p.nslots++;
     }
     if (p.nslots == 0) return KD_ATTN_OK;
+    if (!aligned16(q_gain) || !aligned16(k_gain))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "q_gain / k_gain must be 16-byte aligned");
     if (C > (1 << 20)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features beyond 2^20");
     p.C = (int)C;
     RopeTab tab{};
@@ -1114,8 +1119,9 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
     if (rot && (rc = fill_rope(ctx, rope, L, &tab))) return rc;
     if (p.M == 0) return KD_ATTN_OK;
 
-    const size_t b_bytes = align256((size_t)p.nslots * C * K * 2);
-    const size_t a_bytes = align256((size_t)p.M * K * 2);
+    const int64_t Kp = (K + kGemmKChunk - 1) / kGemmKChunk * kGemmKChunk;  // rows zero-padded to whole K steps
+    const size_t b_bytes = align256((size_t)p.nslots * C * Kp * 2);
+    const size_t a_bytes = align256((size_t)p.M * Kp * 2);
     const size_t cs_bytes = rot ? align256((size_t)L * 64 * sizeof(float2)) : 0;
     if ((rc = ensure_scratch(ctx, b_bytes + a_bytes + cs_bytes, st))) return rc;
     char* scr = static_cast<char*>(ctx->scratch);
@@ -1123,9 +1129,9 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
     __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(scr + b_bytes);
     for (int i = 0; i < 3; ++i)
         if (slot_of[i] >= 0)
-            KD_CUDA(ctx, launch_expand_weights(w[i]->data, w[i]->type, (long long)w[i]->nb1, (int)K, (int)C,
+            KD_CUDA(ctx, launch_expand_weights(w[i]->data, w[i]->type, (long long)w[i]->nb1, (int)K, (int)Kp, (int)C,
                                                slot_of[i] * (int)C, wb, ctx->num_sms, st));
-    KD_CUDA(ctx, launch_to_bf16_rows(x->data, (long long)xnb[1], (long long)xnb[2], (int)K, (int)L, p.M, xb,
+    KD_CUDA(ctx, launch_to_bf16_rows(x->data, (long long)xnb[1], (long long)xnb[2], (int)K, (int)Kp, (int)L, p.M, xb,
                                      ctx->num_sms, st));
     if (rot) {
         float2* cs = reinterpret_cast<float2*>(scr + b_bytes + a_bytes);
@@ -1133,8 +1139,8 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         p.rope_cs = cs;
     }
     CUtensorMap tmX, tmW;
-    if ((rc = make_gemm_map(ctx, &tmX, xb, K, p.M, kGemmBoxRowsA)) ||
-        (rc = make_gemm_map(ctx, &tmW, wb, K, (int64_t)p.nslots * C, kGemmBoxRowsB)))
+    if ((rc = make_gemm_map(ctx, &tmX, xb, Kp, p.M, kGemmBoxRowsA)) ||
+        (rc = make_gemm_map(ctx, &tmW, wb, Kp, (int64_t)p.nslots * C, kGemmBoxRowsB)))
         return rc;
     p.err = ctx->d_words;
     p.abort_flag = ctx->d_words + 1;

@@ -159,16 +159,22 @@ struct QkvParams {
 // rows of B per K step (the kernel's shared-memory slots are sized from these).
 constexpr int kGemmBoxRowsA = 128;
 constexpr int kGemmBoxRowsB = 128;
-// tmX: bf16 [K, M] with a {64, kGemmBoxRowsA} box; tmW: bf16 [K, nslots*C] with a {64, kGemmBoxRowsB} box;
-// both 128-byte swizzled.
+// K per stage, and the 64-wide K slices one TMA copy brings; the operands' rows are zero-padded to a
+// multiple of kGemmKChunk (Kp).
+constexpr int kGemmBoxChunks = 2;
+constexpr int kGemmKChunk = 64 * kGemmBoxChunks;
+// tmX: bf16 [Kp, M] viewed as {64, M, Kp/64} with a {64, kGemmBoxRowsA, kGemmBoxChunks} box; tmW: bf16
+// [Kp, nslots*C] viewed as {64, nslots*C, Kp/64} with a {64, kGemmBoxRowsB, kGemmBoxChunks} box; both
+// 128-byte swizzled.
 cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
                             cudaStream_t st);
 // ggml weight rows [rows][row_bytes] of type f32 (0), f16 (1), q4_0 (2), q8_0 (8), bf16 (30) -> bf16 rows
-// row0 .. row0+rows-1 of dst [*, K]; K a multiple of 32.
-cudaError_t launch_expand_weights(const void* w, int type, long long row_bytes, int K, int rows, int row0,
+// row0 .. row0+rows-1 of dst [*, Kp], columns K .. Kp-1 zero; K and Kp multiples of 32.
+cudaError_t launch_expand_weights(const void* w, int type, long long row_bytes, int K, int Kp, int rows, int row0,
                                   __nv_bfloat16* dst, int num_sms, cudaStream_t st);
-// f32 x [K, L, N] (byte strides nb1, nb2; K a multiple of 8, rows 16-byte aligned) -> bf16 [M = L*N][K].
-cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int K, int L, long long M,
+// f32 x [K, L, N] (byte strides nb1, nb2; K a multiple of 32, rows 16-byte aligned) -> bf16 [M = L*N][Kp],
+// columns K .. Kp-1 zero.
+cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int K, int Kp, int L, long long M,
                                 __nv_bfloat16* dst, int num_sms, cudaStream_t st);
 // (cos, sin) of every token and rotary pair of the 3D RoPE table: cs[l * 64 + i].
 cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms, cudaStream_t st);
