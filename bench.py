@@ -427,7 +427,61 @@ def extra_measurements(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
         "ms_q_already_f16": ms_f16q, "q_rounding_ms": ms_f32q - ms_f16q,
         "q_rounding_share": (ms_f32q - ms_f16q) / ms_f32q}
     del qf, q16, k16, v16, of
+    res["projection_attention"] = projection_attention(args, ctx, kd_attn, torch, q, rope, dev, stream)
     return res
+
+
+def _q8_0_weight(torch, rows, cols, seed, dev):
+    """Synthetic q8_0 Linear weight [cols, rows] (ggml ne): rows of 34-byte blocks, f16 scale 1/(127*64), int8
+    values uniform in [-127, 127] -- a valid block stream of the converter's format."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    raw = torch.empty(rows, cols // 32, 34, dtype=torch.uint8, device=dev)
+    qv = torch.randint(-127, 128, (rows, cols // 32, 32), device=dev, dtype=torch.int16, generator=g).to(torch.int8)
+    raw[..., :2] = torch.full((rows, cols // 32, 1), 1.0 / (127 * 64), dtype=torch.float16,
+                              device=dev).view(torch.uint8)
+    raw[..., 2:] = qv.view(torch.uint8)
+    return raw.view(rows, -1)
+
+
+def projection_attention(args, ctx, kd_attn, torch, x, rope, dev, stream):
+    """Config 1's self-attention block from the hidden states: to_query/to_key/to_value with q8_0 weights and
+    f32 biases (crossdit.hpp:123-125) fused with RMSNorm + RoPE + cast (kd_attn_qkv_projection), then the flash
+    kernel on its bf16 operands.  x is the config-1 synthetic N(0,1) tensor [4096, L, N].  A plain cuBLAS bf16
+    GEMM of the same shape (bf16 out, no epilogue work) is timed beside it as the library reference."""
+    N, L, K = x.shape
+    H, d = K // 128, 128
+    C = H * d
+    ws = [_q8_0_weight(torch, C, K, 11 + i, dev) for i in range(3)]
+    bias = [torch.randn(C, device=dev) * 0.1 for _ in range(3)]
+    lin = [kd_attn.KdLinear.of(ws[i], kd_attn.Q8_0, K, C, bias[i]) for i in range(3)]
+    outs = [torch.empty(N, H, L, d, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    o = torch.empty(N, L, H, d, device=dev, dtype=torch.bfloat16)
+    proj = lambda: ctx.qkv_projection(x, *lin, *outs, rope=rope, stream=stream)
+    attn = lambda: ctx.flash_attn_ext(*outs, o, stream=stream)
+    ms_proj = _timed(torch, stream, proj, args.steps, args.warmup)
+    ms_attn = _timed(torch, stream, attn, args.steps, args.warmup)
+    ms_both = _timed(torch, stream, lambda: (proj(), attn()), args.steps, args.warmup)
+    ctx.device_status()
+    del outs, o, ws, bias, lin
+    xb = x.reshape(-1, K).to(torch.bfloat16)
+    wb = torch.randn(3 * C, K, device=dev, dtype=torch.bfloat16)
+    with torch.cuda.stream(stream):
+        ms_lib = _timed(torch, stream, lambda: torch.matmul(xb, wb.t()), args.steps, args.warmup)
+    del xb, wb
+    pk, _, pk_kind = peaks()
+    proj_flop = 2.0 * N * L * K * 3 * C
+    attn_flop = 4.0 * N * H * L * L * d
+    return {
+        "workload": "config 1 block: x [4096, 31744, 2] f32 -> q8_0 QKV projection + bias + RMSNorm + RoPE -> "
+                    "bf16 operands -> flash attention",
+        "projection_ms": ms_proj, "projection_tflops": proj_flop / (ms_proj * 1e-3) / 1e12,
+        "projection_frac_of_bf16_burst": proj_flop / (ms_proj * 1e-3) / 1e12 / pk, "peak_kind": pk_kind,
+        "attention_ms": ms_attn, "block_ms": ms_both,
+        "block_tflops": (proj_flop + attn_flop) / (ms_both * 1e-3) / 1e12,
+        "f32_projection_bytes_avoided": 2 * 3 * N * L * C * 4,
+        "library_gemm_ms": ms_lib,
+        "library_gemm": "torch.matmul bf16 [2L, 4096] x [4096, 12288] (cuBLAS), bf16 out, no bias/norm/RoPE",
+        "projection_call_includes": "q8_0 -> bf16 weight expansion, x f32 -> bf16, RoPE table, fused GEMM"}
 
 
 def hbm_peak():
