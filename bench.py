@@ -401,6 +401,12 @@ def extra_measurements(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
           already f16, whose difference is the Q-rounding kernel's share."""
     res = {}
     cfg2 = dict(CONFIGS[2])
+    if args.batch:  # profiling overrides shape config 1's Q, which config 2 reuses
+        cfg2["N"] = args.batch
+    if args.heads:
+        cfg2["H"] = args.heads
+    if args.frames:
+        cfg2["grid"] = (args.frames,) + tuple(cfg2["grid"][1:])
     r2 = run_other(args, cfg2, ctx, kd_attn, torch, q, None, None, rope, kd_attn.BF16, torch.bfloat16, stream)
     res["cfg2"] = {"workload": cfg2["name"], "kv_len": r2["config"]["kv_len"], "call_ms": r2["ms_per_step"],
                    "flash_kernel_ms": r2["flash_kernel"]["ms"], "flash_kernel_gbs": r2["flash_kernel"]["gbs"],
