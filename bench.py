@@ -467,8 +467,14 @@ def projection_attention(args, ctx, kd_attn, torch, x, rope, dev, stream):
     ms_proj = _timed(torch, stream, proj, args.steps, args.warmup)
     ms_attn = _timed(torch, stream, attn, args.steps, args.warmup)
     ms_both = _timed(torch, stream, lambda: (proj(), attn()), args.steps, args.warmup)
+    # the whole DiTSelfAttention::forward through one call: projection, attention, q8_0 out-projection
+    wo = _q8_0_weight(torch, C, C, 14, dev)
+    lin_o = kd_attn.KdLinear.of(wo, kd_attn.Q8_0, C, C, torch.randn(C, device=dev) * 0.1)
+    y = torch.empty(N, L, C, device=dev)
+    ms_block = _timed(torch, stream, lambda: ctx.self_attention_block(x, *lin, lin_o, y, rope=rope, stream=stream),
+                      args.steps, args.warmup)
     ctx.device_status()
-    del outs, o, ws, bias, lin
+    del outs, o, ws, bias, lin, wo, lin_o, y
     xb = x.reshape(-1, K).to(torch.bfloat16)
     wb = torch.randn(3 * C, K, device=dev, dtype=torch.bfloat16)
     with torch.cuda.stream(stream):
@@ -485,6 +491,10 @@ def projection_attention(args, ctx, kd_attn, torch, x, rope, dev, stream):
         "attention_ms": ms_attn, "block_ms": ms_both,
         "block_tflops": (proj_flop + attn_flop) / (ms_both * 1e-3) / 1e12,
         "f32_projection_bytes_avoided": 2 * 3 * N * L * C * 4,
+        "self_attention_block_ms": ms_block,
+        "self_attention_block": "kd_attn_self_attention_block: x f32 -> QKV projection -> flash -> q8_0 "
+                                "out-projection -> y f32 [4096, L, N] (crossdit.hpp:117-154)",
+        "self_attention_block_tflops": (proj_flop * 4 / 3 + attn_flop) / (ms_block * 1e-3) / 1e12,
         "library_gemm_ms": ms_lib,
         "library_gemm": "torch.matmul bf16 [2L, 4096] x [4096, 12288] (cuBLAS), bf16 out, no bias/norm/RoPE",
         "projection_call_includes": "q8_0 -> bf16 weight expansion, x f32 -> bf16, RoPE table, fused GEMM"}

@@ -204,6 +204,24 @@ kd_attn_status kd_attn_qkv_projection(kd_attn_ctx* ctx, const kd_tensor* x, cons
                                       const float* k_gain, float eps, const kd_rope3d* rope, int32_t out_dtype,
                                       kd_tensor* q_out, kd_tensor* k_out, kd_tensor* v_out, void* stream);
 
+/* Replaces ops::linear (ops.hpp:27-42): y = x W^T + b, the same GEMM as the projection with a plain
+ * bias epilogue -- the out-projection of the attention blocks (crossdit.hpp:153).
+ * x : [K, L, N] f32 (rounded to bf16 rows inside the call) or bf16 (read in place: K a multiple of
+ *     128, rows evenly spaced and 16-byte aligned)
+ * w : [K, C] (C a multiple of 256), types as for kd_attn_qkv_projection
+ * y : [C, L, N] f32, bf16 or f16, rows contiguous and 16-byte aligned */
+kd_attn_status kd_attn_linear(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* w, kd_tensor* y, void* stream);
+
+/* Replaces DiTSelfAttention::forward (crossdit.hpp:117-154) from the hidden states to the block output:
+ * kd_attn_qkv_projection (bf16 operands), the flash kernel (scale 1/sqrt(128), no mask) and the
+ * out-projection, with the intermediate tensors in the context's scratch.
+ * x : [C, L, N] f32; wq/wk/wv : [C, C]; wo : [C, C_out]; q_gain/k_gain : RMSNorm weights (NULL = unit);
+ * rope : NULL = no rotation; y : [C_out, L, N] f32 (or bf16/f16).  C = n_head * 128. */
+kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                            const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                            const float* q_gain, const float* k_gain, float eps,
+                                            const kd_rope3d* rope, kd_tensor* y, void* stream);
+
 /* ---------------------------------------------------------------------------
  * ggml_flash_attn_ext semantics (called at ops.hpp:176):
  *   out[:, h, i, n] = softmax_j(scale * q[:, i, h, n] . k[:, j, hk, nk] + mask[j, i, h%mh, n%mn]) v[:, j, hk, nk]

@@ -1022,15 +1022,15 @@ int64_t weight_row_bytes(int32_t type, int64_t K) {
     }
 }
 
-// bf16 rows [rows][Kp] (Kp a multiple of kGemmKChunk) viewed as {64, rows, Kp/64}: a {64, box_rows,
-// kGemmBoxChunks} box brings kGemmBoxChunks 64-wide K slices of box_rows rows, 128-byte swizzled; rows past
-// the end read as zeros.
+// bf16 rows [rows] of Kp elements (Kp a multiple of kGemmKChunk), row_bytes apart, viewed as {64, rows, Kp/64}:
+// a {64, box_rows, kGemmBoxChunks} box brings kGemmBoxChunks 64-wide K slices of box_rows rows, 128-byte
+// swizzled; rows past the end read as zeros.
 kd_attn_status make_gemm_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* data, int64_t Kp, int64_t rows,
-                             uint32_t box_rows) {
+                             uint32_t box_rows, uint64_t row_bytes) {
     PFN_encodeTiled_t enc = get_encode();
     if (!enc) return fail(ctx, KD_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(Kp / 64)};
-    cuuint64_t strides[2] = {(cuuint64_t)Kp * 2, 128};
+    cuuint64_t strides[2] = {(cuuint64_t)row_bytes, 128};
     cuuint32_t box[3] = {64, box_rows, (cuuint32_t)kGemmBoxChunks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(data), dims, strides, box, estr,
@@ -1040,34 +1040,127 @@ kd_attn_status make_gemm_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* dat
     return KD_ATTN_OK;
 }
 
-// Launch sequence: each given weight expanded to bf16 rows of one B operand [Kp, nslots*C]; x rounded to
-// bf16 token rows [Kp, L*N] (Kp: K rounded up to the GEMM's K step, zero-padded); the RoPE (cos, sin) table when rotating; then the persistent GEMM whose
-// epilogue writes the operands.  Scratch: [B operand][A operand][RoPE table].
-kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* const w[3],
-                                   const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
-                                   int32_t out_dtype, kd_tensor* const outs[3], cudaStream_t st) {
+// The GEMM's A operand: x [K, L, N] as M = L*N token rows.  f32 x is rounded into bf16 scratch rows of
+// Kp elements; bf16 x whose K is a whole number of K steps and whose rows are evenly spaced and 16-byte
+// aligned is read in place.
+struct GemmInput {
+    const kd_tensor* x = nullptr;
+    int64_t K = 0, L = 0, N = 0, Kp = 0;
+    uint64_t nb[4] = {};
+    bool direct = false;  // bf16 rows read in place
+};
+
+kd_attn_status gemm_input(kd_attn_ctx* ctx, const kd_tensor* x, GemmInput* in) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, x, "x"))) return rc;
-    if (x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x must be f32");
     if (x->ne[3] != 1) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x must be [K, L, N] (ne[3] == 1)");
+    in->x = x;
+    in->K = x->ne[0];
+    in->L = x->ne[1];
+    in->N = x->ne[2];
+    if (in->K <= 0 || in->K % 32)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "in_features %lld is not a positive multiple of 32", (long long)in->K);
+    if (in->L * in->N > INT32_MAX - 256) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than 2^31 tokens");
+    in->Kp = (in->K + kGemmKChunk - 1) / kGemmKChunk * kGemmKChunk;  // rows zero-padded to whole K steps
+    packed_strides(x, in->nb);
+    if (!aligned16(x->data) || in->nb[1] % 16 || in->nb[2] % 16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x rows must be 16-byte aligned");
+    if (x->type == KD_ATTN_TYPE_BF16) {
+        if (in->Kp != in->K || in->nb[2] != in->nb[1] * (uint64_t)in->L)
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED,
+                        "bf16 x is read in place: K must be a multiple of %d and the sequences evenly spaced rows",
+                        kGemmKChunk);
+        in->direct = true;
+    } else if (x->type != KD_ATTN_TYPE_F32) {
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x must be f32 or bf16");
+    }
+    return KD_ATTN_OK;
+}
+
+// Checks one ggml Linear weight [K, C] (C a multiple of 256).
+kd_attn_status check_weight(kd_attn_ctx* ctx, const kd_linear& W, int64_t K) {
+    const int64_t rb = weight_row_bytes(W.type, K);
+    if (rb < 0) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "weight type %d is not f32/f16/bf16/q4_0/q8_0", W.type);
+    if (W.ne[0] != K)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight ne[0] %lld != in_features %lld", (long long)W.ne[0],
+                    (long long)K);
+    if (W.ne[1] <= 0 || W.ne[1] % 256 || W.ne[1] > (1 << 20))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features %lld is not a multiple of 256 up to 2^20",
+                    (long long)W.ne[1]);
+    if ((int64_t)W.nb1 < rb) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight nb1 smaller than a row");
+    if (!W.data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight data is NULL");
+    if ((W.type == KD_ATTN_TYPE_F32 || W.type == KD_ATTN_TYPE_F16 || W.type == KD_ATTN_TYPE_BF16) &&
+        (!aligned16(W.data) || W.nb1 % 16))
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "f32/f16/bf16 weight rows must be 16-byte aligned");
+    if (!aligned16(W.bias)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "bias must be 16-byte aligned");
+    return KD_ATTN_OK;
+}
+
+// Scratch of one GEMM call: [B operand][A operand rows unless read in place][RoPE table].
+size_t gemm_work_bytes(const GemmInput& in, int nslots, int64_t C, bool rot) {
+    return align256((size_t)nslots * C * in.Kp * 2) + (in.direct ? 0 : align256((size_t)in.L * in.N * in.Kp * 2)) +
+           (rot ? align256((size_t)in.L * 64 * sizeof(float2)) : 0);
+}
+
+// Launch sequence of one GEMM: each weight w[i] expanded to bf16 rows of the B operand (slot i = rows
+// [i*C, (i+1)*C)); x rounded to bf16 token rows unless read in place; the RoPE (cos, sin) table when a slot
+// rotates; then the persistent GEMM whose epilogue writes every slot's output.  `work` holds
+// gemm_work_bytes(in, p.nslots, p.C, tab != nullptr) bytes.
+kd_attn_status gemm_run(kd_attn_ctx* ctx, const GemmInput& in, const kd_linear* const* w, QkvParams& p,
+                        const RopeTab* tab, int32_t out_dtype, char* work, cudaStream_t st) {
+    kd_attn_status rc;
+    const int64_t C = p.C, Kp = in.Kp;
+    p.K = (int)in.K;
+    p.L = (int)in.L;
+    p.M = (int)(in.L * in.N);
+    if (p.M == 0) return KD_ATTN_OK;
+    const size_t b_bytes = align256((size_t)p.nslots * C * Kp * 2);
+    const size_t a_bytes = in.direct ? 0 : align256((size_t)p.M * Kp * 2);
+    __nv_bfloat16* wb = reinterpret_cast<__nv_bfloat16*>(work);
+    for (int i = 0; i < p.nslots; ++i)
+        KD_CUDA(ctx, launch_expand_weights(w[i]->data, w[i]->type, (long long)w[i]->nb1, (int)in.K, (int)Kp, (int)C,
+                                           i * (int)C, wb, ctx->num_sms, st));
+    const void* xa = in.x->data;
+    uint64_t xrow = in.nb[1];
+    if (!in.direct) {
+        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(work + b_bytes);
+        KD_CUDA(ctx, launch_to_bf16_rows(in.x->data, (long long)in.nb[1], (long long)in.nb[2], (int)in.K, (int)Kp,
+                                         (int)in.L, p.M, xb, ctx->num_sms, st));
+        xa = xb;
+        xrow = (uint64_t)Kp * 2;
+    }
+    if (tab) {
+        float2* cs = reinterpret_cast<float2*>(work + b_bytes + a_bytes);
+        KD_CUDA(ctx, launch_rope_table(*tab, (int)in.L, cs, ctx->num_sms, st));
+        p.rope_cs = cs;
+    }
+    CUtensorMap tmX, tmW;
+    if ((rc = make_gemm_map(ctx, &tmX, xa, Kp, p.M, kGemmBoxRowsA, xrow)) ||
+        (rc = make_gemm_map(ctx, &tmW, wb, Kp, (int64_t)p.nslots * C, kGemmBoxRowsB, (uint64_t)Kp * 2)))
+        return rc;
+    p.err = ctx->d_words;
+    p.abort_flag = ctx->d_words + 1;
+    p.wait_ns = ctx->wait_ns;
+    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, sizeof(unsigned), st));
+    KD_CUDA(ctx, launch_qkv_gemm(out_type_of(out_dtype), tmX, tmW, p, ctx->num_sms, st));
+    return KD_ATTN_OK;
+}
+
+// to_query/to_key/to_value + prologue (see kd_attn_qkv_projection).  `work` = NULL: the context's scratch.
+kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* const w[3],
+                                   const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
+                                   int32_t out_dtype, kd_tensor* const outs[3], cudaStream_t st, char* work = nullptr) {
+    kd_attn_status rc;
+    GemmInput in;
+    if ((rc = gemm_input(ctx, x, &in))) return rc;
+    if (in.x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x must be f32");
     if (out_dtype != KD_ATTN_TYPE_F16 && out_dtype != KD_ATTN_TYPE_BF16)
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "the projection writes f16 or bf16 operands");
-    const int64_t K = x->ne[0], L = x->ne[1], N = x->ne[2];
-    if (K <= 0 || K % 32)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "in_features %lld is not a positive multiple of 32", (long long)K);
-    uint64_t xnb[4];
-    packed_strides(x, xnb);
-    if (!aligned16(x->data) || xnb[1] % 16 || xnb[2] % 16)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x rows must be 16-byte aligned");
-    if (L * N > INT32_MAX - 128) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "more than 2^31 tokens");
-
+    const int64_t K = in.K, L = in.L, N = in.N;
     QkvParams p{};
-    p.K = (int)K;
-    p.L = (int)L;
-    p.M = (int)(L * N);
     p.eps = eps;
     int64_t C = -1;
-    int slot_of[3] = {-1, -1, -1};
+    const kd_linear* ws[3] = {};
     for (int i = 0; i < 3; ++i) {
         if (!w[i] && !outs[i]) continue;
         if (!w[i] || !outs[i]) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "a weight and its output must both be given");
@@ -1075,29 +1168,15 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         const kd_tensor& o = *outs[i];
         if ((rc = check_tensor(ctx, &o, "projection output"))) return rc;
         if (o.type != out_dtype) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must have type out_dtype");
-        const int64_t rb = weight_row_bytes(W.type, K);
-        if (rb < 0) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "weight type %d is not f32/f16/bf16/q4_0/q8_0", W.type);
-        if (W.ne[0] != K) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight ne[0] %lld != in_features %lld",
-                                      (long long)W.ne[0], (long long)K);
-        if (W.ne[1] <= 0 || W.ne[1] % 256)
-            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features %lld is not a positive multiple of 256",
-                        (long long)W.ne[1]);
+        if ((rc = check_weight(ctx, W, K))) return rc;
         if (C >= 0 && W.ne[1] != C) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the weights disagree on out_features");
         C = W.ne[1];
-        if ((int64_t)W.nb1 < rb) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight nb1 smaller than a row");
-        if (!W.data) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "weight data is NULL");
-        if ((W.type == KD_ATTN_TYPE_F32 || W.type == KD_ATTN_TYPE_F16 || W.type == KD_ATTN_TYPE_BF16) &&
-            (!aligned16(W.data) || W.nb1 % 16))
-            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "f32/f16/bf16 weight rows must be 16-byte aligned");
-        if (W.type == KD_ATTN_TYPE_F32 && ((reinterpret_cast<uintptr_t>(W.data) | W.nb1) & 3))
-            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "f32 weight rows must be 4-byte aligned");
         if (o.ne[0] != kHeadDim || o.ne[1] != L || o.ne[2] * kHeadDim != C || o.ne[3] != N)
             return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must be [128, L, C/128, N]");
         uint64_t onb[4];
         packed_strides(&o, onb);
         if (!aligned16(o.data) || !strides16(onb))
             return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "output rows must be 16-byte aligned");
-        if (!aligned16(W.bias)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "bias must be 16-byte aligned");
         QkvSlot& S = p.slot[p.nslots];
         S.out = o.data;
         S.o_nb1 = (long long)onb[1];
@@ -1107,47 +1186,105 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         S.norm = i < 2;
         S.gain = i == 0 ? q_gain : (i == 1 ? k_gain : nullptr);
         S.rope = (i < 2 && rope) ? 1 : 0;
-        slot_of[i] = p.nslots++;
+        ws[p.nslots++] = w[i];
     }
     if (p.nslots == 0) return KD_ATTN_OK;
     if (!aligned16(q_gain) || !aligned16(k_gain))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "q_gain / k_gain must be 16-byte aligned");
-    if (C > (1 << 20)) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_features beyond 2^20");
     p.C = (int)C;
     RopeTab tab{};
     const bool rot = rope && (p.slot[0].rope || (p.nslots > 1 && p.slot[1].rope));
     if (rot && (rc = fill_rope(ctx, rope, L, &tab))) return rc;
-    if (p.M == 0) return KD_ATTN_OK;
-
-    const int64_t Kp = (K + kGemmKChunk - 1) / kGemmKChunk * kGemmKChunk;  // rows zero-padded to whole K steps
-    const size_t b_bytes = align256((size_t)p.nslots * C * Kp * 2);
-    const size_t a_bytes = align256((size_t)p.M * Kp * 2);
-    const size_t cs_bytes = rot ? align256((size_t)L * 64 * sizeof(float2)) : 0;
-    if ((rc = ensure_scratch(ctx, b_bytes + a_bytes + cs_bytes, st))) return rc;
-    char* scr = static_cast<char*>(ctx->scratch);
-    __nv_bfloat16* wb = reinterpret_cast<__nv_bfloat16*>(scr);
-    __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(scr + b_bytes);
-    for (int i = 0; i < 3; ++i)
-        if (slot_of[i] >= 0)
-            KD_CUDA(ctx, launch_expand_weights(w[i]->data, w[i]->type, (long long)w[i]->nb1, (int)K, (int)Kp, (int)C,
-                                               slot_of[i] * (int)C, wb, ctx->num_sms, st));
-    KD_CUDA(ctx, launch_to_bf16_rows(x->data, (long long)xnb[1], (long long)xnb[2], (int)K, (int)Kp, (int)L, p.M, xb,
-                                     ctx->num_sms, st));
-    if (rot) {
-        float2* cs = reinterpret_cast<float2*>(scr + b_bytes + a_bytes);
-        KD_CUDA(ctx, launch_rope_table(tab, (int)L, cs, ctx->num_sms, st));
-        p.rope_cs = cs;
+    if (L * N == 0) return KD_ATTN_OK;
+    if (!work) {
+        if ((rc = ensure_scratch(ctx, gemm_work_bytes(in, p.nslots, C, rot), st))) return rc;
+        work = static_cast<char*>(ctx->scratch);
     }
-    CUtensorMap tmX, tmW;
-    if ((rc = make_gemm_map(ctx, &tmX, xb, Kp, p.M, kGemmBoxRowsA)) ||
-        (rc = make_gemm_map(ctx, &tmW, wb, Kp, (int64_t)p.nslots * C, kGemmBoxRowsB)))
-        return rc;
-    p.err = ctx->d_words;
-    p.abort_flag = ctx->d_words + 1;
-    p.wait_ns = ctx->wait_ns;
-    KD_CUDA(ctx, cudaMemsetAsync(ctx->d_words + 1, 0, sizeof(unsigned), st));
-    KD_CUDA(ctx, launch_qkv_gemm(out_type_of(out_dtype), tmX, tmW, p, ctx->num_sms, st));
-    return KD_ATTN_OK;
+    return gemm_run(ctx, in, ws, p, rot ? &tab : nullptr, out_dtype, work, st);
+}
+
+// ops::linear (ops.hpp:27-42): y = x W^T + b.  x [K, L, N] f32 or bf16, y [C, L, N] f32 / bf16 / f16 with
+// contiguous, 16-byte-aligned rows.  `work` = NULL: the context's scratch.
+kd_attn_status linear_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* w, kd_tensor* y, cudaStream_t st,
+                           char* work = nullptr) {
+    kd_attn_status rc;
+    GemmInput in;
+    if ((rc = gemm_input(ctx, x, &in))) return rc;
+    if (!w) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "w is NULL");
+    if ((rc = check_weight(ctx, *w, in.K))) return rc;
+    if ((rc = check_tensor(ctx, y, "y"))) return rc;
+    const int64_t C = w->ne[1];
+    if (y->ne[0] != C || y->ne[1] != in.L || y->ne[2] != in.N || y->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "y must be [out_features, L, N]");
+    uint64_t ynb[4];
+    packed_strides(y, ynb);
+    if (!aligned16(y->data) || ynb[1] % 16 || ynb[2] % 16)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "y rows must be 16-byte aligned");
+    QkvParams p{};
+    p.nslots = 1;
+    p.C = (int)C;
+    QkvSlot& S = p.slot[0];
+    // a row-major [C, L, N] output in the epilogue's (row, 128-column group, sequence) addressing
+    S.out = y->data;
+    S.o_nb1 = (long long)ynb[1];
+    S.o_nb2 = (long long)(kHeadDim * elt_size(y->type));
+    S.o_nb3 = (long long)ynb[2];
+    S.bias = w->bias;
+    if (in.L * in.N == 0) return KD_ATTN_OK;
+    if (!work) {
+        if ((rc = ensure_scratch(ctx, gemm_work_bytes(in, 1, C, false), st))) return rc;
+        work = static_cast<char*>(ctx->scratch);
+    }
+    const kd_linear* ws[1] = {w};
+    return gemm_run(ctx, in, ws, p, nullptr, y->type, work, st);
+}
+
+// DiTSelfAttention::forward (crossdit.hpp:117-154) from the hidden states: fused QKV projection, flash
+// attention, out-projection.  Scratch: [Q][K][V operands][attention output][GEMM work, shared by both GEMMs].
+kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                         const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                         const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
+                                         kd_tensor* y, cudaStream_t st) {
+    kd_attn_status rc;
+    GemmInput in;
+    if ((rc = gemm_input(ctx, x, &in))) return rc;
+    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    const int64_t C = wq->ne[1], L = in.L, N = in.N;
+    if (C % kHeadDim || wk->ne[1] != C || wv->ne[1] != C || wo->ne[0] != C)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the projections must map to n_head * 128 features and back");
+    const int32_t H = (int32_t)(C / kHeadDim);
+    const int32_t op = KD_ATTN_TYPE_BF16;
+    const size_t opb = align256((size_t)N * H * L * kHeadDim * 2);
+    const bool rot = rope != nullptr;
+    GemmInput attn_in = in;  // the out-projection reads the attention output [C, L, N] bf16 in place
+    attn_in.K = attn_in.Kp = C;
+    attn_in.direct = true;
+    const size_t work = std::max(gemm_work_bytes(in, 3, C, rot), gemm_work_bytes(attn_in, 1, wo->ne[1], false));
+    if ((rc = ensure_scratch(ctx, 4 * opb + work, st))) return rc;
+    char* base = static_cast<char*>(ctx->scratch);
+    kd_tensor Qs = operand_view(base, op, L, H, N);
+    kd_tensor Ks = operand_view(base + opb, op, L, H, N);
+    kd_tensor Vs = operand_view(base + 2 * opb, op, L, H, N);
+    kd_tensor A{};  // attention output [C, L, N] bf16 = the flash dst [128, H, L, N]
+    A.data = base + 3 * opb;
+    A.type = op;
+    A.ne[0] = C;
+    A.ne[1] = L;
+    A.ne[2] = N;
+    A.ne[3] = 1;
+    A.nb[0] = 2;
+    A.nb[1] = 2 * (size_t)C;
+    A.nb[2] = A.nb[1] * (size_t)L;
+    A.nb[3] = A.nb[2] * (size_t)N;
+    char* gw = base + 4 * opb;
+    const kd_linear* w3[3] = {wq, wk, wv};
+    kd_tensor* o3[3] = {&Qs, &Ks, &Vs};
+    if ((rc = qkv_projection_core(ctx, x, w3, q_gain, k_gain, eps, rope, op, o3, st, gw))) return rc;
+    kd_tensor ov;
+    if ((rc = out_view(ctx, &A, H, L, N, &ov))) return rc;
+    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)kHeadDim), nullptr, &ov, nullptr};
+    if ((rc = flash_run(ctx, fa, st))) return rc;  // bf16 operands, no mask: no scratch of its own
+    return linear_core(ctx, &A, wo, y, st, gw);
 }
 
 }  // namespace
@@ -1350,6 +1487,22 @@ kd_attn_status kd_attn_qkv_projection(kd_attn_ctx* ctx, const kd_tensor* x, cons
     const kd_linear* w[3] = {wq, wk, wv};
     kd_tensor* outs[3] = {q_out, k_out, v_out};
     return qkv_projection_core(ctx, x, w, q_gain, k_gain, eps, rope, out_dtype, outs, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_linear(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* w, kd_tensor* y, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return linear_core(ctx, x, w, y, static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                            const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                            const float* q_gain, const float* k_gain, float eps,
+                                            const kd_rope3d* rope, kd_tensor* y, void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return self_attention_block_core(ctx, x, wq, wk, wv, wo, q_gain, k_gain, eps, rope, y,
+                                     static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,

@@ -903,8 +903,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         float a, bb;
                         if ((kPolyPairs >> i) & 1u) {
-                            a = exp2_poly(xa);
-                            bb = exp2_poly(xb);
+                            exp2_poly2(xa, xb, a, bb);
                         } else {
                             a = ex2_approx(xa);
                             bb = ex2_approx(xb);

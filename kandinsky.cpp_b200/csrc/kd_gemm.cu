@@ -159,6 +159,12 @@ __device__ __forceinline__ void store_chunk(TO* dst, const float* v) {  // 32 va
         d[i] = make_uint4(Pack2<TO>::pack(v[8 * i], v[8 * i + 1]), Pack2<TO>::pack(v[8 * i + 2], v[8 * i + 3]),
                           Pack2<TO>::pack(v[8 * i + 4], v[8 * i + 5]), Pack2<TO>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
+template <>
+__device__ __forceinline__ void store_chunk<float>(float* dst, const float* v) {  // 32 values, 128 bytes
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
 
 // Launched as clusters of 2 (blockIdx.x = 2 * pair + rank); both CTAs run the producer and the epilogue
 // warps, rank 0 also issues the MMAs.
@@ -509,7 +515,8 @@ cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms
 
 cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
                             cudaStream_t st) {
-    auto kern = ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16> : qkv_gemm_kernel<__half>;
+    auto kern = ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16>
+                                    : (ot == OutType::F16 ? qkv_gemm_kernel<__half> : qkv_gemm_kernel<float>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemAlloc);
     if (e != cudaSuccess) return e;
     const long long tiles = (long long)((p.M + kPairM - 1) / kPairM) * (p.nslots * p.C / kBN);

@@ -6,6 +6,10 @@
 // buffers immediately (enqueued on a CUDA stream) instead of adding graph nodes:
 //
 //   kd::ops::attention            src/core/ops.hpp:107-207  (ops::attention, flash branch)
+//   kd::ops::linear               src/core/ops.hpp:27-42    (ops::linear: mul_mat + bias)
+//   kd::Linear                    src/core/module.hpp:87-110 (Linear's weight and bias)
+//   kd::dit_self_attention_block  src/models/crossdit.hpp:117-154 (DiTSelfAttention::forward whole:
+//                                 to_query/to_key/to_value, norms, RoPE, attention, out_layer)
 //   kd::dit_self_attention        src/models/crossdit.hpp:132-150 (DiTSelfAttention::forward
 //                                 between the Q/K/V Linears and out_layer)
 //   kd::dit_cross_attention       src/models/crossdit.hpp:186-198 (DiTCrossAttention::forward)
@@ -79,6 +83,28 @@ struct CrossDiTAttentionConfig {
     static CrossDiTAttentionConfig pro_video() { return CrossDiTAttentionConfig{}; }
 };
 
+// A Linear layer's parameters as Linear::init_params allocates them (module.hpp:97-103): the weight, ggml
+// [in_features, out_features] of type f32 / f16 / bf16 / q4_0 / q8_0 (row r = output feature r, nb1 bytes
+// apart), and an f32 bias [out_features] or none.
+struct Linear {
+    const void* weight = nullptr;
+    int32_t type = KD_ATTN_TYPE_F16;
+    int64_t in_features = 0, out_features = 0;
+    size_t nb1 = 0;
+    const float* bias = nullptr;
+
+    kd_linear view() const {
+        kd_linear l{};
+        l.data = weight;
+        l.type = type;
+        l.ne[0] = in_features;
+        l.ne[1] = out_features;
+        l.nb1 = nb1;
+        l.bias = bias;
+        return l;
+    }
+};
+
 // Owns one kd_attn_ctx (per device).  Move-only.
 class Context {
 public:
@@ -129,7 +155,39 @@ inline bool attention(Context& ctx, const Tensor& q, const Tensor& k, const Tens
                              stream) == KD_ATTN_OK;
 }
 
+// ops::linear(ctx, x, w, b) (ops.hpp:27-42): y = x W^T + b with x [in, L, N] (f32, or bf16 read in place)
+// and y [out, L, N] (f32, bf16 or f16).  false on shapes or types the GEMM does not take.
+inline bool linear(Context& ctx, const Tensor& x, const Linear& w, Tensor& y, void* stream = nullptr) {
+    if (!ctx.ok()) return false;
+    const kd_tensor tx = x.view();
+    const kd_linear tw = w.view();
+    kd_tensor ty = y.view();
+    return kd_attn_linear(ctx.get(), &tx, &tw, &ty, stream) == KD_ATTN_OK;
+}
+
 }  // namespace ops
+
+// DiTSelfAttention::forward (crossdit.hpp:117-154) whole, from the hidden states x [C, L, N] f32 to the
+// out_layer output y [C_out, L, N]: the Q/K/V Linears fused with the per-head RMSNorm and 3D RoPE, the
+// flash attention, out_layer.  The operands are bf16 whatever cfg.op_type says.
+inline bool dit_self_attention_block(Context& ctx, const Tensor& x, const Linear& to_query, const Linear& to_key,
+                                     const Linear& to_value, const Linear& out_layer, const float* query_norm_w,
+                                     const float* key_norm_w, const int32_t grid[3],
+                                     const CrossDiTAttentionConfig& cfg, Tensor& y, void* stream = nullptr) {
+    if (!ctx.ok() || cfg.head_dim != 128) return false;
+    kd_rope3d rope{};
+    for (int a = 0; a < 3; ++a) {
+        rope.axes_dim[a] = cfg.axes_dims[a];
+        rope.grid[a] = grid[a];
+        rope.scale_factor[a] = cfg.scale_factor[a];
+    }
+    rope.theta = cfg.rope_theta;
+    const kd_tensor tx = x.view();
+    const kd_linear wq = to_query.view(), wk = to_key.view(), wv = to_value.view(), wo = out_layer.view();
+    kd_tensor ty = y.view();
+    return kd_attn_self_attention_block(ctx.get(), &tx, &wq, &wk, &wv, &wo, query_norm_w, key_norm_w, cfg.norm_eps,
+                                        &rope, &ty, stream) == KD_ATTN_OK;
+}
 
 // DiTSelfAttention::forward from the Q/K/V projections to the input of out_layer
 // (crossdit.hpp:132-150): per-head RMSNorm of Q and K with the query_norm / key_norm weights

@@ -44,7 +44,7 @@ EXPORTED = [
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
     "kd_attn_selftest_wait", "kd_attn_noalloc_status", "kd_attn_noalloc_selftest_wait",
-    "kd_attn_qkv_projection",
+    "kd_attn_qkv_projection", "kd_attn_linear", "kd_attn_self_attention_block",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -156,6 +156,10 @@ def _load():
     L.kd_attn_qkv_projection.argtypes = [P, T, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D),
                                          ctypes.c_int32, T, T, T, P]
     L.kd_attn_qkv_projection.restype = st
+    L.kd_attn_linear.argtypes = [P, T, W, T, P]
+    L.kd_attn_linear.restype = st
+    L.kd_attn_self_attention_block.argtypes = [P, T, W, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), T, P]
+    L.kd_attn_self_attention_block.restype = st
     L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
@@ -351,6 +355,20 @@ class Context:
                                               int(out_dtype), _ref(q_out), _ref(k_out), _ref(v_out),
                                               _stream_ptr(stream)))
         return q_out, k_out, v_out
+
+    def linear(self, x, w, y, stream=None):
+        """ops::linear: y (N, L, C) = x (N, L, K) W^T + b; x f32 or bf16, w a KdLinear, y f32/bf16/f16."""
+        self.check(lib.kd_attn_linear(self.handle, _ref(x), ctypes.byref(w), _ref(y), _stream_ptr(stream)))
+        return y
+
+    def self_attention_block(self, x, wq, wk, wv, wo, y, q_gain=None, k_gain=None, eps=1e-6, rope=None,
+                             stream=None):
+        """DiTSelfAttention::forward from the hidden states x (N, L, C) f32 to y (N, L, C_out)."""
+        self.check(lib.kd_attn_self_attention_block(self.handle, _ref(x), ctypes.byref(wq), ctypes.byref(wk),
+                                                    ctypes.byref(wv), ctypes.byref(wo), _ptr(q_gain), _ptr(k_gain),
+                                                    float(eps), None if rope is None else ctypes.byref(rope), _ref(y),
+                                                    _stream_ptr(stream)))
+        return y
 
     def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
                        logit_softcap=0.0, tile_mask=None, stream=None):

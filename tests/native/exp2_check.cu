@@ -1,9 +1,12 @@
 // Accuracy of kd::exp2_poly (the FMA-pipe exp2 used for part of the softmax) on the GPU:
 // evaluates it on a dense grid over the argument range the softmax produces ([-130, 8],
-// plus -inf) and compares with exp2 in double on the host.  Prints
-// "max_rel <value> zero_ok <0|1>".  Built and run by tests/test_gpu_exp2.py.
+// plus -inf) and compares with exp2 in double on the host; and checks that the packed
+// kd::exp2_poly2 returns exactly exp2_poly's bits for every pair of grid points.  Prints
+// "max_rel <value> zero_ok <0|1> pair_equal <0|1>".  Built and run by tests/test_gpu_exp2.py.
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <vector>
 
 #include "kd_common.cuh"
@@ -11,6 +14,11 @@
 __global__ void eval(const float* x, float* y, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = kd::exp2_poly(x[i]);
+}
+
+__global__ void eval2(const float* x, float* y, int n) {  // pairs (x[i], x[n-1-i])
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) kd::exp2_poly2(x[i], x[n - 1 - i], y[2 * i], y[2 * i + 1]);
 }
 
 int main() {
@@ -36,7 +44,22 @@ int main() {
         const double rel = std::fabs((double)hy[i] - ref) / ref;
         if (rel > worst) worst = rel;
     }
-    printf("max_rel %.6e zero_ok %d\n", worst, zero_ok);
+    float* dy2 = nullptr;
+    std::vector<float> hy2(2 * (size_t)n);
+    if (cudaMalloc(&dy2, 2 * (size_t)n * 4) != cudaSuccess) return 2;
+    eval2<<<(n + 255) / 256, 256>>>(dx, dy2, n);
+    if (cudaMemcpy(hy2.data(), dy2, 2 * (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return 3;
+    int pair_equal = 1;
+    for (int i = 0; i < n; ++i) {
+        uint32_t a, b, c, d;
+        memcpy(&a, &hy2[2 * i], 4);
+        memcpy(&b, &hy[i], 4);
+        memcpy(&c, &hy2[2 * i + 1], 4);
+        memcpy(&d, &hy[n - 1 - i], 4);
+        if (a != b || c != d) pair_equal = 0;
+    }
+    cudaFree(dy2);
+    printf("max_rel %.6e zero_ok %d pair_equal %d\n", worst, zero_ok, pair_equal);
     cudaFree(dx);
     cudaFree(dy);
     return 0;

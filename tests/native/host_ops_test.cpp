@@ -3,6 +3,9 @@
 //   kd::ops::attention      -- plain flash branch, grouped-query heads, an f16 mask
 //   kd::dit_self_attention  -- RMSNorm (non-unit gains) + 3D RoPE + flash
 //   kd::dit_cross_attention -- RMSNorm + flash over text states with per-sequence valid lengths
+//   kd::ops::linear         -- f16 weight + bias against a double-precision product
+//   kd::dit_self_attention_block -- Linears + RMSNorm + RoPE + flash + out_layer against the oracle's
+//                              pieces composed on the CPU (operands rounded to bf16 where the GPU rounds)
 // and the error behaviour of ops::attention (false + a logged reason, nothing launched).
 // Gates: cosine >= 0.99995 and max-abs <= 2e-2 x output RMS against the oracle's fp64 mode.
 // `--cpu` checks only the host-side pieces (tensor views, constants, no-device failure).
@@ -83,6 +86,28 @@ static int cpu_checks() {
               c.scale_factor[1] == 2.f && c.norm_eps == 1e-6f,
           "pro_video constants");
     return 0;
+}
+
+// bf16 rounding of each element (the GEMM's operand type), kept as f32
+static std::vector<float> bf16_round(const std::vector<float>& a) {
+    std::vector<uint16_t> b(a.size());
+    std::vector<float> r(a.size());
+    kdo_convert(a.data(), (int64_t)a.size(), KDO_BF16, b.data());
+    kdo_to_f32(b.data(), KDO_BF16, (int64_t)b.size(), r.data());
+    return r;
+}
+
+// y[m][c] = sum_k x[m][k] w[c][k] + b[c] in double, rounded to f32 (ops::linear on the CPU)
+static std::vector<float> cpu_linear(const std::vector<float>& x, const std::vector<float>& w, const float* b,
+                                     int64_t M, int64_t K, int64_t C) {
+    std::vector<float> y((size_t)M * C);
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t c = 0; c < C; ++c) {
+            double acc = b ? b[c] : 0.0;
+            for (int64_t k = 0; k < K; ++k) acc += (double)x[m * K + k] * w[c * K + k];
+            y[m * C + c] = (float)acc;
+        }
+    return y;
 }
 
 int main(int argc, char** argv) {
@@ -223,6 +248,104 @@ int main(int argc, char** argv) {
                                           ref.data(), nullptr, 8);
         CHECK(rc == 0, "oracle rc %d", rc);
         gates("dit_cross_attention", got, ref);
+    }
+
+    // ---- ops::linear: f32 x [256, 100, 2], f16 weight [256 -> 512] with bias, f32 y
+    {
+        const int64_t N = 2, L = 100, K = 256, C = 512, M = N * L;
+        std::vector<float> x = randn(41, 0, M * K), w = randn(41, 1, C * K), b = randn(41, 2, C);
+        for (float& e : w) e *= 0.0625f;
+        std::vector<uint16_t> w16(w.size());
+        kdo_convert(w.data(), (int64_t)w.size(), KDO_F16, w16.data());
+        std::vector<float> wf(w.size());
+        kdo_to_f32(w16.data(), KDO_F16, (int64_t)w16.size(), wf.data());
+        Dev dx(x.size() * 4), dw(w16.size() * 2), db(b.size() * 4), dy(M * C * 4);
+        kd::Tensor tx = kd::Tensor::contiguous(upload(dx, x.data(), x.size() * 4), KD_ATTN_TYPE_F32, K, L, N);
+        kd::Linear lin;
+        lin.weight = upload(dw, w16.data(), w16.size() * 2);
+        lin.type = KD_ATTN_TYPE_F16;
+        lin.in_features = K;
+        lin.out_features = C;
+        lin.nb1 = (size_t)K * 2;
+        lin.bias = (const float*)upload(db, b.data(), b.size() * 4);
+        kd::Tensor ty = kd::Tensor::contiguous(dy.p, KD_ATTN_TYPE_F32, C, L, N);
+        const bool ok = kd::ops::linear(ctx, tx, lin, ty);
+        CHECK(ok && ctx.device_status(), "ops::linear: %s", ctx.last_error().c_str());
+        std::vector<float> got(M * C);
+        cudaMemcpy(got.data(), dy.p, got.size() * 4, cudaMemcpyDeviceToHost);
+        gates("ops::linear", got, cpu_linear(bf16_round(x), bf16_round(wf), b.data(), M, K, C));
+        kd::Linear bad = lin;
+        bad.out_features = 320;  // not a multiple of 256
+        CHECK(!kd::ops::linear(ctx, tx, bad, ty), "out_features 320 accepted");
+    }
+
+    // ---- dit_self_attention_block: x [256, 64, 1] -> Linears (f16) -> RMSNorm + RoPE -> flash -> out_layer
+    {
+        const int64_t N = 1, H = 2, C = H * 128;
+        const int32_t grid[3] = {2, 4, 8};
+        const int64_t L = grid[0] * grid[1] * grid[2], M = N * L;
+        std::vector<float> x = randn(51, 0, M * C);
+        std::vector<float> wf[4], bias[4];
+        std::vector<uint16_t> w16[4];
+        Dev dw0(C * C * 2), dw1(C * C * 2), dw2(C * C * 2), dw3(C * C * 2), db0(C * 4), db1(C * 4), db2(C * 4),
+            db3(C * 4);
+        Dev* dws[4] = {&dw0, &dw1, &dw2, &dw3};
+        Dev* dbs[4] = {&db0, &db1, &db2, &db3};
+        kd::Linear lin[4];
+        for (int i = 0; i < 4; ++i) {
+            std::vector<float> w = randn(52, (uint32_t)i, C * C);
+            for (float& e : w) e *= 0.0625f;
+            w16[i].resize(w.size());
+            kdo_convert(w.data(), (int64_t)w.size(), KDO_F16, w16[i].data());
+            wf[i].resize(w.size());
+            kdo_to_f32(w16[i].data(), KDO_F16, (int64_t)w.size(), wf[i].data());
+            bias[i] = randn(53, (uint32_t)i, C);
+            lin[i].weight = upload(*dws[i], w16[i].data(), w16[i].size() * 2);
+            lin[i].type = KD_ATTN_TYPE_F16;
+            lin[i].in_features = C;
+            lin[i].out_features = C;
+            lin[i].nb1 = (size_t)C * 2;
+            lin[i].bias = (const float*)upload(*dbs[i], bias[i].data(), C * 4);
+        }
+        std::vector<float> gq(128), gk(128);
+        for (int i = 0; i < 128; ++i) {
+            gq[i] = 0.75f + (float)i / 256.0f;
+            gk[i] = 1.25f - (float)i / 512.0f;
+        }
+        Dev dx(x.size() * 4), dgq(512), dgk(512), dy(M * C * 4);
+        upload(dgq, gq.data(), 512);
+        upload(dgk, gk.data(), 512);
+        kd::Tensor tx = kd::Tensor::contiguous(upload(dx, x.data(), x.size() * 4), KD_ATTN_TYPE_F32, C, L, N);
+        kd::Tensor ty = kd::Tensor::contiguous(dy.p, KD_ATTN_TYPE_F32, C, L, N);
+        const kd::CrossDiTAttentionConfig cfg = kd::CrossDiTAttentionConfig::pro_video();
+        const bool ok = kd::dit_self_attention_block(ctx, tx, lin[0], lin[1], lin[2], lin[3], (const float*)dgq.p,
+                                                     (const float*)dgk.p, grid, cfg, ty);
+        CHECK(ok && ctx.device_status(), "dit_self_attention_block: %s", ctx.last_error().c_str());
+        std::vector<float> got(M * C);
+        cudaMemcpy(got.data(), dy.p, got.size() * 4, cudaMemcpyDeviceToHost);
+        // CPU: bf16 x and weights -> projections -> RMSNorm -> RoPE -> bf16 operands -> flash (fp64)
+        //      -> bf16 attention output -> out_layer with bf16 weight
+        const std::vector<float> xr = bf16_round(x);
+        std::vector<float> q = cpu_linear(xr, bf16_round(wf[0]), bias[0].data(), M, C, C);
+        std::vector<float> k = cpu_linear(xr, bf16_round(wf[1]), bias[1].data(), M, C, C);
+        std::vector<float> v = cpu_linear(xr, bf16_round(wf[2]), bias[2].data(), M, C, C);
+        std::vector<float> qn(q.size()), kn(k.size()), table((size_t)L * 128);
+        kdo_rms_norm_heads(q.data(), M * H, 128, gq.data(), cfg.norm_eps, qn.data(), 8);
+        kdo_rms_norm_heads(k.data(), M * H, 128, gk.data(), cfg.norm_eps, kn.data(), 8);
+        kdo_visual_rope_table(grid[0], grid[1], grid[2], cfg.axes_dims, cfg.scale_factor, cfg.rope_theta, table.data());
+        kdo_rope_apply(qn.data(), L, N, (int)H, 128, table.data(), 8);
+        kdo_rope_apply(kn.data(), L, N, (int)H, 128, table.data(), 8);
+        std::vector<uint16_t> q16(q.size()), k16(k.size()), v16(v.size());
+        kdo_convert(qn.data(), (int64_t)q.size(), KDO_BF16, q16.data());
+        kdo_convert(kn.data(), (int64_t)k.size(), KDO_BF16, k16.data());
+        kdo_convert(v.data(), (int64_t)v.size(), KDO_BF16, v16.data());
+        const kdo_tensor oq = head_view(q16.data(), KDO_BF16, L, H, N), okk = head_view(k16.data(), KDO_BF16, L, H, N),
+                         ovv = head_view(v16.data(), KDO_BF16, L, H, N);
+        std::vector<float> attn(M * C);
+        const int rc = kdo_flash_attn_ext(&oq, &okk, &ovv, nullptr, 1.0f / std::sqrt(128.0f), nullptr, KDO_MODE_EXACT,
+                                          attn.data(), nullptr, 8);
+        CHECK(rc == 0, "oracle rc %d", rc);
+        gates("dit_self_attention_block", got, cpu_linear(bf16_round(attn), bf16_round(wf[3]), bias[3].data(), M, C, C));
     }
 
     printf(g_fail ? "FAILED\n" : "OK\n");

@@ -1,4 +1,5 @@
-"""exp2_poly (part of the softmax exponentials on the FMA pipe) against exp2 in double, on the GPU.
+"""exp2_poly (part of the softmax exponentials on the FMA pipe) against exp2 in double, on the GPU, and
+its packed f32x2 form exp2_poly2 against it bit for bit.
 
 Bound: 2^-13 relative error over the softmax's argument range (the Remez fit gives 7.5e-5 =
 2^-13.7 before float rounding), exact zeros at or below -126 and for -inf.
@@ -27,6 +28,7 @@ def test_exp2_poly_error_bound(tmp_path):
     out = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stderr
     fields = out.stdout.split()
-    max_rel, zero_ok = float(fields[1]), int(fields[3])
+    max_rel, zero_ok, pair_equal = float(fields[1]), int(fields[3]), int(fields[5])
     assert zero_ok == 1
+    assert pair_equal == 1, "exp2_poly2 differs from exp2_poly"
     assert max_rel <= 2.0 ** -13, max_rel

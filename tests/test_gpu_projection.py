@@ -175,3 +175,58 @@ def test_rejected_shapes(ctx, kd):
     ctx.qkv_projection(x, None, None, lin, None, None, out)
     ctx.device_status()
     assert torch.count_nonzero(out.float()) == 0
+
+
+# ------------------------------------------------------------------ kd_attn_linear and the whole block
+def test_linear_matches_oracle(ctx, kd):
+    """ops::linear through kd_attn_linear: f32 x, q8_0 weight with bias, f32 y against the fp64 product of
+    the dequantized weight; 600 tokens (ragged last tile)."""
+    N, L, K, C = 2, 300, 1024, 512
+    x = seeded((N, L, K), 111, 0)
+    lin, keep, deq, b = make_weight(kd, 112, 0, C, K, kd.Q8_0)
+    y = torch.full((N, L, C), float("nan"), device="cuda")
+    ctx.linear(dev(x), lin, y)
+    ctx.device_status()
+    exact = oracle.linear(x, deq, b)
+    got = y.cpu().numpy()
+    assert_gates(got, exact, label="linear vs exact operands")
+    rounded = oracle.linear(bf16_round(x), bf16_round(deq), b)
+    rms = float(np.sqrt(np.mean(rounded ** 2)))
+    assert float(np.max(np.abs(got - rounded))) / rms <= TIGHT
+
+
+def test_linear_bf16_input_read_in_place(ctx, kd):
+    """bf16 x whose K is a whole number of K steps is read without a copy; f16 weight, bf16 y."""
+    N, L, K, C = 1, 200, 512, 256
+    xb = oracle.to_type(seeded((N, L, K), 121, 0), oracle.BF16)
+    x = oracle.to_f32(xb, oracle.BF16)
+    lin, keep, deq, b = make_weight(kd, 122, 0, C, K, kd.F16)
+    y = torch.empty((N, L, C), device="cuda", dtype=torch.bfloat16)
+    ctx.linear(torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16), lin, y)
+    ctx.device_status()
+    exact = oracle.linear(x, deq, b)
+    assert_gates(y.float().cpu().numpy(), exact, label="bf16 linear", out_type="bf16")
+
+
+def test_self_attention_block_matches_oracle(ctx, kd):
+    """DiTSelfAttention::forward (crossdit.hpp:117-154) from the hidden states: q8_0 Q/K/V weights with
+    biases, RMSNorm gains, 3D RoPE, f16 out-projection; against the oracle's linear -> RMSNorm -> RoPE ->
+    flash_attn_ext -> linear chain on the exact operands (the block rounds x, the weights, the operands and
+    the attention output to bf16)."""
+    N, grid, C = 1, (2, 8, 16), 512
+    H, L = C // 128, int(np.prod(grid))
+    x = seeded((N, L, C), 131, 0)
+    lin = [make_weight(kd, 132, 10 * i, C, C, kd.Q8_0) for i in range(3)]
+    lo, keep_o, deq_o, b_o = make_weight(kd, 133, 0, C, C, kd.F16)
+    q_gain = (1.0 + 0.1 * seeded((128,), 134, 0)).astype(np.float32)
+    k_gain = (1.0 + 0.1 * seeded((128,), 134, 1)).astype(np.float32)
+    y = torch.full((N, L, C), float("nan"), device="cuda")
+    ctx.self_attention_block(dev(x), lin[0][0], lin[1][0], lin[2][0], lo, y, q_gain=dev(q_gain),
+                             k_gain=dev(k_gain), rope=kd.Rope3D.make(grid))
+    ctx.device_status()
+    proj = [oracle.linear(x, l[2], l[3]).astype(np.float32) for l in lin]
+    attn = oracle.self_attention(*proj, H, q_gain=q_gain, k_gain=k_gain, rope_table=oracle.visual_rope_table(grid),
+                                 kv_type=oracle.BF16, q_type=oracle.BF16, mode=oracle.EXACT)
+    ref = oracle.linear(attn, deq_o, b_o)
+    m = oracle.parity_metrics(y.cpu().numpy(), ref)
+    assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m
