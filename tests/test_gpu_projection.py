@@ -230,3 +230,21 @@ def test_self_attention_block_matches_oracle(ctx, kd):
     ref = oracle.linear(attn, deq_o, b_o)
     m = oracle.parity_metrics(y.cpu().numpy(), ref)
     assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m
+
+
+@pytest.mark.parametrize("N,L,K,C", [(1, 5, 32, 256), (3, 129, 96, 512), (2, 0, 64, 256)])
+def test_small_and_degenerate_shapes(ctx, kd, N, L, K, C):
+    """One K step that is mostly padding (K = 32), a single 256-feature tile, fewer tokens than one CTA
+    pair's 256 rows, three sequences of 129 tokens, and zero tokens (nothing launched)."""
+    H = C // 128
+    x = seeded((N, L, K), 141, 0)
+    lin = [make_weight(kd, 142, 10 * i, C, K, kd.Q4_0) for i in range(3)]
+    outs = [torch.zeros((N, H, L, 128), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(dev(x), lin[0][0], lin[1][0], lin[2][0], *outs)
+    y = torch.zeros((N, L, C), device="cuda")
+    ctx.linear(dev(x), lin[2][0], y)
+    ctx.device_status()
+    if L == 0:
+        return
+    check(outs, x, [l[2] for l in lin], [l[3] for l in lin], H, None, None, None, "bf16", f"small {N}x{L}x{K}")
+    assert_gates(y.cpu().numpy(), oracle.linear(x, lin[2][2], lin[2][3]), label="small linear")
