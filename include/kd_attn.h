@@ -222,6 +222,16 @@ kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x
                                             const float* q_gain, const float* k_gain, float eps,
                                             const kd_rope3d* rope, kd_tensor* y, void* stream);
 
+/* Replaces DiTCrossAttention::forward (crossdit.hpp:174-200): visual queries from x_query [C, Lq, N] f32,
+ * keys and values from the text states x_kv [C, Lk, N] f32 (RMSNorm on Q and K, no RoPE), flash
+ * attention with the text's valid lengths -- kv_len (device int32 [N]) and/or an f16 mask as for
+ * kd_attn_flash_ext, either may be NULL -- and the out-projection; y : [C_out, Lq, N]. */
+kd_attn_status kd_attn_cross_attention_block(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
+                                             const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
+                                             const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
+                                             const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
+                                             void* stream);
+
 /* ---------------------------------------------------------------------------
  * ggml_flash_attn_ext semantics (called at ops.hpp:176):
  *   out[:, h, i, n] = softmax_j(scale * q[:, i, h, n] . k[:, j, hk, nk] + mask[j, i, h%mh, n%mn]) v[:, j, hk, nk]

@@ -1287,6 +1287,64 @@ kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, c
     return linear_core(ctx, &A, wo, y, st, gw);
 }
 
+// DiTCrossAttention::forward (crossdit.hpp:174-200) from the visual and text hidden states: the Q
+// projection of x_query and the K/V projections of x_kv (RMSNorm on Q and K, no RoPE), the flash kernel
+// with the text's valid lengths (kv_len and/or an f16 mask), the out-projection.  Scratch: [the flash
+// core's mask-class scratch][Q][K][V operands][attention output][GEMM work shared by the three GEMMs].
+kd_attn_status cross_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
+                                          const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
+                                          const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
+                                          const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
+                                          cudaStream_t st) {
+    kd_attn_status rc;
+    GemmInput iq, ikv;
+    if ((rc = gemm_input(ctx, x_query, &iq)) || (rc = gemm_input(ctx, x_kv, &ikv))) return rc;
+    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    const int64_t C = wq->ne[1], Lq = iq.L, Lk = ikv.L, N = iq.N;
+    if (ikv.N != N) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x_query and x_kv disagree on the batch");
+    if (C % kHeadDim || wk->ne[1] != C || wv->ne[1] != C || wo->ne[0] != C)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the projections must map to n_head * 128 features and back");
+    const int32_t H = (int32_t)(C / kHeadDim);
+    const int32_t op = KD_ATTN_TYPE_BF16;
+    const size_t qb = align256((size_t)N * H * Lq * kHeadDim * 2);
+    const size_t kb = align256((size_t)N * H * Lk * kHeadDim * 2);
+    const size_t flash_extra =
+        mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
+    GemmInput attn_in = iq;  // the out-projection reads the attention output [C, Lq, N] bf16 in place
+    attn_in.K = attn_in.Kp = C;
+    attn_in.direct = true;
+    const size_t work = std::max({gemm_work_bytes(iq, 1, C, false), gemm_work_bytes(ikv, 2, C, false),
+                                  gemm_work_bytes(attn_in, 1, wo->ne[1], false)});
+    if ((rc = ensure_scratch(ctx, flash_extra + 2 * qb + 2 * kb + work, st))) return rc;
+    char* base = static_cast<char*>(ctx->scratch) + flash_extra;
+    kd_tensor Qs = operand_view(base, op, Lq, H, N);
+    kd_tensor Ks = operand_view(base + qb, op, Lk, H, N);
+    kd_tensor Vs = operand_view(base + qb + kb, op, Lk, H, N);
+    kd_tensor A{};  // attention output [C, Lq, N] bf16 = the flash dst [128, H, Lq, N]
+    A.data = base + qb + 2 * kb;
+    A.type = op;
+    A.ne[0] = C;
+    A.ne[1] = Lq;
+    A.ne[2] = N;
+    A.ne[3] = 1;
+    A.nb[0] = 2;
+    A.nb[1] = 2 * (size_t)C;
+    A.nb[2] = A.nb[1] * (size_t)Lq;
+    A.nb[3] = A.nb[2] * (size_t)N;
+    char* gw = base + 2 * qb + 2 * kb;
+    const kd_linear* wq3[3] = {wq, nullptr, nullptr};
+    kd_tensor* oq3[3] = {&Qs, nullptr, nullptr};
+    if ((rc = qkv_projection_core(ctx, x_query, wq3, q_gain, nullptr, eps, nullptr, op, oq3, st, gw))) return rc;
+    const kd_linear* wkv3[3] = {nullptr, wk, wv};
+    kd_tensor* okv3[3] = {nullptr, &Ks, &Vs};
+    if ((rc = qkv_projection_core(ctx, x_kv, wkv3, nullptr, k_gain, eps, nullptr, op, okv3, st, gw))) return rc;
+    kd_tensor ov;
+    if ((rc = out_view(ctx, &A, H, Lq, N, &ov))) return rc;
+    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, nullptr};
+    if ((rc = flash_run(ctx, fa, st))) return rc;
+    return linear_core(ctx, &A, wo, y, st, gw);
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1503,6 +1561,17 @@ kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x
     DeviceGuard g(ctx->device);
     return self_attention_block_core(ctx, x, wq, wk, wv, wo, q_gain, k_gain, eps, rope, y,
                                      static_cast<cudaStream_t>(stream));
+}
+
+kd_attn_status kd_attn_cross_attention_block(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
+                                             const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
+                                             const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
+                                             const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
+                                             void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return cross_attention_block_core(ctx, x_query, x_kv, wq, wk, wv, wo, q_gain, k_gain, eps, mask, kv_len, y,
+                                      static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,

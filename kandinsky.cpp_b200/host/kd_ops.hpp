@@ -10,6 +10,7 @@
 //   kd::Linear                    src/core/module.hpp:87-110 (Linear's weight and bias)
 //   kd::dit_self_attention_block  src/models/crossdit.hpp:117-154 (DiTSelfAttention::forward whole:
 //                                 to_query/to_key/to_value, norms, RoPE, attention, out_layer)
+//   kd::dit_cross_attention_block src/models/crossdit.hpp:174-200 (DiTCrossAttention::forward whole)
 //   kd::dit_self_attention        src/models/crossdit.hpp:132-150 (DiTSelfAttention::forward
 //                                 between the Q/K/V Linears and out_layer)
 //   kd::dit_cross_attention       src/models/crossdit.hpp:186-198 (DiTCrossAttention::forward)
@@ -187,6 +188,24 @@ inline bool dit_self_attention_block(Context& ctx, const Tensor& x, const Linear
     kd_tensor ty = y.view();
     return kd_attn_self_attention_block(ctx.get(), &tx, &wq, &wk, &wv, &wo, query_norm_w, key_norm_w, cfg.norm_eps,
                                         &rope, &ty, stream) == KD_ATTN_OK;
+}
+
+// DiTCrossAttention::forward (crossdit.hpp:174-200) whole: x_query [C, Lq, N] visual and x_kv [C, Lk, N]
+// text hidden states (f32) to out_layer's output y [C_out, Lq, N]; RMSNorm on Q and K, no RoPE; the text's
+// valid lengths as kv_len (device int32 [N]) and/or an f16 mask, either may be null.
+inline bool dit_cross_attention_block(Context& ctx, const Tensor& x_query, const Tensor& x_kv, const Linear& to_query,
+                                      const Linear& to_key, const Linear& to_value, const Linear& out_layer,
+                                      const float* query_norm_w, const float* key_norm_w, const int32_t* kv_len,
+                                      const Tensor* mask, const CrossDiTAttentionConfig& cfg, Tensor& y,
+                                      void* stream = nullptr) {
+    if (!ctx.ok() || cfg.head_dim != 128) return false;
+    const kd_tensor tq = x_query.view(), tkv = x_kv.view();
+    const kd_linear wq = to_query.view(), wk = to_key.view(), wv = to_value.view(), wo = out_layer.view();
+    kd_tensor tm{};
+    if (mask) tm = mask->view();
+    kd_tensor ty = y.view();
+    return kd_attn_cross_attention_block(ctx.get(), &tq, &tkv, &wq, &wk, &wv, &wo, query_norm_w, key_norm_w,
+                                         cfg.norm_eps, mask ? &tm : nullptr, kv_len, &ty, stream) == KD_ATTN_OK;
 }
 
 // DiTSelfAttention::forward from the Q/K/V projections to the input of out_layer

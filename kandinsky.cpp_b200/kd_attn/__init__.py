@@ -44,7 +44,7 @@ EXPORTED = [
     "kd_attn_tile_stats", "kd_attn_set_log_callback", "kd_attn_symmetric_alloc", "kd_attn_symmetric_free",
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
     "kd_attn_selftest_wait", "kd_attn_noalloc_status", "kd_attn_noalloc_selftest_wait",
-    "kd_attn_qkv_projection", "kd_attn_linear", "kd_attn_self_attention_block",
+    "kd_attn_qkv_projection", "kd_attn_linear", "kd_attn_self_attention_block", "kd_attn_cross_attention_block",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -160,6 +160,8 @@ def _load():
     L.kd_attn_linear.restype = st
     L.kd_attn_self_attention_block.argtypes = [P, T, W, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), T, P]
     L.kd_attn_self_attention_block.restype = st
+    L.kd_attn_cross_attention_block.argtypes = [P, T, T, W, W, W, W, P, P, ctypes.c_float, T, P, T, P]
+    L.kd_attn_cross_attention_block.restype = st
     L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
@@ -368,6 +370,16 @@ class Context:
                                                     ctypes.byref(wv), ctypes.byref(wo), _ptr(q_gain), _ptr(k_gain),
                                                     float(eps), None if rope is None else ctypes.byref(rope), _ref(y),
                                                     _stream_ptr(stream)))
+        return y
+
+    def cross_attention_block(self, x_query, x_kv, wq, wk, wv, wo, y, q_gain=None, k_gain=None, eps=1e-6,
+                              mask=None, kv_len=None, stream=None):
+        """DiTCrossAttention::forward: x_query (N, Lq, C) f32 visual, x_kv (N, Lk, C) f32 text -> y (N, Lq, C_out);
+        kv_len: device int32 (N,) valid text lengths, mask: f16 (mn, mh, >=Lq, >=Lk), either may be None."""
+        self.check(lib.kd_attn_cross_attention_block(self.handle, _ref(x_query), _ref(x_kv), ctypes.byref(wq),
+                                                     ctypes.byref(wk), ctypes.byref(wv), ctypes.byref(wo),
+                                                     _ptr(q_gain), _ptr(k_gain), float(eps), _ref(mask),
+                                                     _ptr(kv_len), _ref(y), _stream_ptr(stream)))
         return y
 
     def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
