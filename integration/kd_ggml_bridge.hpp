@@ -7,7 +7,9 @@
 //   - supports_attention: the shape/type test libkd_attn applies, made at graph-build time, so the
 //     caller keeps ggml's own path for what the library does not cover -- the role of
 //     ggml_backend_supports_op in ops.hpp:179-181;
-//   - attention_node / dit_self_attention_node: ggml custom-op callbacks that run the library on
+//   - linear_from_ggml / supports_self_attention_block: a Linear's ggml weight (f32/f16/bf16/q4_0/q8_0)
+//     and bias as a kd_linear, and the build-time test for DiTSelfAttention::forward as one node;
+//   - attention_node / dit_self_attention_node / dit_block_node: ggml custom-op callbacks that run the library on
 //     the node's tensors (device memory: the node is computed where the tensors live, i.e. the DiT
 //     graph is split at each attention node -- INTEGRATION.md);
 //   - cfg_pair_*: the two classifier-free-guidance halves (two batch-1 forwards in the reference,
@@ -127,6 +129,63 @@ inline void dit_self_attention_node(ggml_tensor* dst, int ith, int /*nth*/, void
                                            a->use_rope ? &a->rope : nullptr, s.op_type, &o, nullptr, s.stream);
     if (s.last_status != KD_ATTN_OK)
         fprintf(stderr, "kd_bridge: kd_attn_self_attention failed (%d): %s\n", s.last_status,
+                kd_attn_last_error(s.ctx));
+}
+
+// A Linear's parameters (module.hpp:97-103: weight ggml [in, out], f32 bias [out] or none) as a kd_linear.
+inline bool linear_from_ggml(const ggml_tensor* w, const ggml_tensor* b, kd_linear* out) {
+    if (!w) return false;
+    switch (w->type) {
+        case GGML_TYPE_F32: out->type = KD_ATTN_TYPE_F32; break;
+        case GGML_TYPE_F16: out->type = KD_ATTN_TYPE_F16; break;
+        case GGML_TYPE_BF16: out->type = KD_ATTN_TYPE_BF16; break;
+        case GGML_TYPE_Q4_0: out->type = KD_ATTN_TYPE_Q4_0; break;
+        case GGML_TYPE_Q8_0: out->type = KD_ATTN_TYPE_Q8_0; break;
+        default: return false;
+    }
+    if (b && (b->type != GGML_TYPE_F32 || b->ne[0] != w->ne[1])) return false;
+    out->data = w->data;
+    out->ne[0] = w->ne[0];
+    out->ne[1] = w->ne[1];
+    out->nb1 = w->nb[1];
+    out->bias = b ? static_cast<const float*>(b->data) : nullptr;
+    return true;
+}
+
+// Would kd_attn_self_attention_block take DiTSelfAttention::forward(x) with these parameters?  x [C, L, N]
+// f32 with C = n_head * 128, the four Linears [C, C] (out_layer [C, C_out]) of types the GEMM expands,
+// C and C_out multiples of 256, a RoPE grid covering L.
+inline bool supports_self_attention_block(const ggml_tensor* x, const ggml_tensor* const w[4],
+                                          const ggml_tensor* const b[4], int64_t n_head, const kd_rope3d* rope) {
+    if (!x || x->type != GGML_TYPE_F32 || x->nb[0] != 4 || x->ne[3] != 1 || n_head <= 0) return false;
+    const int64_t C = x->ne[0];
+    if (C != n_head * 128 || C % 256) return false;
+    for (int i = 0; i < 4; ++i) {
+        kd_linear l{};
+        if (!linear_from_ggml(w[i], b[i], &l) || l.ne[0] != C || l.ne[1] % 256 || (i < 3 && l.ne[1] != C)) return false;
+    }
+    return !rope || (int64_t)rope->grid[0] * rope->grid[1] * rope->grid[2] == x->ne[1];
+}
+
+// Custom-op callback: dst [C_out, L, N] f32 = DiTSelfAttention::forward (crossdit.hpp:117-154) of
+// dst->src[0] = x, with src[1..8] = to_query, to_key, to_value, out_layer (weight, bias) pairs (a null
+// bias slot = no bias) and the norms / RoPE of `userdata` (a DitAttentionParams).
+inline void dit_block_node(ggml_tensor* dst, int ith, int /*nth*/, void* userdata) {
+    if (ith != 0) return;
+    State& s = state();
+    const DitAttentionParams* a = static_cast<const DitAttentionParams*>(userdata);
+    kd_tensor x, y;
+    kd_linear w[4];
+    bool ok = s.ctx && a && kd_from_ggml(dst->src[0], &x) && kd_from_ggml(dst, &y);
+    for (int i = 0; i < 4 && ok; ++i) ok = linear_from_ggml(dst->src[1 + 2 * i], dst->src[2 + 2 * i], &w[i]);
+    if (!ok) {
+        s.last_status = KD_ATTN_ERR_INVALID_ARGUMENT;
+        return;
+    }
+    s.last_status = kd_attn_self_attention_block(s.ctx, &x, &w[0], &w[1], &w[2], &w[3], a->q_gain, a->k_gain, a->eps,
+                                                 a->use_rope ? &a->rope : nullptr, &y, s.stream);
+    if (s.last_status != KD_ATTN_OK)
+        fprintf(stderr, "kd_bridge: kd_attn_self_attention_block failed (%d): %s\n", s.last_status,
                 kd_attn_last_error(s.ctx));
 }
 

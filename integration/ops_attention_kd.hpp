@@ -11,6 +11,8 @@
 // ops_kd::dit_self_attention is the fused form for DiTSelfAttention::forward (crossdit.hpp:132-150):
 // RMSNorm of q and k, 3D RoPE, attention, from the raw to_query/to_key/to_value outputs, as one node.
 // It returns nullptr when the library does not cover the call; the call site then keeps its code.
+// ops_kd::dit_self_attention_block is the whole module (crossdit.hpp:117-154) as one node: the Linears
+// with their GGUF weights, the norms, RoPE, attention and out_layer.
 //
 // Include after the reference's core/ops.hpp (for ops::attention) and after ggml.h.
 #pragma once
@@ -45,6 +47,20 @@ inline ggml_tensor* dit_self_attention(ggml_context* ctx, ggml_tensor* q, ggml_t
     ggml_tensor* args[3] = {q, k, v};
     return ggml_custom_4d(ctx, GGML_TYPE_F32, q->ne[0], q->ne[1], q->ne[2], 1, args, 3,
                           kd_bridge::dit_self_attention_node, 1, const_cast<kd_bridge::DitAttentionParams*>(params));
+}
+
+// DiTSelfAttention::forward (crossdit.hpp:117-154) whole as one node: x [C, L, N] f32 and the module's
+// parameters (to_query, to_key, to_value, out_layer weights and biases; a bias may be null) -> the
+// out_layer output [C_out, L, N] f32.  The weights stay in their GGUF types (q4_0 / q8_0 / f16 / bf16 /
+// f32).  nullptr when the library does not cover the call; the call site then keeps its code.
+inline ggml_tensor* dit_self_attention_block(ggml_context* ctx, ggml_tensor* x, ggml_tensor* const w[4],
+                                             ggml_tensor* const b[4], const kd_bridge::DitAttentionParams* params) {
+    if (!kd_bridge::enabled() || !params ||
+        !kd_bridge::supports_self_attention_block(x, w, b, params->n_head, params->use_rope ? &params->rope : nullptr))
+        return nullptr;
+    ggml_tensor* args[9] = {x, w[0], b[0], w[1], b[1], w[2], b[2], w[3], b[3]};
+    return ggml_custom_4d(ctx, GGML_TYPE_F32, w[3]->ne[1], x->ne[1], x->ne[2], 1, args, 9, kd_bridge::dit_block_node, 1,
+                          const_cast<kd_bridge::DitAttentionParams*>(params));
 }
 
 }  // namespace ops_kd

@@ -77,6 +77,18 @@ kd_attn_status kd_attn_self_attention(kd_attn_ctx*, const kd_tensor* q, const kd
     g_calls.push_back(c);
     return g_status;
 }
+static kd_linear g_block_w[4];
+static kd_tensor g_block_x, g_block_y;
+kd_attn_status kd_attn_self_attention_block(kd_attn_ctx*, const kd_tensor* x, const kd_linear* wq, const kd_linear* wk,
+                                            const kd_linear* wv, const kd_linear* wo, const float* qg, const float* kg,
+                                            float, const kd_rope3d* rope, kd_tensor* y, void*) {
+    Call c;
+    c.fn = "self_attention_block"; c.qg = qg; c.kg = kg; c.rope = rope;
+    g_block_x = *x; g_block_y = *y;
+    g_block_w[0] = *wq; g_block_w[1] = *wk; g_block_w[2] = *wv; g_block_w[3] = *wo;
+    g_calls.push_back(c);
+    return g_status;
+}
 const char* kd_attn_last_error(const kd_attn_ctx*) { return "fake"; }
 }
 
@@ -191,6 +203,38 @@ int main() {
     prm.rope.grid[0] = 6;  // grid no longer covers L: the call site keeps its own code
     CHECK(ops_kd::dit_self_attention(&gctx, &q, &k, &v, &prm) == nullptr);
     prm.rope.grid[0] = 5;
+
+    // 6b. the whole DiTSelfAttention::forward as one node, GGUF weight types kept (q8_0 Q/K/V, q4_0 out_layer)
+    {
+        ggml_tensor x = make(GGML_TYPE_F32, C, L, N, 0x800000);
+        ggml_tensor w[4], b[4];
+        for (int i = 0; i < 4; ++i) {
+            w[i] = make(i < 3 ? GGML_TYPE_Q8_0 : GGML_TYPE_Q4_0, C, C, 1, 0x900000 + 0x100000 * i);
+            w[i].nb[1] = (size_t)C / 32 * (i < 3 ? 34 : 18);  // ggml row size of the block types
+            b[i] = make(GGML_TYPE_F32, C, 1, 1, 0xd00000 + 0x10000 * i);
+        }
+        ggml_tensor* wp[4] = {&w[0], &w[1], &w[2], &w[3]};
+        ggml_tensor* bp[4] = {&b[0], &b[1], nullptr, &b[3]};  // to_value without a bias
+        const size_t before = g_nodes.size();
+        g_calls.clear();
+        ggml_tensor* bnode = ops_kd::dit_self_attention_block(&gctx, &x, wp, bp, &prm);
+        CHECK(bnode && g_nodes.size() == before + 1);
+        CHECK(bnode->ne[0] == C && bnode->ne[1] == L && bnode->ne[2] == N);
+        g_funs.back()(bnode, 0, 1, g_user.back());
+        CHECK(g_calls.size() == 1 && !strcmp(g_calls[0].fn, "self_attention_block"));
+        CHECK(same(g_block_x, x, KD_ATTN_TYPE_F32) && same(g_block_y, *bnode, KD_ATTN_TYPE_F32));
+        CHECK(g_block_w[0].type == KD_ATTN_TYPE_Q8_0 && g_block_w[3].type == KD_ATTN_TYPE_Q4_0);
+        CHECK(g_block_w[1].data == w[1].data && g_block_w[1].nb1 == w[1].nb[1] && g_block_w[1].ne[0] == C);
+        CHECK(g_block_w[0].bias == b[0].data && g_block_w[2].bias == nullptr);
+        CHECK(g_calls[0].qg == gains[0] && g_calls[0].rope == &prm.rope);
+        ggml_tensor bad = w[1];
+        bad.type = (enum ggml_type)3;  // q4_1: not a type the GEMM expands
+        ggml_tensor* wbad[4] = {&w[0], &bad, &w[2], &w[3]};
+        CHECK(ops_kd::dit_self_attention_block(&gctx, &x, wbad, bp, &prm) == nullptr);
+        ggml_tensor wsmall = make(GGML_TYPE_F16, C, 384, 1, 0x900000);  // 384 outputs: not a multiple of 256
+        ggml_tensor* wsm[4] = {&w[0], &w[1], &w[2], &wsmall};
+        CHECK(ops_kd::dit_self_attention_block(&gctx, &x, wsm, bp, &prm) == nullptr);
+    }
 
     // 7. CFG halves as one batch-2 call (pipeline.cpp:1571-1592 runs two batch-1 forwards)
     {
