@@ -370,7 +370,7 @@ def exchange_check(ctx, torch, dist, proj, out_full, rope, op, out_dt, ws, rank,
     """After the timed sharded steps, every rank's out_full must hold every rank's heads.  Each rank
     recomputes, with the single-GPU kd_attn_self_attention, its own heads and those of the next rank
     (from that rank's seed) and requires the columns of its out_full -- its own written locally,
-    the peer's written over NVLink by the peer's flash kernel -- to be bit-identical.  The verdict
+    the peer's written over NVLink by the peer's flash kernel -- to be bit-identical.  The outcome
     is min-reduced over the ranks, so every rank reports the same one."""
     checked = []
     ok = True

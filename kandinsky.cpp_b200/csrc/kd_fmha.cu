@@ -1059,12 +1059,6 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
     return cudaGetLastError();
 }
 
-template <typename T, typename TO>
-int regs_t() {
-    cudaFuncAttributes a{};
-    if (cudaFuncGetAttributes(&a, fmha_fwd_kernel<T, TO, false, false, false>) != cudaSuccess) return -1;
-    return a.numRegs;
-}
 
 }  // namespace
 
@@ -1083,15 +1077,5 @@ cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUt
     return launch_t<__half, __half>(tmQ, tmK, tmV, tmO, p, st);
 }
 
-int fmha_num_regs(OpType op, OutType ot) {
-    if (op == OpType::BF16) {
-        if (ot == OutType::F32) return regs_t<__nv_bfloat16, float>();
-        if (ot == OutType::BF16) return regs_t<__nv_bfloat16, __nv_bfloat16>();
-        return regs_t<__nv_bfloat16, __half>();
-    }
-    if (ot == OutType::F32) return regs_t<__half, float>();
-    if (ot == OutType::BF16) return regs_t<__half, __nv_bfloat16>();
-    return regs_t<__half, __half>();
-}
 
 }  // namespace kd

@@ -73,8 +73,6 @@ int fmha_smem_bytes();
 // tmK/tmV over [512, Lk, Hkv, Nkv] with a {64, 64, 1, 1} box, all 128-byte swizzled.
 cudaError_t launch_fmha512(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                            const CUtensorMap& tmV, const FmhaParams& p, cudaStream_t st);
-// Register count the compiler gave the kernel (the host refuses to launch if it is not the expected one).
-int fmha_num_regs(OpType op, OutType ot);
 
 // ---------------------------------------------------------------- prologue
 struct RopeTab {
