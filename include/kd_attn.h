@@ -400,6 +400,20 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
                                               const float* k_gain, float eps, const kd_rope3d* rope,
                                               int32_t op_type, kd_tensor* out_full, void* stream);
 
+/* DiTSelfAttention::forward (crossdit.hpp:117-154) with heads sharded over the group: rank r passes the
+ * replicated hidden states x [C, L, N] f32, ITS column shard of the Q/K/V weights (wq/wk/wv: [C, C_local],
+ * the output features of heads [r*n_head_local, (r+1)*n_head_local), C_local a multiple of 256) and the
+ * full out_layer weight wo [n_ranks*C_local, C_out].  The projection and attention of its heads run
+ * locally, the flash epilogue stores its heads into every rank's attn_full (bf16
+ * [n_ranks*C_local, L, N], contiguous, inside a kd_attn_symmetric_alloc buffer), and after the closing
+ * barrier each rank applies out_layer to the gathered output: y [C_out, L, N] on every rank.
+ * Collective (two barriers on the communicator). */
+kd_attn_status kd_attn_self_attention_block_sharded(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                                    const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                                    const float* q_gain, const float* k_gain, float eps,
+                                                    const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
+                                                    void* stream);
+
 /* The same for DiTCrossAttention::forward (crossdit.hpp:186-198): this rank's heads of the
  * visual queries against the text keys/values (column shards of k_in/v_in), no RoPE, the
  * optional mask / kv_len of kd_attn_cross_attention, every row exchanged in the flash epilogue. */

@@ -1740,9 +1740,88 @@ kd_attn_status sharded_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_te
     return rank_barrier(ctx, st);  // every rank's rows have landed in every copy
 }
 
+// DiTSelfAttention::forward with heads sharded over the group: this rank's column shard of the Q/K/V
+// weights (its n_head_local heads) projects the replicated hidden states x, the flash kernel's epilogue
+// stores this rank's heads into every rank's attn_full (the fused exchange), and after the closing
+// barrier every rank runs the out-projection on the gathered attention output -- the all-gather ->
+// out_layer order of crossdit.hpp:150-153.  Scratch: [Q][K][V operands][GEMM work].
+kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                                 const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                                 const float* q_gain, const float* k_gain, float eps,
+                                                 const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
+                                                 cudaStream_t st) {
+    kd_attn_status rc;
+    GemmInput in;
+    if ((rc = gemm_input(ctx, x, &in))) return rc;
+    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    if ((rc = check_tensor(ctx, attn_full, "attn_full"))) return rc;
+    const int R = ctx->n_ranks;
+    const int64_t Cl = wq->ne[1], C = Cl * R, L = in.L, N = in.N;
+    if (Cl % kHeadDim || wk->ne[1] != Cl || wv->ne[1] != Cl || wo->ne[0] != C)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT,
+                    "wq/wk/wv must be this rank's n_head_local * 128 output features and wo take all n_ranks of them");
+    if (attn_full->type != KD_ATTN_TYPE_BF16 || attn_full->ne[0] != C || attn_full->ne[1] != L ||
+        attn_full->ne[2] != N || attn_full->ne[3] != 1 || attn_full->nb[0] != 2 ||
+        attn_full->nb[1] != 2 * (size_t)C || attn_full->nb[2] != attn_full->nb[1] * (size_t)L)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "attn_full must be a contiguous bf16 [n_ranks * C_local, L, N]");
+    const int32_t Hl = (int32_t)(Cl / kHeadDim);
+    const int32_t op = KD_ATTN_TYPE_BF16;
+    const size_t opb = align256((size_t)N * Hl * L * kHeadDim * 2);
+    const bool rot = rope != nullptr;
+    GemmInput attn_in = in;  // the out-projection reads attn_full in place
+    attn_in.x = attn_full;
+    attn_in.K = attn_in.Kp = C;
+    attn_in.direct = true;
+    const size_t work = std::max(gemm_work_bytes(in, 3, Cl, rot), gemm_work_bytes(attn_in, 1, wo->ne[1], false));
+    if ((rc = ensure_scratch(ctx, 3 * opb + work, st))) return rc;
+    char* base = static_cast<char*>(ctx->scratch);
+    kd_tensor Qs = operand_view(base, op, L, Hl, N);
+    kd_tensor Ks = operand_view(base + opb, op, L, Hl, N);
+    kd_tensor Vs = operand_view(base + 2 * opb, op, L, Hl, N);
+    char* gw = base + 3 * opb;
+    const kd_linear* w3[3] = {wq, wk, wv};
+    kd_tensor* o3[3] = {&Qs, &Ks, &Vs};
+    if ((rc = qkv_projection_core(ctx, x, w3, q_gain, k_gain, eps, rope, op, o3, st, gw))) return rc;
+    const size_t extent = attn_full->nb[2] * (size_t)N;
+    char* peers[kMaxPeers];
+    int np = 0;
+    const char* sbase = nullptr;
+    if (R > 1) {
+        kd_attn_ctx::SymBuf* b = find_sym(ctx, attn_full->data, L * N ? extent : 0);
+        if (!b) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "attn_full must lie in a kd_attn_symmetric_alloc buffer");
+        for (int i = 0; i < R; ++i)
+            if (i != ctx->rank) peers[np++] = b->peer[i];
+        sbase = b->local;
+    }
+    kd_tensor cols = *attn_full;  // this rank's heads: columns [rank * Cl, (rank + 1) * Cl) of every copy
+    cols.data = static_cast<char*>(attn_full->data) + (size_t)ctx->rank * Cl * 2;
+    cols.ne[0] = Cl;
+    kd_tensor ov;
+    if ((rc = out_view(ctx, &cols, Hl, L, N, &ov))) return rc;
+    if ((rc = rank_barrier(ctx, st))) return rc;  // nobody still reads the previous contents of its copy
+    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)kHeadDim), nullptr, &ov, nullptr};
+    fa.out_base = sbase;
+    fa.peer_base = peers;
+    fa.n_peers = np;
+    if ((rc = flash_run(ctx, fa, st))) return rc;
+    if ((rc = rank_barrier(ctx, st))) return rc;  // every rank's heads have landed in every copy
+    return linear_core(ctx, attn_full, wo, y, st, gw);
+}
+
 }  // namespace
 
 extern "C" {
+
+kd_attn_status kd_attn_self_attention_block_sharded(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
+                                                    const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
+                                                    const float* q_gain, const float* k_gain, float eps,
+                                                    const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
+                                                    void* stream) {
+    if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    return self_attention_block_sharded_core(ctx, x, wq, wk, wv, wo, q_gain, k_gain, eps, rope, attn_full, y,
+                                             static_cast<cudaStream_t>(stream));
+}
 
 kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
                                               const kd_tensor* v_in, int32_t n_head_local, const float* q_gain,

@@ -45,6 +45,7 @@ EXPORTED = [
     "kd_attn_self_attention_sharded", "kd_attn_cross_attention_sharded", "kd_attn_attention",
     "kd_attn_selftest_wait", "kd_attn_noalloc_status", "kd_attn_noalloc_selftest_wait",
     "kd_attn_qkv_projection", "kd_attn_linear", "kd_attn_self_attention_block", "kd_attn_cross_attention_block",
+    "kd_attn_self_attention_block_sharded",
 ]
 
 # scratch held by the allocation-free entry point on each device (KD_ATTN_NOALLOC_SCRATCH_BYTES)
@@ -162,6 +163,9 @@ def _load():
     L.kd_attn_self_attention_block.restype = st
     L.kd_attn_cross_attention_block.argtypes = [P, T, T, W, W, W, W, P, P, ctypes.c_float, T, P, T, P]
     L.kd_attn_cross_attention_block.restype = st
+    L.kd_attn_self_attention_block_sharded.argtypes = [P, T, W, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D),
+                                                       T, T, P]
+    L.kd_attn_self_attention_block_sharded.restype = st
     L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
     L.kd_attn_self_attention.argtypes = [P, T, T, T, ctypes.c_int32, P, P, ctypes.c_float,
@@ -466,6 +470,17 @@ class Context:
                                                       None if rope is None else ctypes.byref(rope), int(op_type),
                                                       _ref(out_full), _stream_ptr(stream)))
         return out_full
+
+    def self_attention_block_sharded(self, x, wq, wk, wv, wo, attn_full, y, q_gain=None, k_gain=None, eps=1e-6,
+                                     rope=None, stream=None):
+        """Heads sharded over the group: x (N, L, C) f32 replicated, this rank's Q/K/V weight shards (KdLinear,
+        C_local outputs), the full wo; attn_full a symmetric bf16 (N, L, n_ranks*C_local); y (N, L, C_out)."""
+        self.check(lib.kd_attn_self_attention_block_sharded(self.handle, _ref(x), ctypes.byref(wq), ctypes.byref(wk),
+                                                            ctypes.byref(wv), ctypes.byref(wo), _ptr(q_gain),
+                                                            _ptr(k_gain), float(eps),
+                                                            None if rope is None else ctypes.byref(rope),
+                                                            _ref(attn_full), _ref(y), _stream_ptr(stream)))
+        return y
 
     def cross_attention_sharded(self, q_in, k_in, v_in, n_head_local, out_full, mask=None, kv_len=None,
                                 q_gain=None, k_gain=None, eps=1e-6, op_type=BF16, stream=None):

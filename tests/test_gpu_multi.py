@@ -159,3 +159,66 @@ def test_two_gpu_fused_exchange_matches_single_gpu(tmp_path):
             exact = oracle.self_attention(q, k, v, 8, rope_table=tab, kv_type=oracle.BF16, mode=oracle.EXACT)
             got = res[str(torch.float32)][0].numpy()
             assert_gates(got, exact, label="2-GPU fused exchange (f32 out) vs oracle")
+
+
+def _rank_main_block(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "kandinsky.cpp_b200"))
+    import kd_attn
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank), timeout=datetime.timedelta(seconds=60))
+    obj = [kd_attn.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    N, H, d, grid = 2, 8, 128, (4, 16, 16)
+    L, C = grid[0] * grid[1] * grid[2], H * d
+    Cl = C // world
+    rope = kd_attn.Rope3D.make(grid, scale=(1, 2, 2))
+    g = torch.Generator(device="cuda").manual_seed(91)      # the same weights on every rank
+    ws = [(torch.randn(C, C, device="cuda", generator=g) / 32).to(torch.float16) for _ in range(4)]
+    bs = [torch.randn(C, device="cuda", generator=g) * 0.1 for _ in range(4)]
+    gains = [1 + 0.1 * torch.randn(128, device="cuda", generator=g) for _ in range(2)]
+    res = {}
+    with kd_attn.Context(device=rank, n_ranks=world, rank=rank, nccl_id=obj[0]) as ctx:
+        x = torch.empty(N * L * C, device="cuda")
+        ctx.fill_randn(x, seed=92, offset=0)
+        x = x.view(N, L, C)
+        rows = slice(rank * Cl, (rank + 1) * Cl)              # this rank's heads' output features
+        shard = [kd_attn.KdLinear.of(ws[i][rows], kd_attn.F16, C, Cl, bs[i][rows]) for i in range(3)]
+        wo = kd_attn.KdLinear.of(ws[3], kd_attn.F16, C, C, bs[3])
+        attn_full = ctx.symmetric_tensor((N, L, C), torch.bfloat16)
+        y = torch.full((N, L, C), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+        for _ in range(2):    # the second call overwrites the first in place
+            ctx.self_attention_block_sharded(x, *shard, wo, attn_full, y, q_gain=gains[0], k_gain=gains[1], rope=rope)
+        ctx.device_status()
+        with kd_attn.Context(device=rank) as single:
+            full = [kd_attn.KdLinear.of(ws[i], kd_attn.F16, C, C, bs[i]) for i in range(4)]
+            ref = torch.empty(N, L, C, device="cuda")
+            single.self_attention_block(x, *full, ref, q_gain=gains[0], k_gain=gains[1], rope=rope)
+            single.device_status()
+        res["y"] = (y.cpu(), ref.cpu())
+        ctx.symmetric_free(attn_full)
+    torch.save(res, os.path.join(out_dir, f"block_r{rank}.pt"))
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+def test_two_gpu_sharded_block_matches_single_gpu(tmp_path):
+    """kd_attn_self_attention_block_sharded: each rank projects and attends its heads from its weight
+    shards, the exchange fills every rank's attn_full, every rank applies out_layer; each rank's y must
+    equal the single-GPU kd_attn_self_attention_block bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_rank_main_block, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        got, ref = torch.load(os.path.join(str(tmp_path), f"block_r{r}.pt"))["y"]
+        assert torch.isfinite(got).all()
+        assert torch.equal(got, ref)

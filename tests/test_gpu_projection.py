@@ -283,3 +283,22 @@ def test_cross_attention_block_matches_oracle(ctx, kd):
     assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m
     m2 = oracle.parity_metrics(y2.cpu().numpy(), got)
     assert m2["cos"] >= 0.999999 and m2["maxabs_over_rms"] <= 1e-3, m2
+
+
+def test_sharded_block_single_rank_equals_block(ctx, kd):
+    """kd_attn_self_attention_block_sharded on a one-rank context (no peers to exchange with) writes the
+    attention output into the caller's attn_full and equals kd_attn_self_attention_block bit for bit."""
+    N, grid, C = 1, (2, 8, 8), 512
+    L = int(np.prod(grid))
+    x = seeded((N, L, C), 161, 0)
+    lin = [make_weight(kd, 162, 10 * i, C, C, kd.Q8_0) for i in range(4)]
+    rope = kd.Rope3D.make(grid)
+    y = torch.empty((N, L, C), device="cuda")
+    ctx.self_attention_block(dev(x), *(l[0] for l in lin), y, rope=rope)
+    attn_full = torch.empty((N, L, C), device="cuda", dtype=torch.bfloat16)
+    y1 = torch.full((N, L, C), float("nan"), device="cuda")
+    ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), attn_full, y1, rope=rope)
+    ctx.device_status()
+    assert torch.equal(y, y1)
+    with pytest.raises(kd.KdAttnError):  # attn_full must be bf16
+        ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), attn_full.float(), y1, rope=rope)
