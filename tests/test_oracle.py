@@ -255,3 +255,19 @@ def test_qkv_projection_oracle_is_linear_then_prologue():
     yv = (x.astype(np.float64) @ w[2].T.astype(np.float64) + b[2]).astype(np.float32)
     np.testing.assert_array_equal(v, yv.reshape(N, L, H, 128).transpose(0, 2, 1, 3))
     assert k.shape == (N, H, L, 128)
+
+
+def test_dequantize_matches_ggml_python_reference():
+    """The block formats pinned a second way: gguf (ggml's own Python package, gguf-py 0.19.0 in this
+    image) dequantizes the reference converter's q8_0 / q4_0 bytes to exactly the oracle's values.  (gguf's
+    own q8_0 quantizer differs from the converter only on an all-zero block, stored with scale 0 instead of
+    1 -- both decode to zeros; the oracle follows the converter that writes the model's GGUF files.)"""
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+    g = np.load(QUANT_GOLD)
+    for case in ("rand", "heavy", "edge"):
+        K = g[f"{case}_w"].shape[1]
+        for t, gt in ((oracle.Q8_0, gguf.GGMLQuantizationType.Q8_0), (oracle.Q4_0, gguf.GGMLQuantizationType.Q4_0)):
+            raw = g[f"{case}_{'q8_0' if t == oracle.Q8_0 else 'q4_0'}"]
+            ref = quants.dequantize(raw, gt).reshape(raw.shape[0], K)
+            np.testing.assert_array_equal(oracle.dequantize(raw, t, K), ref)
