@@ -148,6 +148,25 @@ def test_flash_ext_kv_len(ctx):
     assert_gates(got[:2], exact[:2], lse=lse.cpu().numpy()[:2], lse_ref=lse_ref[:2], label="kv_len")
 
 
+@pytest.mark.parametrize("kv_type", [oracle.F16, oracle.BF16])
+def test_flash_ext_kv_len_remainders(ctx, kv_type):
+    """Valid lengths at every kind of remainder of the 128-key tile and its 16-key MMA steps (the
+    short-key kernel computes each tile's scores and P V only up to the valid keys rounded to 16)."""
+    kv_len = np.array([1, 15, 16, 17, 100, 128, 129, 200, 255, 256], np.int32)
+    N, H, Lq, Lk, D = len(kv_len), 2, 130, 256, 128
+    qf = seeded((N, H, Lq, D), 43, 0)
+    kf = seeded((N, H, Lk, D), 43, 1)
+    vf = seeded((N, H, Lk, D), 43, 2)
+    kb, vb = oracle.to_type(kf, kv_type), oracle.to_type(vf, kv_type)
+    exact, lse_ref = oracle.flash_attn_ext(qf, kb, vb, kv_len=kv_len, mode=oracle.EXACT, lse=True)
+    out = torch.full((N, Lq, H, D), 7.0, device="cuda")
+    lse = torch.empty(N, H, Lq, device="cuda")
+    ctx.flash_attn_ext(dev(qf), op_tensor(kf, kv_type), op_tensor(vf, kv_type), out,
+                       kv_len=torch.from_numpy(kv_len).cuda(), lse=lse)
+    ctx.device_status()
+    assert_gates(out.cpu().numpy(), exact, lse=lse.cpu().numpy(), lse_ref=lse_ref, label=f"kv_len remainders {kv_type}")
+
+
 def test_mask_broadcast_over_heads_and_sequences(ctx):
     """mask planes (mh, mn) broadcast as h % mh, n % mn (ggml's rule)."""
     N, H, Lq, Lk, D = 2, 4, 130, 200, 128
