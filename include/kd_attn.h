@@ -43,7 +43,7 @@ extern "C" {
 typedef enum {
     KD_ATTN_OK = 0,
     KD_ATTN_ERR_INVALID_ARGUMENT = -1, /* null pointer, inconsistent shapes or strides */
-    KD_ATTN_ERR_UNSUPPORTED = -2,      /* valid for ggml but not covered here (e.g. head_dim != 128) */
+    KD_ATTN_ERR_UNSUPPORTED = -2,      /* valid for ggml but not covered here (e.g. head_dim 96) */
     KD_ATTN_ERR_CUDA = -3,             /* a CUDA runtime call failed; see kd_attn_last_error */
     KD_ATTN_ERR_OUT_OF_MEMORY = -4,    /* context scratch could not grow */
     KD_ATTN_ERR_DEVICE_TIMEOUT = -5,   /* a bounded device-side wait expired (kd_attn_device_status) */
@@ -150,8 +150,10 @@ kd_attn_status kd_attn_selftest_wait(kd_attn_ctx* ctx, uint32_t wait_ms, void* s
  * x : [H*d, L, N] f32 (ggml [C, L, N] from to_query/to_key/to_value)
  * y : [d, L, H, N] of type f16, bf16 or f32 (the flash operand layout)
  * norm: 0 = no RMSNorm (V), 1 = RMSNorm with `gain` (device [d], NULL = unit gain)
- * rope: NULL = no rotation (cross-attention, V).  d must be even; with rope,
- *       axes_dim must sum to d and grid must multiply to L. */
+ * rope: NULL = no rotation (cross-attention, V).  With rope, axes_dim must sum
+ *       to d and grid must multiply to L.
+ * d = x.ne[0] / n_head is 128 (CrossDiT pro_video, lite_image) or 64 (lite_video:
+ * 28 heads of 1792 channels, axes {16, 24, 24}, crossdit.hpp:36,48-56). */
 kd_attn_status kd_attn_prologue(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm,
                                 const float* gain, float eps, const kd_rope3d* rope, kd_tensor* y,
                                 void* stream);
@@ -256,8 +258,10 @@ kd_attn_status kd_attn_cross_attention_block(kd_attn_ctx* ctx, const kd_tensor* 
  * lse  : NULL or device f32 [N, H, Lq], natural-log softmax denominator
  *        (ln sum_j exp(scale*q.k_j + mask_j)); -inf for fully masked rows.
  * max_bias and logit_softcap must be 0 (the only values ops.hpp:176 passes).
- * Rows whose keys are all masked produce 0.  D is 128, or 512 -- one head of a VAE mid block
- * (src/models/vae.hpp:89) -- with no mask, kv_len or tile_mask and at least one key. */
+ * Rows whose keys are all masked produce 0.  D is 128, 64 (the lite video model's
+ * heads, crossdit.hpp:36,48-56: same kernel, one 64-column box per tile), or 512 -- one
+ * head of a VAE mid block (src/models/vae.hpp:89) -- with no mask, kv_len or tile_mask
+ * and at least one key. */
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k,
                                  const kd_tensor* v, const kd_tensor* mask, float scale,
                                  float max_bias, float logit_softcap, const int32_t* kv_len,
@@ -318,17 +322,18 @@ kd_attn_status kd_attn_noalloc_selftest_wait(uint32_t wait_ms, void* stream);
  *   out-projection (crossdit.hpp:132-150 + ops.hpp:107-206).
  * Cross-attention: DiTCrossAttention::forward (crossdit.hpp:186-198 +
  *   ops.hpp:107-206), no RoPE, optional mask / kv_len.
- * q_in, k_in, v_in : [C = n_head*128, L, N] f32
+ * q_in, k_in, v_in : [C = n_head*d, L, N] f32, head dim d = 128 or 64 (as ops::attention
+ *                    derives it, q.ne[0] / n_head, ops.hpp:116); rope axes sum to d
  * op_type          : operand type, KD_ATTN_TYPE_F16 (ggml semantics) or BF16
  * out              : [C, Lq, N] f32 | bf16 */
 /* ops::attention's flash branch as it stands (ops.hpp:107-185,204-206), for
- * callers that apply no RMSNorm / RoPE first: q_in [n_head*128, Lq, N], k_in and
- * v_in [n_kv_head*128, Lk, N] (f32, n_head % n_kv_head == 0: the GQA expansion of
- * ops.hpp:135-157 is done by indexing, not by copies); Q, K and V are permuted and
- * rounded to op_type (ops.hpp:122-131,167-169, f16 in ggml), then flash attention
- * with scale 1/sqrt(128).  mask: NULL or f16 in ggml's flash orientation
+ * callers that apply no RMSNorm / RoPE first: q_in [n_head*d, Lq, N], k_in and
+ * v_in [n_kv_head*d, Lk, N] (f32, d = 128 or 64, n_head % n_kv_head == 0: the GQA
+ * expansion of ops.hpp:135-157 is done by indexing, not by copies); Q, K and V are
+ * permuted and rounded to op_type (ops.hpp:122-131,167-169, f16 in ggml), then flash
+ * attention with scale 1/sqrt(d).  mask: NULL or f16 in ggml's flash orientation
  * [>=Lk, >=Lq, mh, mn] (ops.hpp:171-174 transposes an [N, Lq, Lk] mask first; that
- * branch is never reached by the CrossDiT call sites).  out [n_head*128, Lq, N].
+ * branch is never reached by the CrossDiT call sites).  out [n_head*d, Lq, N].
  * n_head = 1 with 512 channels (packed rows, no mask) is the VAE mid-block call (vae.hpp:89):
  * head_dim 512, scale 1/sqrt(512). */
 kd_attn_status kd_attn_attention(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,
@@ -384,11 +389,11 @@ kd_attn_status kd_attn_symmetric_free(kd_attn_ctx* ctx, void* ptr, void* stream)
  * kernel: the reference runs the whole of DiTSelfAttention::forward's
  * attention (crossdit.hpp:132-150) on one device; here rank r of n computes
  * heads [r*n_head_local, (r+1)*n_head_local) from its column shard of the
- * projections (q_in, k_in, v_in: [n_head_local*128, L, N] f32) and its
+ * projections (q_in, k_in, v_in: [n_head_local*d, L, N] f32, d = 128 or 64) and its
  * flash-kernel epilogue stores every output row both into its own copy of
  * out_full and, over NVLink, into every other rank's copy, at the rank's
  * columns, so the exchange overlaps the attention math instead of following it.
- * out_full: [n_head_local*n_ranks*128, L, N] (f32 or op_type) inside a
+ * out_full: [n_head_local*n_ranks*d, L, N] (f32 or op_type) inside a
  * kd_attn_symmetric_alloc buffer, at the same offset on every rank.
  * Collective: two barriers on the communicator, one before the kernels (no rank
  * still reads the previous contents of its copy) and one after (every row has

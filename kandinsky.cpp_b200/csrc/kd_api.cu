@@ -180,13 +180,13 @@ kd_attn_status make_operand_map(kd_attn_ctx* ctx, CUtensorMap* map, const void* 
     return KD_ATTN_OK;
 }
 
-// The flash output [128, H, Lq, N] (16-bit) for TMA stores of 128-row O tiles: {64, 1, 128, 1} box,
+// The flash output [D, H, Lq, N] (16-bit) for TMA stores of 128-row O tiles: {64, 1, 128, 1} box,
 // 128-byte swizzle.  Returns false (and the kernel stores rows directly) if the driver rejects it.
-bool make_out_map(CUtensorMap* map, const void* data, int32_t type, int64_t H, int64_t Lq, int64_t N,
+bool make_out_map(CUtensorMap* map, const void* data, int32_t type, int64_t D, int64_t H, int64_t Lq, int64_t N,
                   const uint64_t nb[4]) {
     PFN_encodeTiled_t enc = get_encode();
     if (!enc || !aligned16(data)) return false;
-    cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)H, (cuuint64_t)Lq, (cuuint64_t)N};
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)Lq, (cuuint64_t)N};
     cuuint64_t strides[3] = {nb[1], nb[2], nb[3]};
     cuuint32_t box[4] = {64, 1, (cuuint32_t)kBlockM, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -396,10 +396,11 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         (rc = check_tensor(ctx, a.v, "v")) || (rc = check_tensor(ctx, a.out, "out")))
         return rc;
     const kd_tensor &q = *a.q, &k = *a.k, &v = *a.v, &o = *a.out;
-    // head_dim 128 (CrossDiT) or 512 (the VAE mid block, kd_fmha512.cu: no mask, no kv_len, no peers)
+    // head_dim 128 (CrossDiT pro and lite image), 64 (CrossDiT lite video) or 512 (the VAE mid block,
+    // kd_fmha512.cu: no mask, no kv_len, no peers)
     const int64_t D = q.ne[0];
-    if ((D != kHeadDim && D != kHeadDim512) || k.ne[0] != D || v.ne[0] != D)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 128 or 512 (q %lld, k %lld, v %lld)",
+    if ((D != kHeadDim && D != kHeadDim64 && D != kHeadDim512) || k.ne[0] != D || v.ne[0] != D)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 512 (q %lld, k %lld, v %lld)",
                     (long long)q.ne[0], (long long)k.ne[0], (long long)v.ne[0]);
     const bool d512 = D == kHeadDim512;
     if (d512 && (a.mask || a.kv_len || a.tile_mask || a.n_peers))
@@ -500,7 +501,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         cp.L = (int)Lq;
         cp.H = (int)H;
         cp.N = (int)N;
-        cp.sub = (int)(D / kHeadDim);
+        cp.D = (int)D;
         KD_CUDA(ctx, launch_convert_q(bf16 ? OpType::BF16 : OpType::F16, cp, num_sms, st));
         qdata = scr;
         qnb[1] = (uint64_t)D * 2;
@@ -554,16 +555,17 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
         KD_CUDA(ctx, launch_fmha512(bf16 ? OpType::BF16 : OpType::F16, out_type_of(o.type), tmQ, tmK, tmV, p, st));
         return KD_ATTN_OK;
     }
-    if ((rc = make_operand_map(ctx, &tmQ, qdata, bf16, Lq, H, N, qnb))) return rc;
+    if ((rc = make_operand_map(ctx, &tmQ, qdata, bf16, Lq, H, N, qnb, D))) return rc;
     if (Lk > 0) {
-        if ((rc = make_operand_map(ctx, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb))) return rc;
-        if ((rc = make_operand_map(ctx, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb))) return rc;
+        if ((rc = make_operand_map(ctx, &tmK, k.data, bf16, Lk, Hkv, Nkv, knb, D))) return rc;
+        if ((rc = make_operand_map(ctx, &tmV, v.data, bf16, Lk, Hkv, Nkv, vnb, D))) return rc;
     } else {
         tmK = tmQ;  // never dereferenced: no key tiles to visit
         tmV = tmQ;
     }
 
     FmhaParams p{};
+    p.D = (int)D;
     p.Lq = (int)Lq;
     p.Lk = (int)Lk;
     p.H = (int)H;
@@ -608,7 +610,7 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
     p.tma_out = 0;
     if (!tiled && Lk > 0 && Lk <= kQ2MaxKeys && a.n_peers == 0 &&
         (o.type == KD_ATTN_TYPE_BF16 || o.type == KD_ATTN_TYPE_F16) &&
-        make_out_map(&tmO, o.data, o.type, H, Lq, N, onb))
+        make_out_map(&tmO, o.data, o.type, D, H, Lq, N, onb))
         p.tma_out = 1;
     // abort flag and work counter start at zero for every launch
     KD_CUDA(ctx, cudaMemsetAsync(words + 1, 0, 2 * sizeof(unsigned), st));
@@ -617,10 +619,12 @@ kd_attn_status flash_run(kd_attn_ctx* ctx, const FlashArgs& a, cudaStream_t st) 
 }
 
 // ------------------------------------------------------------------ prologue core
-kd_attn_status fill_rope(kd_attn_ctx* ctx, const kd_rope3d* rope, int64_t L, RopeTab* tab) {
+// The RoPE table of one call: axes_dim must sum to the head dim D of the rotated tensors.
+kd_attn_status fill_rope(kd_attn_ctx* ctx, const kd_rope3d* rope, int64_t L, int64_t D, RopeTab* tab) {
     const int a0 = rope->axes_dim[0], a1 = rope->axes_dim[1], a2 = rope->axes_dim[2];
-    if (a0 < 0 || a1 < 0 || a2 < 0 || (a0 | a1 | a2) & 1 || a0 + a1 + a2 != kHeadDim)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope axes_dim {%d,%d,%d} must be even and sum to 128", a0, a1, a2);
+    if (a0 < 0 || a1 < 0 || a2 < 0 || (a0 | a1 | a2) & 1 || a0 + a1 + a2 != D)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope axes_dim {%d,%d,%d} must be even and sum to the head dim %lld",
+                    a0, a1, a2, (long long)D);
     const int64_t g = (int64_t)rope->grid[0] * rope->grid[1] * rope->grid[2];
     if (rope->grid[0] <= 0 || rope->grid[1] <= 0 || rope->grid[2] <= 0 || g != L)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "rope grid %dx%dx%d does not cover L = %lld", rope->grid[0],
@@ -642,18 +646,22 @@ kd_attn_status fill_rope(kd_attn_ctx* ctx, const kd_rope3d* rope, int64_t L, Rop
     return KD_ATTN_OK;
 }
 
-// Checks one prologue tensor pair and fills its kernel description.
+// Checks one prologue tensor pair and fills its kernel description.  The head dim is
+// D = x.ne[0] / n_head (as ops::attention derives it, ops.hpp:116): 128, or 64 (the lite models).
 kd_attn_status prep_prologue_tensor(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_head, int32_t norm,
-                                    const float* gain, bool rope, const kd_tensor* y, PrologueJob* t) {
+                                    const float* gain, bool rope, const kd_tensor* y, PrologueJob* t, int64_t* D_out) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, x, "x")) || (rc = check_tensor(ctx, y, "y"))) return rc;
     if (x->type != KD_ATTN_TYPE_F32) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "prologue input must be f32");
-    if (n_head <= 0 || x->ne[0] != (int64_t)n_head * kHeadDim)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x.ne[0] = %lld is not n_head * 128", (long long)x->ne[0]);
+    const int64_t D = n_head > 0 ? x->ne[0] / n_head : 0;
+    if (n_head <= 0 || (D != kHeadDim && D != kHeadDim64) || x->ne[0] != (int64_t)n_head * D)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "x.ne[0] = %lld is not n_head * 128 or n_head * 64",
+                    (long long)x->ne[0]);
     if (x->ne[3] != 1) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x must be [C, L, N] (ne[3] == 1)");
     const int64_t L = x->ne[1], N = x->ne[2];
-    if (y->ne[0] != kHeadDim || y->ne[1] != L || y->ne[2] != n_head || y->ne[3] != N)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "y must be [128, L, n_head, N]");
+    if (y->ne[0] != D || y->ne[1] != L || y->ne[2] != n_head || y->ne[3] != N)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "y must be [D, L, n_head, N]");
+    *D_out = D;
     if (L > INT32_MAX || N > INT32_MAX) return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "L or N beyond 2^31");
     uint64_t xnb[4], ynb[4];
     packed_strides(x, xnb);
@@ -702,14 +710,18 @@ kd_attn_status prologue_multi(kd_attn_ctx* ctx, const PrologueReq* req, int coun
     for (int i = 0; i < count; ++i) {
         PrologueJob t;
         const bool r = rope && req[i].rope;
-        if ((rc = prep_prologue_tensor(ctx, req[i].x, n_head, req[i].norm, req[i].gain, r, req[i].y, &t))) return rc;
+        int64_t D = 0;
+        if ((rc = prep_prologue_tensor(ctx, req[i].x, n_head, req[i].norm, req[i].gain, r, req[i].y, &t, &D)))
+            return rc;
+        if (p.D && D != p.D) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "prologue tensors of different head dims");
+        p.D = (int)D;
         if (ytype >= 0 && req[i].y->type != ytype)
             return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "prologue outputs must share one type");
         ytype = req[i].y->type;
         if (r) {
             if (rope_L >= 0 && rope_L != t.L)
                 return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "RoPE applied to tensors of different lengths");
-            if (rope_L < 0 && (rc = fill_rope(ctx, rope, t.L, &p.tab))) return rc;
+            if (rope_L < 0 && (rc = fill_rope(ctx, rope, t.L, D, &p.tab))) return rc;
             rope_L = t.L;
         }
         if ((int64_t)t.L * t.N == 0) continue;
@@ -726,33 +738,34 @@ kd_attn_status prologue_core(kd_attn_ctx* ctx, const kd_tensor* x, int32_t n_hea
     return prologue_multi(ctx, &r, 1, n_head, eps, rope, st);
 }
 
-kd_tensor operand_view(void* data, int32_t type, int64_t L, int64_t H, int64_t N) {
+kd_tensor operand_view(void* data, int32_t type, int64_t L, int64_t H, int64_t N, int64_t D = kHeadDim) {
     kd_tensor t{};
     t.data = data;
     t.type = type;
-    t.ne[0] = kHeadDim;
+    t.ne[0] = D;
     t.ne[1] = L;
     t.ne[2] = H;
     t.ne[3] = N;
     t.nb[0] = elt_size(type);
-    t.nb[1] = t.nb[0] * kHeadDim;
+    t.nb[1] = t.nb[0] * D;
     t.nb[2] = t.nb[1] * (size_t)L;
     t.nb[3] = t.nb[2] * (size_t)H;
     return t;
 }
 
-// out [C, Lq, N] viewed as the flash dst [128, H, Lq, N]
-kd_attn_status out_view(kd_attn_ctx* ctx, const kd_tensor* out, int32_t n_head, int64_t Lq, int64_t N, kd_tensor* v) {
+// out [C, Lq, N] viewed as the flash dst [D, H, Lq, N]
+kd_attn_status out_view(kd_attn_ctx* ctx, const kd_tensor* out, int32_t n_head, int64_t Lq, int64_t N, kd_tensor* v,
+                        int64_t D = kHeadDim) {
     kd_attn_status rc;
     if ((rc = check_tensor(ctx, out, "out"))) return rc;
-    if (out->ne[0] != (int64_t)n_head * kHeadDim || out->ne[1] != Lq || out->ne[2] != N || out->ne[3] != 1)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [n_head*128, Lq, N]");
+    if (out->ne[0] != (int64_t)n_head * D || out->ne[1] != Lq || out->ne[2] != N || out->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [n_head*D, Lq, N] (D = %lld)", (long long)D);
     *v = *out;
-    v->ne[0] = kHeadDim;
+    v->ne[0] = D;
     v->ne[1] = n_head;
     v->ne[2] = Lq;
     v->ne[3] = N;
-    v->nb[1] = out->nb[0] * kHeadDim;
+    v->nb[1] = out->nb[0] * D;
     v->nb[2] = out->nb[1];
     v->nb[3] = out->nb[2];
     return KD_ATTN_OK;
@@ -830,27 +843,33 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
     const int64_t Lq = q_in->ne[1], N = q_in->ne[2], Lk = k_in->ne[1];
     if (k_in->ne[2] != N || v_in->ne[1] != Lk || v_in->ne[2] != N || v_in->ne[0] != k_in->ne[0])
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
-    // K/V heads: k_in->ne[0] / 128, a divisor of n_head (grouped-query attention, ops.hpp:135-157)
-    if (k_in->ne[0] % kHeadDim)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k_in.ne[0] = %lld is not a multiple of 128", (long long)k_in->ne[0]);
-    const int64_t n_kv_head = k_in->ne[0] / kHeadDim;
+    // head dim D = q_in.ne[0] / n_head (ops.hpp:116): 128, or 64 for the lite models
+    const int64_t D = n_head > 0 ? q_in->ne[0] / n_head : 0;
+    if (n_head <= 0 || (D != kHeadDim && D != kHeadDim64) || q_in->ne[0] != (int64_t)n_head * D)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "q_in.ne[0] = %lld is not n_head * 128 or n_head * 64",
+                    (long long)q_in->ne[0]);
+    // K/V heads: k_in->ne[0] / D, a divisor of n_head (grouped-query attention, ops.hpp:135-157)
+    if (k_in->ne[0] % D)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "k_in.ne[0] = %lld is not a multiple of %lld", (long long)k_in->ne[0],
+                    (long long)D);
+    const int64_t n_kv_head = k_in->ne[0] / D;
     if (n_kv_head <= 0 || n_head % n_kv_head)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "invalid GQA ratio n_head=%d n_kv_head=%lld", n_head,
                     (long long)n_kv_head);
     kd_tensor ov;
-    if ((rc = out_view(ctx, out, n_head, Lq, N, &ov))) return rc;
+    if ((rc = out_view(ctx, out, n_head, Lq, N, &ov, D))) return rc;
     const size_t es = 2;
-    const size_t qb = align256((size_t)N * n_head * Lq * kHeadDim * es);
-    const size_t kb = align256((size_t)N * n_kv_head * Lk * kHeadDim * es);
+    const size_t qb = align256((size_t)N * n_head * Lq * D * es);
+    const size_t kb = align256((size_t)N * n_kv_head * Lk * D * es);
     // operand scratch sits after the flash core's own scratch needs: reserve them up front
     const size_t flash_extra =
         mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
     if ((rc = ensure_scratch(ctx, flash_extra + qb + 2 * kb, st))) return rc;
     // The flash core carves its scratch from the start of the buffer; operands go after it.
     char* base = static_cast<char*>(ctx->scratch) + flash_extra;
-    kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N);
-    kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_kv_head, N);
-    kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_kv_head, N);
+    kd_tensor Qs = operand_view(base, op_type, Lq, n_head, N, D);
+    kd_tensor Ks = operand_view(base + qb, op_type, Lk, n_kv_head, N, D);
+    kd_tensor Vs = operand_view(base + qb + kb, op_type, Lk, n_kv_head, N, D);
     const int32_t nq = norm_qk ? 1 : 0;
     if (n_kv_head == n_head) {
         const PrologueReq req[3] = {{q_in, nq, q_gain, true, &Qs}, {k_in, nq, k_gain, true, &Ks},
@@ -862,7 +881,7 @@ kd_attn_status attention_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_
         if ((rc = prologue_multi(ctx, rq, 1, n_head, eps, rope, st))) return rc;
         if ((rc = prologue_multi(ctx, rkv, 2, (int32_t)n_kv_head, eps, rope, st))) return rc;
     }
-    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, lse};
+    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)D), kv_len, &ov, lse};
     fa.out_base = out_base;
     fa.peer_base = peer_base;
     fa.n_peers = n_peers;
@@ -921,10 +940,11 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     for (const kd_tensor* t : {k_in, v_in})
         if (t->ne[0] != C || t->ne[1] != L || t->ne[2] != N || t->ne[3] != 1)
             return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "q_in/k_in/v_in shapes disagree");
-    if (n_head <= 0 || C != (int64_t)n_head * kHeadDim || q_in->ne[3] != 1)
-        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "inputs must be [n_head*128, L, N]");
+    const int64_t D = n_head > 0 ? C / n_head : 0;  // head dim: 128, or 64
+    if (n_head <= 0 || (D != kHeadDim && D != kHeadDim64) || C != (int64_t)n_head * D || q_in->ne[3] != 1)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "inputs must be [n_head*128, L, N] or [n_head*64, L, N]");
     if (out->ne[0] != C || out->ne[1] != L || out->ne[2] != N || out->ne[3] != 1)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [n_head*128, L, N]");
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out must be [C, L, N] like the inputs");
     if (out->type != KD_ATTN_TYPE_F32 && out->type != op_type)
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out must be f32 or the operand type");
     if (L * N == 0) return KD_ATTN_OK;
@@ -946,12 +966,12 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
         rest -= part;
     }
     const int groups = (int)sizes.size();
-    const size_t in_w = (size_t)G * kHeadDim * 4;                  // bytes per row of one input slab (max)
+    const size_t in_w = (size_t)G * D * 4;                  // bytes per row of one input slab (max)
     const size_t out_es = elt_size(out->type);
-    const size_t out_w = (size_t)G * kHeadDim * out_es;
+    const size_t out_w = (size_t)G * D * out_es;
     const size_t in_slab = align256(in_w * (size_t)(L * N));
     const size_t out_slab = align256(out_w * (size_t)(L * N));
-    const size_t opb = align256((size_t)N * G * L * kHeadDim * 2);  // one operand for one group
+    const size_t opb = align256((size_t)N * G * L * D * 2);  // one operand for one group
     const size_t core = 3 * opb;                                     // attention_core's operand scratch
     if ((rc = ensure_copy_streams(ctx))) return rc;
     if ((rc = ensure_scratch(ctx, core + 2 * (3 * in_slab + out_slab), st))) return rc;
@@ -968,11 +988,11 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
     for (int g = 0; g < groups; head0 += sizes[g], ++g) {
         const int b = g & 1;
         const int gh = sizes[g];                                       // heads in this group
-        const size_t gin_w = (size_t)gh * kHeadDim * 4, gout_w = (size_t)gh * kHeadDim * out_es;
+        const size_t gin_w = (size_t)gh * D * 4, gout_w = (size_t)gh * D * out_es;
         // inputs of group g go into slab b once group g-2's compute has finished with it
         if (g >= 2) KD_CUDA(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_done[b], 0));
         for (int x = 0; x < 3; ++x)
-            if ((rc = copy_columns(ctx, ins[x], (size_t)head0 * kHeadDim * 4, gin_w, in_buf(b, x), true, ctx->h2d)))
+            if ((rc = copy_columns(ctx, ins[x], (size_t)head0 * D * 4, gin_w, in_buf(b, x), true, ctx->h2d)))
                 return rc;
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_in[b], ctx->h2d));
         // compute group g on the caller's stream; its output slab must have been copied out (group g-2)
@@ -982,14 +1002,14 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
         for (int x = 0; x < 3; ++x) {
             xs[x] = *ins[x];
             xs[x].data = in_buf(b, x);
-            xs[x].ne[0] = (int64_t)gh * kHeadDim;
+            xs[x].ne[0] = (int64_t)gh * D;
             xs[x].nb[1] = gin_w;
             xs[x].nb[2] = gin_w * (size_t)L;
             xs[x].nb[3] = xs[x].nb[2] * (size_t)N;
         }
         os = *out;
         os.data = out_buf(b);
-        os.ne[0] = (int64_t)gh * kHeadDim;
+        os.ne[0] = (int64_t)gh * D;
         os.nb[1] = gout_w;
         os.nb[2] = gout_w * (size_t)L;
         os.nb[3] = os.nb[2] * (size_t)N;
@@ -999,7 +1019,7 @@ kd_attn_status self_attention_host(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_done[b], st));
         // copy group g's heads out into their columns of the host output
         KD_CUDA(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_done[b], 0));
-        if ((rc = copy_columns(ctx, out, (size_t)head0 * kHeadDim * out_es, gout_w, out_buf(b), false, ctx->d2h)))
+        if ((rc = copy_columns(ctx, out, (size_t)head0 * D * out_es, gout_w, out_buf(b), false, ctx->d2h)))
             return rc;
         KD_CUDA(ctx, cudaEventRecord(ctx->ev_out[b], ctx->d2h));
     }
@@ -1194,7 +1214,7 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
     p.C = (int)C;
     RopeTab tab{};
     const bool rot = rope && (p.slot[0].rope || (p.nslots > 1 && p.slot[1].rope));
-    if (rot && (rc = fill_rope(ctx, rope, L, &tab))) return rc;
+    if (rot && (rc = fill_rope(ctx, rope, L, kHeadDim, &tab))) return rc;
     if (L * N == 0) return KD_ATTN_OK;
     if (!work) {
         if ((rc = ensure_scratch(ctx, gemm_work_bytes(in, p.nslots, C, rot), st))) return rc;
@@ -1709,11 +1729,13 @@ kd_attn_status sharded_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_te
                             const kd_rope3d* rope, const kd_tensor* mask, const int32_t* kv_len, int32_t op_type,
                             kd_tensor* out_full, cudaStream_t st) {
     kd_attn_status rc;
-    if ((rc = check_tensor(ctx, out_full, "out_full"))) return rc;
+    if ((rc = check_tensor(ctx, out_full, "out_full")) || (rc = check_tensor(ctx, q_in, "q_in"))) return rc;
     const int R = ctx->n_ranks;
-    const int64_t C = (int64_t)n_head_local * R * kHeadDim;
+    // head dim D = q_in.ne[0] / n_head_local (128, or 64; attention_core checks it)
+    const int64_t D = n_head_local > 0 ? q_in->ne[0] / n_head_local : 0;
+    const int64_t C = (int64_t)n_head_local * R * D;
     if (n_head_local <= 0 || out_full->ne[0] != C || out_full->ne[3] != 1)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out_full must be [n_head_local * n_ranks * 128, L, N]");
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "out_full must be [n_head_local * n_ranks * D, L, N]");
     const size_t es = elt_size(out_full->type);
     if (out_full->nb[0] != es || out_full->nb[2] < out_full->nb[1] * (size_t)out_full->ne[1])
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "out_full rows must be contiguous and sequences not overlapping");
@@ -1729,10 +1751,10 @@ kd_attn_status sharded_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_te
             if (i != ctx->rank) peers[np++] = b->peer[i];
         base = b->local;
     }
-    // this rank's heads are columns [rank * n_head_local * 128, +n_head_local * 128) of every copy
+    // this rank's heads are columns [rank * n_head_local * D, +n_head_local * D) of every copy
     kd_tensor cols = *out_full;
-    cols.data = static_cast<char*>(out_full->data) + (size_t)ctx->rank * n_head_local * kHeadDim * es;
-    cols.ne[0] = (int64_t)n_head_local * kHeadDim;
+    cols.data = static_cast<char*>(out_full->data) + (size_t)ctx->rank * n_head_local * D * es;
+    cols.ne[0] = (int64_t)n_head_local * D;
     if ((rc = rank_barrier(ctx, st))) return rc;  // nobody still reads the previous contents
     if ((rc = attention_core(ctx, q_in, k_in, v_in, n_head_local, q_gain, k_gain, eps, rope, mask, kv_len, op_type,
                              &cols, nullptr, st, base, peers, np)))

@@ -91,6 +91,11 @@ constexpr int kListConsumers = 32 + 32 + 2 * kBlockM;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8 between rescales
+// The short-key instantiation rescales whenever the running maximum grows: a unit there sees one or two
+// K/V tiles, and a P taken against a stale maximum leaves the row's largest weight > 1 and rounded to
+// the operand type instead of exactly 1 -- on peaked rows (a few dominant keys, as against text states)
+// that rounding is most of the output error.
+constexpr float kRescaleThresholdQ2 = 0.0f;
 // Tuning knobs (compile-time):
 //   KD_FMHA_POLY_PAIRS: bit i set = score pair i of each 32-key chunk takes exp2 from the
 //                       FMA pipe (exp2_poly) instead of MUFU ex2 (0 = all MUFU).
@@ -172,7 +177,7 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v
                           Pack2<__half>::pack(v[8 * i + 6], v[8 * i + 7]));
 }
 
-template <typename T, typename TO, bool kSparse, bool kPairs, bool kQ2>
+template <typename T, typename TO, bool kSparse, bool kPairs, bool kQ2, int kD>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -190,6 +195,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const DevCtl ctl{p.err, p.abort_flag, p.wait_ns};
+    // Head dim kD = 128, or 64: then only the first 64-column box of every Q/K/V tile is loaded, the S
+    // MMAs take 4 K-steps, the PV MMAs N = 64 (O_i's first 64 TMEM columns) and rows are 64 wide.
+    static_assert(kD == kHeadDim || kD == kHeadDim64, "head dim 128 or 64");
+    constexpr int nbox = kD / 64;
     // Units: normally 256 query rows (Q tiles 0, 1) of one head; in head-pair mode (masked kernel,
     // one mask plane for all heads) the same 128 rows of heads 2hp and 2hp + 1, which need exactly
     // the same K/V tiles, so both Q tiles always have work at every listed tile.
@@ -306,13 +315,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             !__all_sync(0xffffffffu, mbar_wait(&q_empty[qb], (q_uses / kQBufs - 1) & 1, ctl, kErrTimeoutQ)))
             return false;
         if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full[qb], kQTiles * kTileBytes);
+            mbar_arrive_expect_tx(&q_full[qb], kQTiles * nbox * kBoxBytes);
 #pragma unroll
             for (int i = 0; i < kQTiles; ++i)
 #pragma unroll
                 for (int bx = 0; bx < 2; ++bx)
-                    tma_load_4d(smem + kSmemQ + (qb * kQTiles + i) * kTileBytes + bx * kBoxBytes, &tmQ, &q_full[qb],
-                                bx * 64, ug.row0[i], ug.head[i], ug.n);
+                    if (bx < nbox)
+                        tma_load_4d(smem + kSmemQ + (qb * kQTiles + i) * kTileBytes + bx * kBoxBytes, &tmQ,
+                                    &q_full[qb], bx * 64, ug.row0[i], ug.head[i], ug.n);
         }
         __syncwarp();
         ++q_uses;
@@ -458,12 +468,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = __all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ph ^ 1u, ctl, kErrTimeoutKVEmpty));
                         if (!ok) break;
                         if (lane == 0) {
-                            mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+                            mbar_arrive_expect_tx(&kv_full[s], nbox * kBoxBytes);
                             const CUtensorMap* map = is_v ? &tmV : &tmK;
 #pragma unroll
                             for (int bx = 0; bx < 2; ++bx)
-                                tma_load_4d(smem + kSmemKV + s * kTileBytes + bx * kBoxBytes, map, &kv_full[s],
-                                            bx * 64, kt * kBlockN, hk, nk);
+                                if (bx < nbox)
+                                    tma_load_4d(smem + kSmemKV + s * kTileBytes + bx * kBoxBytes, map, &kv_full[s],
+                                                bx * 64, kt * kBlockN, hk, nk);
                         }
                         __syncwarp();
                         ++it;
@@ -485,7 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t qa = smem_u32(smem + kSmemQ);
         const uint32_t kva = smem_u32(smem + kSmemKV);
         constexpr uint32_t idS = idesc_f16_f32acc(kBf16, kBlockM, kBlockN, false);
-        constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kHeadDim, true);
+        // PV's N is the head dim: O_i's first D columns
+        constexpr uint32_t idPV = idesc_f16_f32acc(kBf16, kBlockM, kD, true);
         uint32_t it = 0;       // K/V ring position
         uint32_t units = 0;    // units with at least one tile: Q buffer units % kQBufs and its phase
         bool issued = false;
@@ -504,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t alo = sw128_desc_lo(qa + (qb * kQTiles + i) * kTileBytes, 16),
                            blo = sw128_desc_lo(kva + s * kTileBytes, 16);
 #pragma unroll
-            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            for (int kk = 0; kk < kD / 16; ++kk) {
                 const uint32_t o = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
                 mma_ss(tmem + i * 128, desc_join(alo + o, dhi), desc_join(blo + o, dhi), idS, kk > 0 ? 1u : 0u);
             }
@@ -721,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // or two (16-bit) whole rows: NVLink sees full contiguous rows, and the softmax warps never
         // wait on remote memory.
         if (p.n_peer_out) {
-            constexpr int kChunks = kHeadDim * (int)sizeof(TO) / 16;  // 16-byte chunks per row
+            constexpr int kChunks = kD * (int)sizeof(TO) / 16;  // 16-byte chunks per row (8 to 32)
             constexpr int kRowsPerInstr = 32 / kChunks;
             constexpr int kBatch = 8;                                  // instructions of loads in flight
             const int chunk = lane % kChunks, sub = lane / kChunks;
@@ -859,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
                 const float m_tile = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
                 const float m_new = fmaxf(m, m_tile);
-                const bool resc = m_new > m + kRescaleThreshold;
+                const bool resc = m_new > m + (kQ2 ? kRescaleThresholdQ2 : kRescaleThreshold);
                 const bool warp_resc = __any_sync(0xffffffffu, resc);
                 float alpha = 1.0f;
                 if (resc) {
@@ -988,7 +1000,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (r == 0) {
                             const int row0 = wg ? ug.row0[1] : ug.row0[0];
 #pragma unroll
-                            for (int bx = 0; bx < 2; ++bx) tma_store_4d(&tmO, stg + bx * kBoxBytes, bx * 64, h, row0, n);
+                            for (int bx = 0; bx < 2; ++bx)
+                                if (bx < nbox) tma_store_4d(&tmO, stg + bx * kBoxBytes, bx * 64, h, row0, n);
                             bulk_commit_group();
                             bulk_wait_group_read0();  // the staging tile has been read: the Q buffer may refill
                             mbar_arrive(&q_empty[qb_unit]);
@@ -999,6 +1012,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (orow) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
+                        if (c * 32 >= kD) break;
                         float v[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[c * 32 + i]) * inv;
@@ -1013,7 +1027,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) z[i] = 0.f;
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) store_row32<TO>(orow + c * 32, z);
+                for (int c = 0; c < kD / 32; ++c) store_row32<TO>(orow + c * 32, z);
             }
             if (row_valid && p.lse)
                 p.lse[((long long)n * p.H + h) * p.Lq + qrow] = (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
@@ -1033,16 +1047,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <typename T, typename TO>
+template <typename T, typename TO, int kD>
 cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const CUtensorMap& tmO,
                      const FmhaParams& p, cudaStream_t st) {
     // a mask (tile classes) selects the instantiation that skips K/V tiles per Q tile
     // head-pair units when every head shares one mask plane (p.head_pairs, set by the host)
     // without a mask, a short key sequence selects the double-buffered-Q instantiation
     const bool q2 = !p.tile_cls && p.Lk <= kQ2MaxKeys;
-    auto kern = p.tile_cls ? (p.head_pairs ? fmha_fwd_kernel<T, TO, true, true, false>
-                                           : fmha_fwd_kernel<T, TO, true, false, false>)
-                           : (q2 ? fmha_fwd_kernel<T, TO, false, false, true> : fmha_fwd_kernel<T, TO, false, false, false>);
+    auto kern = p.tile_cls ? (p.head_pairs ? fmha_fwd_kernel<T, TO, true, true, false, kD>
+                                           : fmha_fwd_kernel<T, TO, true, false, false, kD>)
+                           : (q2 ? fmha_fwd_kernel<T, TO, false, false, true, kD>
+                                 : fmha_fwd_kernel<T, TO, false, false, false, kD>);
     // set on every launch: the attribute belongs to the current device, and the call is cheap
     const int smem_bytes = p.tile_cls ? Layout<true>::kSmemAlloc
                                       : (q2 ? Layout<false, true>::kSmemAlloc : Layout<false>::kSmemAlloc);
@@ -1060,21 +1075,28 @@ cudaError_t launch_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
 }
 
 
+template <int kD>
+cudaError_t launch_d(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                     const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st) {
+    if (op == OpType::BF16) {
+        if (ot == OutType::F32) return launch_t<__nv_bfloat16, float, kD>(tmQ, tmK, tmV, tmO, p, st);
+        if (ot == OutType::BF16) return launch_t<__nv_bfloat16, __nv_bfloat16, kD>(tmQ, tmK, tmV, tmO, p, st);
+        return launch_t<__nv_bfloat16, __half, kD>(tmQ, tmK, tmV, tmO, p, st);
+    }
+    if (ot == OutType::F32) return launch_t<__half, float, kD>(tmQ, tmK, tmV, tmO, p, st);
+    if (ot == OutType::BF16) return launch_t<__half, __nv_bfloat16, kD>(tmQ, tmK, tmV, tmO, p, st);
+    return launch_t<__half, __half, kD>(tmQ, tmK, tmV, tmO, p, st);
+}
+
 }  // namespace
 
 int fmha_smem_bytes() { return Layout<true>::kSmemAlloc; }
 
-
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                         const CUtensorMap& tmV, const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st) {
-    if (op == OpType::BF16) {
-        if (ot == OutType::F32) return launch_t<__nv_bfloat16, float>(tmQ, tmK, tmV, tmO, p, st);
-        if (ot == OutType::BF16) return launch_t<__nv_bfloat16, __nv_bfloat16>(tmQ, tmK, tmV, tmO, p, st);
-        return launch_t<__nv_bfloat16, __half>(tmQ, tmK, tmV, tmO, p, st);
-    }
-    if (ot == OutType::F32) return launch_t<__half, float>(tmQ, tmK, tmV, tmO, p, st);
-    if (ot == OutType::BF16) return launch_t<__half, __nv_bfloat16>(tmQ, tmK, tmV, tmO, p, st);
-    return launch_t<__half, __half>(tmQ, tmK, tmV, tmO, p, st);
+    if (p.D == kHeadDim64) return launch_d<kHeadDim64>(op, ot, tmQ, tmK, tmV, tmO, p, st);
+    if (p.D != kHeadDim) return cudaErrorInvalidValue;
+    return launch_d<kHeadDim>(op, ot, tmQ, tmK, tmV, tmO, p, st);
 }
 
 

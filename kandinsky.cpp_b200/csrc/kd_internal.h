@@ -14,6 +14,7 @@ enum : uint8_t { kTileSkip = 0, kTileFull = 1, kTileMixed = 2 };
 
 // Flash-attention forward geometry (sm_100a kernel in kd_fmha.cu).
 constexpr int kHeadDim = 128;
+constexpr int kHeadDim64 = 64;    // the lite video model's head (axes 16 + 24 + 24): kd_fmha.cu at D = 64
 constexpr int kHeadDim512 = 512;  // the VAE mid-block head (kd_fmha512.cu)
 constexpr int kBlockM = 128;   // query rows per Q tile = one M=128 tcgen05 MMA
 constexpr int kQTiles = 2;     // Q tiles per CTA, one softmax warpgroup each
@@ -30,6 +31,7 @@ constexpr int kMaxPeers = 7;       // other ranks an output row is also written 
 constexpr int kQ2MaxKeys = KD_FMHA_Q2_MAX_KEYS;
 
 struct FmhaParams {
+    int D;                   // head dim: 128, or 64 (the lite models' heads)
     int Lq, Lk, H, N;        // query rows, keys, heads, sequences
     int rk2, rk3;            // H / Hkv, N / Nkv (ggml broadcast ratios)
     float scale_log2;        // scale * log2(e)
@@ -63,8 +65,8 @@ enum class OpType { F16, BF16 };
 enum class OutType { F32, F16, BF16 };
 
 // Launches the tcgen05 flash-attention forward.  tmQ/tmK/tmV are 4-D tiled
-// tensor maps over [128, L, heads, seqs] with a {64, 128, 1, 1} box and
-// 128-byte swizzle; tmO (read only when p.tma_out) maps `out` as [128, H, Lq, N]
+// tensor maps over [D, L, heads, seqs] with a {64, 128, 1, 1} box and
+// 128-byte swizzle; tmO (read only when p.tma_out) maps `out` as [D, H, Lq, N]
 // with a {64, 1, 128, 1} box (the same 128 rows of 128 bytes in shared memory) and swizzle.
 cudaError_t launch_fmha(OpType op, OutType ot, const CUtensorMap& tmQ, const CUtensorMap& tmK,
                         const CUtensorMap& tmV, const CUtensorMap& tmO, const FmhaParams& p, cudaStream_t st);
@@ -76,19 +78,19 @@ cudaError_t launch_fmha512(OpType op, OutType ot, const CUtensorMap& tmQ, const 
 
 // ---------------------------------------------------------------- prologue
 struct RopeTab {
-    float freq[64];          // per rotary pair: theta^(-i/half_axis), computed like rope.hpp:23-29
+    float freq[64];          // per rotary pair (D/2 of them): theta^(-i/half_axis), computed like rope.hpp:23-29
     float div[64];           // scale_factor of the pair's axis
     unsigned char axis[64];  // 0 = t, 1 = h, 2 = w
     int grid_h, grid_w;      // token -> (t,h,w): t = l/(gh*gw), h = (l/gw)%gh, w = l%gw
 };
 
-// One projection handled by the prologue: x [C = H*128, L, N] f32 -> y [128, L, H, N].
+// One projection handled by the prologue: x [C = H*D, L, N] f32 -> y [D, L, H, N].
 struct PrologueJob {
     const float* x;          // dim 0 contiguous
     long long x_nb1, x_nb2;  // byte strides of x (token, sequence)
     void* y;
     long long y_nb1, y_nb2, y_nb3;  // byte strides of y (row, head, sequence)
-    const float* gain;       // [128] or null (unit gain); used when norm
+    const float* gain;       // [D] or null (unit gain); used when norm
     int norm;                // 1: RMSNorm
     int rope;                // 1: apply RoPE with the shared table
     int L, N, H;
@@ -100,18 +102,19 @@ constexpr int kPrologueHeads = 8;  // heads per warp item (8 row loads in flight
 struct PrologueParams {
     PrologueJob job[kPrologueMaxJobs];
     int njobs;
+    int D;                   // head dim of every job: 128, or 64 (two heads per 128-element warp row)
     float eps;
     RopeTab tab;             // shared by every projection with rope = 1
 };
 cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cudaStream_t st);
 
-// Rounds a strided [128, L, H, N] f32/f16/bf16 tensor to the operand type, contiguous.
+// Rounds a strided [D, L, H, N] f32/f16/bf16 tensor to the operand type, contiguous.
 struct ConvertParams {
     const void* src; int src_type;   // kd_attn_type id
     long long nb1, nb2, nb3;
-    void* dst;                       // contiguous [128 * sub, L, H, N]
+    void* dst;                       // contiguous [D, L, H, N]
     int L, H, N;
-    int sub;                         // 128-element pieces per row (1, or 4 for head_dim 512)
+    int D;                           // row width: 64, 128 or 512
 };
 cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st);
 

@@ -32,15 +32,16 @@ __device__ __forceinline__ void store4<__half>(void* dst, float a, float b, floa
 
 __device__ __forceinline__ float pick_pos(int axis, int t, int h, int w) { return (float)(axis == 0 ? t : (axis == 1 ? h : w)); }
 
-// RMSNorm over one 128-wide head row held as one float4 per lane, following
-// ggml's CPU rms_norm: squares formed in float, summed in double, mean
+// RMSNorm over one head row of D elements held as one float4 per lane in D/4 consecutive lanes (all
+// 32 lanes call it), following ggml's CPU rms_norm: squares formed in float, summed in double, mean
 // rounded to float, scale = 1/sqrtf(mean + eps), y = x*scale*g.
+template <int D>
 __device__ __forceinline__ float4 rms_norm_row(float4 x, float4 g, float eps) {
     double ss = (double)__fmul_rn(x.x, x.x) + (double)__fmul_rn(x.y, x.y) + (double)__fmul_rn(x.z, x.z) +
                 (double)__fmul_rn(x.w, x.w);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float mean = (float)(ss * (1.0 / kHeadDim));
+    for (int o = D / 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean = (float)(ss * (1.0 / D));  // 1/D is exact: D is a power of two
     const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
     return make_float4(__fmul_rn(__fmul_rn(x.x, scale), g.x), __fmul_rn(__fmul_rn(x.y, scale), g.y),
                        __fmul_rn(__fmul_rn(x.z, scale), g.z), __fmul_rn(__fmul_rn(x.w, scale), g.w));
@@ -55,40 +56,53 @@ __device__ __forceinline__ float4 rope_row(float4 x, float s0, float c0, float s
 
 // blockIdx.y selects the projection (its parameters stay in registers for the
 // whole loop); one warp per (sequence n, token l, group of kPrologueHeads
-// heads) of it, all of the group's row loads issued before any arithmetic.
-// Lane owns elements 4*lane .. 4*lane+3 of each 128-wide head row, i.e.
-// rotary pairs 2*lane and 2*lane+1, whose angle depends only on the token:
-// sin/cos are computed once per token and reused for the group's heads.  The
-// angle is pos * freq / scale_factor as rope.hpp:78-95 computes it.
+// warp rows) of it, all of the group's row loads issued before any arithmetic.
+// A warp row is 128 consecutive elements of x: one head of 128, or two heads of
+// 64 (lanes 0-15 and 16-31).  A lane owns elements 4*hl .. 4*hl+3 of its head
+// (hl = lane within the head), i.e. rotary pairs 2*hl and 2*hl+1, whose angle
+// depends only on the token: sin/cos are computed once per token and reused
+// for the group's heads.  The angle is pos * freq / scale_factor as
+// rope.hpp:78-95 computes it.
 // (Q, K and V of one token in one item, sharing sin/cos between Q and K, was
 // measured slower: 12 rows per item needs 104 registers and halves occupancy.)
-template <typename TO>
+template <typename TO, int D>
 __global__ void __launch_bounds__(256) prologue_kernel(const __grid_constant__ PrologueParams p) {
     const int lane = threadIdx.x & 31;
+    constexpr int lph = D / 4;           // lanes per head: 32 or 16
+    constexpr int hpr = 128 / D;         // heads per warp row: 1 or 2
+    const int hl = lane & (lph - 1);     // lane within its head
+    const int sub = lane / lph;          // head within the warp row
     // per-lane RoPE constants, read from the parameter bank once (not per row)
-    const float fr0 = p.tab.freq[2 * lane], fr1 = p.tab.freq[2 * lane + 1];
-    const float dv0 = p.tab.div[2 * lane], dv1 = p.tab.div[2 * lane + 1];
-    const int ax0 = p.tab.axis[2 * lane], ax1 = p.tab.axis[2 * lane + 1];
+    const float fr0 = p.tab.freq[2 * hl], fr1 = p.tab.freq[2 * hl + 1];
+    const float dv0 = p.tab.div[2 * hl], dv1 = p.tab.div[2 * hl + 1];
+    const int ax0 = p.tab.axis[2 * hl], ax1 = p.tab.axis[2 * hl + 1];
     const PrologueJob& T = p.job[blockIdx.y];
     float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (T.norm && T.gain) g = __ldg(reinterpret_cast<const float4*>(T.gain) + lane);
+    if (T.norm && T.gain) g = __ldg(reinterpret_cast<const float4*>(T.gain) + hl);
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    const int hgroups = (T.H + kPrologueHeads - 1) / kPrologueHeads;
+    const int wrows = (T.H + hpr - 1) / hpr;  // warp rows per token
+    const int hgroups = (wrows + kPrologueHeads - 1) / kPrologueHeads;
     const long long items = (long long)T.N * T.L * hgroups;
     for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
         const int hg = (int)(it % hgroups);
         const long long nl = it / hgroups;
         const int l = (int)(nl % T.L);
         const int n = (int)(nl / T.L);
-        const int h0 = hg * kPrologueHeads;
-        const int nh = min(kPrologueHeads, T.H - h0);
+        const int r0 = hg * kPrologueHeads;               // first warp row of the item
+        const int nr = min(kPrologueHeads, wrows - r0);
+        const int h0 = r0 * hpr + sub;                    // this lane's head in warp row 0
         const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(T.x) +
                                                             (long long)n * T.x_nb2 + (long long)l * T.x_nb1) +
-                            (h0 * kHeadDim) / 4 + lane;
+                            r0 * 32 + lane;
+        // head of warp row j present (with two heads per row, an odd head count leaves the second
+        // half of the last row empty: zeros, normalised beside the others, never stored)
+        auto present = [&](int j) { return hpr == 1 || h0 + j * hpr < T.H; };
         float4 v[kPrologueHeads];
 #pragma unroll
-        for (int j = 0; j < kPrologueHeads; ++j)
-            if (j < nh) v[j] = __ldcs(src + j * (kHeadDim / 4));
+        for (int j = 0; j < kPrologueHeads; ++j) {
+            if (hpr > 1) v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (j < nr && present(j)) v[j] = __ldcs(src + j * 32);
+        }
         float s0 = 0.f, c0 = 1.f, s1 = 0.f, c1 = 1.f;
         if (T.rope) {
             const int hw = p.tab.grid_h * p.tab.grid_w;
@@ -97,14 +111,14 @@ __global__ void __launch_bounds__(256) prologue_kernel(const __grid_constant__ P
             sincosf(__fdiv_rn(__fmul_rn(pick_pos(ax1, t, hh, w), fr1), dv1), &s1, &c1);
         }
         char* dst = reinterpret_cast<char*>(T.y) + (long long)n * T.y_nb3 + (long long)h0 * T.y_nb2 +
-                    (long long)l * T.y_nb1 + (long long)lane * 4 * sizeof(TO);
+                    (long long)l * T.y_nb1 + (long long)hl * 4 * sizeof(TO);
 #pragma unroll
         for (int j = 0; j < kPrologueHeads; ++j) {
-            if (j >= nh) break;
+            if (j >= nr) break;
             float4 x = v[j];
-            if (T.norm) x = rms_norm_row(x, g, p.eps);
+            if (T.norm) x = rms_norm_row<D>(x, g, p.eps);
             if (T.rope) x = rope_row(x, s0, c0, s1, c1);
-            store4<TO>(dst + (long long)j * T.y_nb2, x.x, x.y, x.z, x.w);
+            if (present(j)) store4<TO>(dst + (long long)j * hpr * T.y_nb2, x.x, x.y, x.z, x.w);
         }
     }
 }
@@ -116,27 +130,31 @@ __device__ __forceinline__ float load_elt(const void* base, long long idx, int t
     return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
-// One warp per 128-element piece of a row (p.sub pieces per row); the source row is contiguous
-// (nb0 = element size), so piece j of row l starts 128 * j elements into it.
+// One warp per piece of a row -- the whole row for D = 64 or 128 (4 elements per lane), 128 elements
+// for D = 512; the source row is contiguous (nb0 = element size), so piece j starts 128 * j elements
+// into it.
 template <typename TD>
 __global__ void __launch_bounds__(256) convert_q_kernel(const ConvertParams p) {
     const int lane = threadIdx.x & 31;
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    const long long lsub = (long long)p.L * p.sub;
+    const int width = p.D < kHeadDim ? p.D : kHeadDim;  // elements per piece
+    const int sub = p.D / width;                        // pieces per row
+    const long long lsub = (long long)p.L * sub;
     const long long rows = (long long)p.N * p.H * lsub;
     const int esz = p.src_type == 0 ? 4 : 2;
+    if (4 * lane >= width) return;  // (64-wide rows: lanes 16-31 have nothing to do)
     for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
          row += warps) {
         const long long lj = row % lsub;
-        const int l = (int)(lj / p.sub), j = (int)(lj % p.sub);
+        const int l = (int)(lj / sub), j = (int)(lj % sub);
         const long long nh = row / lsub;
         const int h = (int)(nh % p.H);
         const int n = (int)(nh / p.H);
         const char* src = reinterpret_cast<const char*>(p.src) + (long long)n * p.nb3 + (long long)h * p.nb2 +
-                          (long long)l * p.nb1 + (long long)j * kHeadDim * esz;
+                          (long long)l * p.nb1 + (long long)j * width * esz;
         float a = load_elt(src, 4 * lane + 0, p.src_type), b = load_elt(src, 4 * lane + 1, p.src_type);
         float c = load_elt(src, 4 * lane + 2, p.src_type), d = load_elt(src, 4 * lane + 3, p.src_type);
-        char* dst = reinterpret_cast<char*>(p.dst) + (row * kHeadDim + 4 * lane) * (long long)sizeof(TD);
+        char* dst = reinterpret_cast<char*>(p.dst) + (row * width + 4 * lane) * (long long)sizeof(TD);
         store4<TD>(dst, a, b, c, d);
     }
 }
@@ -280,17 +298,27 @@ cudaError_t launch_prologue(OutType yt, const PrologueParams& p, int num_sms, cu
     long long items = 0;
     for (int j = 0; j < p.njobs; ++j) {
         const PrologueJob& J = p.job[j];
-        const long long n = (long long)J.N * J.L * ((J.H + kPrologueHeads - 1) / kPrologueHeads);
+        const int wrows = (J.H + 128 / p.D - 1) / (128 / p.D);
+        const long long n = (long long)J.N * J.L * ((wrows + kPrologueHeads - 1) / kPrologueHeads);
         items = items > n ? items : n;
     }
     if (items == 0 || p.njobs <= 0) return cudaSuccess;
     const dim3 grid(grid_for(items, num_sms), p.njobs);
-    if (yt == OutType::BF16)
-        prologue_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
-    else if (yt == OutType::F16)
-        prologue_kernel<__half><<<grid, 256, 0, st>>>(p);
-    else
-        prologue_kernel<float><<<grid, 256, 0, st>>>(p);
+    if (p.D == kHeadDim64) {
+        if (yt == OutType::BF16)
+            prologue_kernel<__nv_bfloat16, kHeadDim64><<<grid, 256, 0, st>>>(p);
+        else if (yt == OutType::F16)
+            prologue_kernel<__half, kHeadDim64><<<grid, 256, 0, st>>>(p);
+        else
+            prologue_kernel<float, kHeadDim64><<<grid, 256, 0, st>>>(p);
+    } else {
+        if (yt == OutType::BF16)
+            prologue_kernel<__nv_bfloat16, kHeadDim><<<grid, 256, 0, st>>>(p);
+        else if (yt == OutType::F16)
+            prologue_kernel<__half, kHeadDim><<<grid, 256, 0, st>>>(p);
+        else
+            prologue_kernel<float, kHeadDim><<<grid, 256, 0, st>>>(p);
+    }
     return cudaGetLastError();
 }
 
@@ -300,7 +328,7 @@ cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned l
 }
 
 cudaError_t launch_convert_q(OpType dt, const ConvertParams& p, int num_sms, cudaStream_t st) {
-    const long long rows = (long long)p.N * p.H * p.L * p.sub;
+    const long long rows = (long long)p.N * p.H * p.L * (p.D > kHeadDim ? p.D / kHeadDim : 1);
     if (rows == 0) return cudaSuccess;
     const int grid = grid_for(rows, num_sms);
     if (dt == OpType::BF16)

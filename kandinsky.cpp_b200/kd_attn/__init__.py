@@ -328,7 +328,7 @@ class Context:
 
     # -------------------------------------------------------------- entry points
     def prologue(self, x, n_head, y, norm=True, gain=None, eps=1e-6, rope=None, stream=None):
-        """x: (N, L, C) f32 -> y: (N, n_head, L, 128) f32/f16/bf16 (ggml [128, L, H, N])."""
+        """x: (N, L, C) f32 -> y: (N, n_head, L, d) f32/f16/bf16 (ggml [d, L, H, N]), d = C / n_head = 128 or 64."""
         self.check(lib.kd_attn_prologue(self.handle, _ref(x), int(n_head), 1 if norm else 0, _ptr(gain),
                                         float(eps), None if rope is None else ctypes.byref(rope), _ref(y),
                                         _stream_ptr(stream)))
@@ -336,7 +336,7 @@ class Context:
 
     def qk_prologue(self, q_in, k_in, v_in, q_out, k_out, v_out, q_gain=None, k_gain=None, eps=1e-6, rope=None,
                     stream=None):
-        """One launch: q_in/k_in (N, L, C) f32 -> RMSNorm (+RoPE) -> q_out/k_out (N, H, L, 128); v_in -> v_out
+        """One launch: q_in/k_in (N, L, C) f32 -> RMSNorm (+RoPE) -> q_out/k_out (N, H, L, d); v_in -> v_out
         cast only.  Any (in, out) pair may be None."""
         if len({t.dtype for t in (q_out, k_out, v_out) if t is not None}) != 1:
             raise ValueError("outputs must share one dtype")
@@ -388,8 +388,8 @@ class Context:
 
     def flash_attn_ext(self, q, k, v, out, mask=None, scale=None, kv_len=None, lse=None, max_bias=0.0,
                        logit_softcap=0.0, tile_mask=None, stream=None):
-        """ggml_flash_attn_ext.  q: (N, H, Lq, 128); k, v: (Nkv, Hkv, Lk, 128);
-        mask: (mn, mh, >=Lq, >=Lk) f16 or None; out: (N, Lq, H, 128); lse: (N, H, Lq) f32 or None;
+        """ggml_flash_attn_ext.  q: (N, H, Lq, D); k, v: (Nkv, Hkv, Lk, D), D = 128, 64 or 512;
+        mask: (mn, mh, >=Lq, >=Lk) f16 or None; out: (N, Lq, H, D); lse: (N, H, Lq) f32 or None;
         tile_mask: device uint8 bitmap of kept 64x64 tiles (tile_bitmap layout) or None."""
         if scale is None:
             scale = 1.0 / (q.shape[-1] ** 0.5)
@@ -463,8 +463,8 @@ class Context:
 
     def self_attention_sharded(self, q_in, k_in, v_in, n_head_local, out_full, rope=None, q_gain=None, k_gain=None,
                                eps=1e-6, op_type=BF16, stream=None):
-        """This rank's column shard (N, L, n_head_local*128) f32 of the projections -> every rank's
-        out_full (N, L, n_ranks*n_head_local*128), the exchange fused into the flash epilogue."""
+        """This rank's column shard (N, L, n_head_local*d) f32 of the projections -> every rank's
+        out_full (N, L, n_ranks*n_head_local*d), the exchange fused into the flash epilogue."""
         self.check(lib.kd_attn_self_attention_sharded(self.handle, _ref(q_in), _ref(k_in), _ref(v_in),
                                                       int(n_head_local), _ptr(q_gain), _ptr(k_gain), float(eps),
                                                       None if rope is None else ctypes.byref(rope), int(op_type),
@@ -492,7 +492,7 @@ class Context:
         return out_full
 
     def allgather_heads(self, shard, full, stream=None):
-        """shard: (N, Lq, H/n, 128) -> full: (N, Lq, H, 128), one NCCL all-gather + permute."""
+        """shard: (N, Lq, H/n, D) -> full: (N, Lq, H, D), one NCCL all-gather + permute."""
         self.check(lib.kd_attn_allgather_heads(self.handle, _ref(shard), _ref(full), _stream_ptr(stream)))
         return full
 

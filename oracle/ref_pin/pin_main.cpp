@@ -10,6 +10,7 @@
 //   7. compute_visual_rope(3,4,5, {32,48,48}, {1,2,2})
 //   8. compute_visual_rope(5,16,16, {32,48,48}, {1,2,2}) rows 0,1,17,255,256,1279
 //   9. compute_visual_rope(31,32,32,{32,48,48}, {1,1,1}) rows 0, 1023, 1024, 31743
+//  10. compute_visual_rope(3,4,5, {16,24,24}, {1,2,2})   (the lite video model's head_dim 64)
 #include <cstdio>
 #include <vector>
 #include "rng.hpp"
@@ -36,5 +37,6 @@ int main() {
         auto t = rope::compute_visual_rope(31, 32, 32, {32, 48, 48}, {1.0f, 1.0f, 1.0f});
         for (int r : {0, 1023, 1024, 31743}) put(std::vector<float>(t.begin() + (size_t)r * 128, t.begin() + ((size_t)r + 1) * 128));
     }
+    put(rope::compute_visual_rope(3, 4, 5, {16, 24, 24}, {1.0f, 2.0f, 2.0f}));
     return 0;
 }

@@ -31,6 +31,7 @@ LAYOUT = [  # name, number of float32 values, in the order pin_main.cpp writes t
     ("visual_rope_3x4x5_s122", 60 * 128),
     ("visual_rope_5x16x16_s122_rows", 6 * 128),
     ("visual_rope_31x32x32_s111_rows", 4 * 128),
+    ("visual_rope_3x4x5_a162424_s122", 60 * 64),
 ]
 ROWS_5x16x16 = [0, 1, 17, 255, 256, 1279]
 ROWS_31x32x32 = [0, 1023, 1024, 31743]

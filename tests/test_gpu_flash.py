@@ -150,8 +150,8 @@ def test_flash_ext_kv_len(ctx):
 
 @pytest.mark.parametrize("kv_type", [oracle.F16, oracle.BF16])
 def test_flash_ext_kv_len_remainders(ctx, kv_type):
-    """Valid lengths at every kind of remainder of the 128-key tile and its 16-key MMA steps (the
-    short-key kernel computes each tile's scores and P V only up to the valid keys rounded to 16)."""
+    """Valid lengths at every kind of remainder of the 128-key tile and of its 16-key MMA steps, through
+    the short-key instantiation (keys past the valid length masked in the softmax, padded chunks zero)."""
     kv_len = np.array([1, 15, 16, 17, 100, 128, 129, 200, 255, 256], np.int32)
     N, H, Lq, Lk, D = len(kv_len), 2, 130, 256, 128
     qf = seeded((N, H, Lq, D), 43, 0)
@@ -237,8 +237,8 @@ def test_ops_attention_mirror(ctx, kd):
 
 # ------------------------------------------------------------------ argument errors come back as statuses
 def test_rejects_unsupported_and_invalid(ctx, kd):
-    q = torch.zeros(1, 2, 16, 64, device="cuda", dtype=torch.float16)
-    out = torch.empty(1, 16, 2, 64, device="cuda")
+    q = torch.zeros(1, 2, 16, 96, device="cuda", dtype=torch.float16)   # head_dim 96: not a CrossDiT head
+    out = torch.empty(1, 16, 2, 96, device="cuda")
     with pytest.raises(kd.KdAttnError) as e:
         ctx.flash_attn_ext(q, q, q, out)
     assert e.value.status == kd.ERR_UNSUPPORTED

@@ -45,6 +45,13 @@ def test_visual_rope_matches_reference(gold, scale, key):
     assert np.array_equal(oracle.visual_rope_table((3, 4, 5), scale=scale).ravel(), gold[key])
 
 
+def test_visual_rope_lite_axes_match_reference(gold):
+    """The lite video model's axes {16, 24, 24} (head_dim 64, crossdit.hpp:36,52) with its scale {1, 2, 2}."""
+    t = oracle.visual_rope_table((3, 4, 5), axes=(16, 24, 24), scale=(1, 2, 2))
+    assert t.shape == (60, 64)
+    assert np.array_equal(t.ravel(), gold["visual_rope_3x4x5_a162424_s122"])
+
+
 def test_visual_rope_benchmark_grids_match_reference(gold):
     t = oracle.visual_rope_table((5, 16, 16), scale=(1, 2, 2))
     assert np.array_equal(t[gold["rows_5x16x16"]].ravel(), gold["visual_rope_5x16x16_s122_rows"])
