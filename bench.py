@@ -433,8 +433,33 @@ def extra_measurements(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
         "ms_q_already_f16": ms_f16q, "q_rounding_ms": ms_f32q - ms_f16q,
         "q_rounding_share": (ms_f32q - ms_f16q) / ms_f32q}
     del qf, q16, k16, v16, of
+    res["lite_video"] = lite_video(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream)
     res["projection_attention"] = projection_attention(args, ctx, kd_attn, torch, q, rope, dev, stream)
     return res
+
+
+def lite_video(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
+    """The lite video model's self-attention (CrossDiTConfig::lite_video, crossdit.hpp:48-56: 28 heads of
+    head_dim 64, RoPE axes {16, 24, 24}, scale {1, 2, 2}) over config 1's tokens: the first 1792 channels
+    of config 1's projections, bf16 operands.  The whole call (prologue + flash) and the flash kernel
+    alone, in dense-equivalent TFLOP/s (4 B H L^2 d)."""
+    N, L, _ = q.shape
+    H, d = 28, 64
+    ql, kl, vl = (x[:, :, :H * d] for x in (q, k, v))          # strided views: rows of 4096 floats
+    rope_l = kd_attn.Rope3D.make(tuple(rope.grid), axes=(16, 24, 24), scale=(1, 2, 2))
+    out = torch.empty(N, L, H * d, device=dev, dtype=torch.bfloat16)
+    call_ms = _timed(torch, stream, lambda: ctx.self_attention(ql, kl, vl, H, out, rope=rope_l, op_type=kd_attn.BF16,
+                                                               stream=stream), args.steps, args.warmup)
+    qs = torch.empty(N, H, L, d, device=dev, dtype=torch.bfloat16)
+    ks, vs = torch.empty_like(qs), torch.empty_like(qs)
+    ctx.qk_prologue(ql, kl, vl, qs, ks, vs, rope=rope_l, stream=stream)
+    o4 = out.view(N, L, H, d)
+    fa_ms = _timed(torch, stream, lambda: ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream), args.steps, args.warmup)
+    ctx.device_status()
+    flop = 4.0 * N * H * L * L * d
+    return {"workload": f"lite video self-attn B{N} L{L} H{H} d{d} bf16", "call_ms": call_ms,
+            "call_tflops": flop / (call_ms * 1e-3) / 1e12, "flash_kernel_ms": fa_ms,
+            "flash_kernel_tflops": flop / (fa_ms * 1e-3) / 1e12}
 
 
 def _q8_0_weight(torch, rows, cols, seed, dev):
