@@ -188,8 +188,9 @@ kd_attn_status kd_attn_qk_prologue(kd_attn_ctx* ctx, const kd_tensor* q_in, cons
  * wq/wk/wv : weights in ggml layout [K, C] (row r = output feature r); any of the
  *         three may be NULL together with its output (e.g. the Q projection of
  *         cross-attention alone, or its K/V projection of the text states)
- * q_out/k_out/v_out : [128, L, H, N] f16 or bf16 (= out_dtype), H*128 = C a
- *         multiple of 256, rows 16-byte aligned.  Q and K are normalised (and
+ * q_out/k_out/v_out : [d, L, H, N] f16 or bf16 (= out_dtype), d = 128 or 64 (the
+ *         lite video model; rope axes then sum to 64), H*d = C a multiple of 256,
+ *         rows 16-byte aligned.  Q and K are normalised (and
  *         rotated), V only cast. */
 #define KD_ATTN_TYPE_Q4_0 2 /* ggml.h GGML_TYPE_Q4_0: 18-byte blocks of 32 (f16 scale, 16 bytes of nibbles) */
 #define KD_ATTN_TYPE_Q8_0 8 /* ggml.h GGML_TYPE_Q8_0: 34-byte blocks of 32 (f16 scale, 32 int8) */

@@ -1119,7 +1119,7 @@ kd_attn_status check_weight(kd_attn_ctx* ctx, const kd_linear& W, int64_t K) {
 // Scratch of one GEMM call: [B operand][A operand rows unless read in place][RoPE table].
 size_t gemm_work_bytes(const GemmInput& in, int nslots, int64_t C, bool rot) {
     return align256((size_t)nslots * C * in.Kp * 2) + (in.direct ? 0 : align256((size_t)in.L * in.N * in.Kp * 2)) +
-           (rot ? align256((size_t)in.L * 64 * sizeof(float2)) : 0);
+           (rot ? align256((size_t)in.L * (kHeadDim / 2) * sizeof(float2)) : 0);  // (at most 64 pairs per token)
 }
 
 // Launch sequence of one GEMM: each weight w[i] expanded to bf16 rows of the B operand (slot i = rows
@@ -1151,7 +1151,7 @@ kd_attn_status gemm_run(kd_attn_ctx* ctx, const GemmInput& in, const kd_linear* 
     }
     if (tab) {
         float2* cs = reinterpret_cast<float2*>(work + b_bytes + a_bytes);
-        KD_CUDA(ctx, launch_rope_table(*tab, (int)in.L, cs, ctx->num_sms, st));
+        KD_CUDA(ctx, launch_rope_table(*tab, (int)in.L, p.D / 2, cs, ctx->num_sms, st));
         p.rope_cs = cs;
     }
     CUtensorMap tmX, tmW;
@@ -1179,7 +1179,7 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
     const int64_t K = in.K, L = in.L, N = in.N;
     QkvParams p{};
     p.eps = eps;
-    int64_t C = -1;
+    int64_t C = -1, D = -1;
     const kd_linear* ws[3] = {};
     for (int i = 0; i < 3; ++i) {
         if (!w[i] && !outs[i]) continue;
@@ -1191,8 +1191,13 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
         if ((rc = check_weight(ctx, W, K))) return rc;
         if (C >= 0 && W.ne[1] != C) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the weights disagree on out_features");
         C = W.ne[1];
-        if (o.ne[0] != kHeadDim || o.ne[1] != L || o.ne[2] * kHeadDim != C || o.ne[3] != N)
-            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must be [128, L, C/128, N]");
+        // head dim from the outputs: 128, or 64 (the lite video model)
+        if (D >= 0 && o.ne[0] != D) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs disagree on the head dim");
+        D = o.ne[0];
+        if (D != kHeadDim && D != kHeadDim64)
+            return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "output head dim %lld is not 128 or 64", (long long)D);
+        if (o.ne[1] != L || o.ne[2] * D != C || o.ne[3] != N)
+            return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "outputs must be [D, L, C/D, N]");
         uint64_t onb[4];
         packed_strides(&o, onb);
         if (!aligned16(o.data) || !strides16(onb))
@@ -1212,9 +1217,10 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
     if (!aligned16(q_gain) || !aligned16(k_gain))
         return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "q_gain / k_gain must be 16-byte aligned");
     p.C = (int)C;
+    p.D = (int)D;
     RopeTab tab{};
     const bool rot = rope && (p.slot[0].rope || (p.nslots > 1 && p.slot[1].rope));
-    if (rot && (rc = fill_rope(ctx, rope, L, kHeadDim, &tab))) return rc;
+    if (rot && (rc = fill_rope(ctx, rope, L, D, &tab))) return rc;
     if (L * N == 0) return KD_ATTN_OK;
     if (!work) {
         if ((rc = ensure_scratch(ctx, gemm_work_bytes(in, p.nslots, C, rot), st))) return rc;
@@ -1243,6 +1249,7 @@ kd_attn_status linear_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear
     QkvParams p{};
     p.nslots = 1;
     p.C = (int)C;
+    p.D = kHeadDim;  // no norm or RoPE: the output is addressed in 128-column groups
     QkvSlot& S = p.slot[0];
     // a row-major [C, L, N] output in the epilogue's (row, 128-column group, sequence) addressing
     S.out = y->data;

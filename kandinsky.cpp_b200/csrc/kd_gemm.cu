@@ -168,7 +168,7 @@ __device__ __forceinline__ void store_chunk<float>(float* dst, const float* v) {
 
 // Launched as clusters of 2 (blockIdx.x = 2 * pair + rank); both CTAs run the producer and the epilogue
 // warps, rank 0 also issues the MMAs.
-template <typename TO>
+template <typename TO, int kD>
 __global__ void __launch_bounds__(kGThreads, 1)
     qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ QkvParams p) {
@@ -305,19 +305,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
             const int l = valid ? (int)(m % p.L) : 0, n = valid ? (int)(m / p.L) : 0;
             const int col0 = nt * kBN + hh * 128;
             const QkvSlot& S = p.slot[col0 / p.C];
-            const int h = (col0 % p.C) / 128;
+            const int fcol = col0 % p.C + half * 64;        // this warpgroup's first feature of the slot
+            const int h = fcol / kD, c0 = fcol % kD;        // its head and first column within the head
             // this thread's 64 accumulator columns, then the buffer is released at once: the MMAs of a later
             // tile may overwrite it while the values are processed from registers
             uint32_t xr[64];
             tmem_ld64_sync(tmem + lane_addr + ab * kBN + hh * 128 + half * 64, xr);
             tc_fence_before();
             mbar_arrive_remote(acc_empty0 + 8u * ab);
-            const int c0 = half * 64;  // first column within the head
             float x[64];
 #pragma unroll
             for (int d = 0; d < 64; ++d) x[d] = __uint_as_float(xr[d]);
             if (S.bias) {  // 16-byte aligned (checked by the host)
-                const float4* b4 = reinterpret_cast<const float4*>(S.bias + h * 128 + c0);
+                const float4* b4 = reinterpret_cast<const float4*>(S.bias + fcol);
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
                     const float4 b = __ldg(b4 + q);
@@ -332,7 +332,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
             // here), so the sum is carried as an unevaluated float pair (Knuth's TwoSum, ~48 significant bits):
             // its rounding to float equals that of the double sum except within ~2^-48 of a rounding tie.
             // Each warpgroup sums its half of the row; the halves are swapped through shared memory on every
-            // tile (so the exchange barriers' phases follow the tile count) and combined in a fixed order.
+            // tile (so the exchange barriers' phases follow the tile count) and combined in a fixed order.  A
+            // 64-wide head is one warpgroup's whole row and ignores the other half's sum; the exchange runs
+            // all the same (without it this instantiation's epilogue spilled 812 bytes).
             float hi = 0.0f, lo = 0.0f;
 #pragma unroll
             for (int d = 0; d < 64; ++d) two_sum_acc(hi, lo, __fmul_rn(x[d], x[d]));
@@ -341,13 +343,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
             uint64_t* xb = &exch[(tc & 1u) * 2 + hh];
             mbar_arrive(xb);
             if (!__all_sync(0xffffffffu, mbar_wait(xb, (tc >> 1) & 1u, ctl, kErrTimeoutO))) break;
-            const float2 other = pp[(wg ^ 1) * 128 + r];
+            const float2 other = kD == 128 ? pp[(wg ^ 1) * 128 + r] : make_float2(0.0f, 0.0f);
             float scale = 1.0f;
             if (S.norm) {
                 float thi = half == 0 ? hi : other.x, tlo = half == 0 ? lo : other.y;
-                two_sum_acc(thi, tlo, half == 0 ? other.x : hi);
+                two_sum_acc(thi, tlo, half == 0 ? other.x : hi);  // (+0: the sum unchanged for 64-wide heads)
                 tlo = __fadd_rn(tlo, half == 0 ? other.y : lo);
-                const float mean = __fmul_rn(__fadd_rn(thi, tlo), 1.0f / 128.0f);  // exact scaling by 2^-7
+                // exact scaling by 2^-7 or 2^-6
+                const float mean = __fmul_rn(__fadd_rn(thi, tlo), 1.0f / kD);
                 scale = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, p.eps)));
 #pragma unroll
                 for (int d = 0; d < 64; ++d) x[d] = __fmul_rn(x[d], scale);
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             }
             TO* dst = reinterpret_cast<TO*>(static_cast<char*>(S.out) + (long long)n * S.o_nb3 +
                                             (long long)h * S.o_nb2 + (long long)l * S.o_nb1) + c0;
-            const float2* cs = S.rope ? p.rope_cs + (long long)l * 64 + c0 / 2 : nullptr;
+            const float2* cs = S.rope ? p.rope_cs + (long long)l * (kD / 2) + c0 / 2 : nullptr;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 if (cs) {
@@ -468,10 +471,10 @@ __global__ void to_bf16_rows_kernel(const char* x, long long nb1, long long nb2,
 
 // (cos, sin) of every (token l, rotary pair i): angle = pos_axis(l) * freq_i / scale_axis, the
 // prologue's formula (rope.hpp:78-95 order of operations, correctly rounded float ops).
-__global__ void rope_table_kernel(const RopeTab tab, int L, float2* cs) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)L * 64;
+__global__ void rope_table_kernel(const RopeTab tab, int L, int pairs, float2* cs) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)L * pairs;
          i += (long long)gridDim.x * blockDim.x) {
-        const int l = (int)(i / 64), pi = (int)(i % 64);
+        const int l = (int)(i / pairs), pi = (int)(i % pairs);
         const int w = l % tab.grid_w, hh = (l / tab.grid_w) % tab.grid_h, t = l / (tab.grid_w * tab.grid_h);
         const int ax = tab.axis[pi];
         const float pos = (float)(ax == 0 ? t : (ax == 1 ? hh : w));
@@ -507,16 +510,21 @@ cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int
     return cudaGetLastError();
 }
 
-cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms, cudaStream_t st) {
+cudaError_t launch_rope_table(const RopeTab& tab, int L, int pairs, float2* cs, int num_sms, cudaStream_t st) {
     if (L == 0) return cudaSuccess;
-    rope_table_kernel<<<grid_1d((long long)L * 64, num_sms), 256, 0, st>>>(tab, L, cs);
+    rope_table_kernel<<<grid_1d((long long)L * pairs, num_sms), 256, 0, st>>>(tab, L, pairs, cs);
     return cudaGetLastError();
 }
 
 cudaError_t launch_qkv_gemm(OutType ot, const CUtensorMap& tmX, const CUtensorMap& tmW, const QkvParams& p, int num_sms,
                             cudaStream_t st) {
-    auto kern = ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16>
-                                    : (ot == OutType::F16 ? qkv_gemm_kernel<__half> : qkv_gemm_kernel<float>);
+    // head dim 64 (the lite model's normalised/rotated slots) or 128 (also every plain linear)
+    auto kern = p.D == 64 ? (ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16, 64>
+                                                 : (ot == OutType::F16 ? qkv_gemm_kernel<__half, 64>
+                                                                       : qkv_gemm_kernel<float, 64>))
+                          : (ot == OutType::BF16 ? qkv_gemm_kernel<__nv_bfloat16, 128>
+                                                 : (ot == OutType::F16 ? qkv_gemm_kernel<__half, 128>
+                                                                       : qkv_gemm_kernel<float, 128>));
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemAlloc);
     if (e != cudaSuccess) return e;
     const long long tiles = (long long)((p.M + kPairM - 1) / kPairM) * (p.nslots * p.C / kBN);

@@ -134,7 +134,7 @@ struct MaskClassParams {
 cudaError_t launch_mask_classify(const MaskClassParams& p, cudaStream_t st);
 
 // ---------------------------------------------------------------- QKV projection (kd_gemm.cu)
-// One projection of the fused GEMM: C output features = C/128 heads, written as [128, L, H, N].
+// One projection of the fused GEMM: C output features = C/D heads, written as [D, L, H, N].
 struct QkvSlot {
     void* out;
     long long o_nb1, o_nb2, o_nb3;  // byte strides of out (row, head, sequence)
@@ -145,13 +145,15 @@ struct QkvSlot {
 };
 struct QkvParams {
     QkvSlot slot[3];
+    int D;                   // head dim of the normalised/rotated slots: 128, or 64 (a warpgroup's 64 columns
+                             // are one whole head: no exchange of RMSNorm sums); 128 for plain linears
     int nslots;              // projections concatenated along the B operand's rows (slot s = rows [s*C, (s+1)*C))
     int C;                   // output features per projection, a multiple of 256
     int K;                   // input features
     int M;                   // tokens = L * N
     int L;                   // tokens per sequence (token m is l = m % L of sequence n = m / L)
     float eps;
-    const float2* rope_cs;   // [L][64] (cos, sin) or null
+    const float2* rope_cs;   // [L][D/2] (cos, sin) or null
     unsigned* err;
     unsigned* abort_flag;
     unsigned long long wait_ns;
@@ -177,8 +179,8 @@ cudaError_t launch_expand_weights(const void* w, int type, long long row_bytes, 
 // columns K .. Kp-1 zero.
 cudaError_t launch_to_bf16_rows(const void* x, long long nb1, long long nb2, int K, int Kp, int L, long long M,
                                 __nv_bfloat16* dst, int num_sms, cudaStream_t st);
-// (cos, sin) of every token and rotary pair of the 3D RoPE table: cs[l * 64 + i].
-cudaError_t launch_rope_table(const RopeTab& tab, int L, float2* cs, int num_sms, cudaStream_t st);
+// (cos, sin) of every token and rotary pair of the 3D RoPE table: cs[l * pairs + i], pairs = D/2.
+cudaError_t launch_rope_table(const RopeTab& tab, int L, int pairs, float2* cs, int num_sms, cudaStream_t st);
 
 // One bounded wait that nothing releases (sets the self-test error bit after wait_ns).
 cudaError_t launch_wait_selftest(unsigned* err, unsigned* abort_flag, unsigned long long wait_ns, cudaStream_t st);

@@ -200,3 +200,45 @@ def test_lite_rejects_rope_of_the_wrong_width(ctx, kd):
         ctx.prologue(x, H, y, norm=True, rope=kd.Rope3D.make(grid))
     assert e.value.status == kd.ERR_INVALID_ARGUMENT
     ctx.device_status()
+
+
+# ------------------------------------------------------------------ the fused QKV projection at head_dim 64
+@pytest.mark.parametrize("wname", ["q8_0", "q4_0"])
+def test_lite_qkv_projection_matches_oracle(ctx, kd, wname):
+    """to_query/to_key/to_value of the lite video model (model_dim 1792 = 28 heads of 64) as one GEMM whose
+    epilogue normalises each 64-wide head alone and rotates it with the {16, 24, 24} RoPE."""
+    from test_gpu_projection import WTYPES, check, make_weight
+    from test_gpu_projection import dev as pdev
+    N, grid, K, H = 2, (3, 10, 10), 1792, 28
+    L, C = int(np.prod(grid)), H * D
+    x = seeded((N, L, K), 61, 0)
+    lin = [make_weight(kd, 62, 10 * i, C, K, WTYPES[wname], bias=(i != 1)) for i in range(3)]
+    q_gain = (1.0 + 0.1 * seeded((D,), 63, 0)).astype(np.float32)
+    k_gain = (1.0 + 0.1 * seeded((D,), 63, 1)).astype(np.float32)
+    tab = oracle.visual_rope_table(grid, axes=LITE_AXES, scale=LITE_SCALE)
+    outs = [torch.full((N, H, L, D), float("nan"), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(pdev(x), lin[0][0], lin[1][0], lin[2][0], *outs, q_gain=pdev(q_gain), k_gain=pdev(k_gain),
+                       rope=kd.Rope3D.make(grid, axes=LITE_AXES, scale=LITE_SCALE))
+    ctx.device_status()
+    check(outs, x, [l[2] for l in lin], [l[3] for l in lin], H, q_gain, k_gain, tab, "bf16", f"lite {wname}")
+
+
+def test_lite_projection_feeds_flash(ctx, kd):
+    """Lite projection -> flash attention (head_dim 64) against the oracle's composition."""
+    from test_gpu_projection import make_weight
+    from test_gpu_projection import dev as pdev
+    N, grid, K, H = 1, (2, 8, 10), 1792, 28
+    L, C = int(np.prod(grid)), H * D
+    x = seeded((N, L, K), 67, 0)
+    lin = [make_weight(kd, 68, 10 * i, C, K, kd.Q8_0) for i in range(3)]
+    tab = oracle.visual_rope_table(grid, axes=LITE_AXES, scale=LITE_SCALE)
+    ops = [torch.empty((N, H, L, D), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ctx.qkv_projection(pdev(x), lin[0][0], lin[1][0], lin[2][0], *ops,
+                       rope=kd.Rope3D.make(grid, axes=LITE_AXES, scale=LITE_SCALE))
+    out = torch.empty(N, L, H, D, device="cuda")
+    ctx.flash_attn_ext(*ops, out)
+    ctx.device_status()
+    q, k, v = oracle.qkv_projection(x, [l[2] for l in lin], [l[3] for l in lin], H, rope_table=tab)
+    exact = oracle.flash_attn_ext(q, oracle.to_type(k, oracle.BF16), oracle.to_type(v, oracle.BF16),
+                                  mode=oracle.EXACT)
+    assert_gates(out.cpu().numpy(), exact, label="lite projection -> flash")
