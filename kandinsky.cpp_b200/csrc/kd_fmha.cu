@@ -105,6 +105,9 @@ constexpr float kRescaleThresholdQ2 = 0.0f;
 #ifndef KD_FMHA_POLY_PAIRS
 #define KD_FMHA_POLY_PAIRS 0x0000u
 #endif
+#ifndef KD_FMHA_POLY_PAIRS_D64  // the same for the head_dim-64 kernels, whose exponentials bound them
+#define KD_FMHA_POLY_PAIRS_D64 0x1249u
+#endif
 #ifndef KD_FMHA_SPLIT_P
 #define KD_FMHA_SPLIT_P 0
 #endif
@@ -112,6 +115,7 @@ constexpr float kRescaleThresholdQ2 = 0.0f;
 #define KD_FMHA_MAX3 1
 #endif
 constexpr uint32_t kPolyPairs = KD_FMHA_POLY_PAIRS;
+constexpr uint32_t kPolyPairsD64 = KD_FMHA_POLY_PAIRS_D64;
 
 
 // A list entry's class bits cover the unit's four 64-row groups, two per Q tile: Q tile i needs
@@ -914,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             xb = fmaf(__uint_as_float(su[c * 32 + 2 * i + 1]), sl2, neg_mu);
                         }
                         float a, bb;
-                        if ((kPolyPairs >> i) & 1u) {
+                        if (((kD == kHeadDim64 ? kPolyPairsD64 : kPolyPairs) >> i) & 1u) {
                             exp2_poly2(xa, xb, a, bb);
                         } else {
                             a = ex2_approx(xa);
