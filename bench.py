@@ -496,8 +496,8 @@ def projection_attention(args, ctx, kd_attn, torch, x, rope, dev, stream):
     wo = _q8_0_weight(torch, C, C, 14, dev)
     lin_o = kd_attn.KdLinear.of(wo, kd_attn.Q8_0, C, C, torch.randn(C, device=dev) * 0.1)
     y = torch.empty(N, L, C, device=dev)
-    ms_block = _timed(torch, stream, lambda: ctx.self_attention_block(x, *lin, lin_o, y, rope=rope, stream=stream),
-                      args.steps, args.warmup)
+    ms_block = _timed(torch, stream, lambda: ctx.self_attention_block(x, *lin, lin_o, C // 128, y, rope=rope,
+                                                                      stream=stream), args.steps, args.warmup)
     ctx.device_status()
     del outs, o, ws, bias, lin, wo, lin_o, y
     xb = x.reshape(-1, K).to(torch.bfloat16)

@@ -216,24 +216,27 @@ kd_attn_status kd_attn_qkv_projection(kd_attn_ctx* ctx, const kd_tensor* x, cons
 kd_attn_status kd_attn_linear(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* w, kd_tensor* y, void* stream);
 
 /* Replaces DiTSelfAttention::forward (crossdit.hpp:117-154) from the hidden states to the block output:
- * kd_attn_qkv_projection (bf16 operands), the flash kernel (scale 1/sqrt(128), no mask) and the
+ * kd_attn_qkv_projection (bf16 operands), the flash kernel (scale 1/sqrt(d), no mask) and the
  * out-projection, with the intermediate tensors in the context's scratch.
- * x : [C, L, N] f32; wq/wk/wv : [C, C]; wo : [C, C_out]; q_gain/k_gain : RMSNorm weights (NULL = unit);
- * rope : NULL = no rotation; y : [C_out, L, N] f32 (or bf16/f16).  C = n_head * 128. */
+ * x : [C, L, N] f32; wq/wk/wv : [C, C]; wo : [C, C_out]; n_head : the module's num_heads, head dim
+ * d = C / n_head = 128 (pro_video, lite_image) or 64 (lite_video); q_gain/k_gain : RMSNorm weights
+ * [d] (NULL = unit); rope : NULL = no rotation, else axes summing to d; y : [C_out, L, N] f32 (or
+ * bf16/f16). */
 kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                             const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                            const float* q_gain, const float* k_gain, float eps,
+                                            int32_t n_head, const float* q_gain, const float* k_gain, float eps,
                                             const kd_rope3d* rope, kd_tensor* y, void* stream);
 
 /* Replaces DiTCrossAttention::forward (crossdit.hpp:174-200): visual queries from x_query [C, Lq, N] f32,
  * keys and values from the text states x_kv [C, Lk, N] f32 (RMSNorm on Q and K, no RoPE), flash
  * attention with the text's valid lengths -- kv_len (device int32 [N]) and/or an f16 mask as for
- * kd_attn_flash_ext, either may be NULL -- and the out-projection; y : [C_out, Lq, N]. */
+ * kd_attn_flash_ext, either may be NULL -- and the out-projection; y : [C_out, Lq, N].  n_head as
+ * for kd_attn_self_attention_block. */
 kd_attn_status kd_attn_cross_attention_block(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
                                              const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
-                                             const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
-                                             const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
-                                             void* stream);
+                                             const kd_linear* wo, int32_t n_head, const float* q_gain,
+                                             const float* k_gain, float eps, const kd_tensor* mask,
+                                             const int32_t* kv_len, kd_tensor* y, void* stream);
 
 /* ---------------------------------------------------------------------------
  * ggml_flash_attn_ext semantics (called at ops.hpp:176):
@@ -409,16 +412,16 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
 /* DiTSelfAttention::forward (crossdit.hpp:117-154) with heads sharded over the group: rank r passes the
  * replicated hidden states x [C, L, N] f32, ITS column shard of the Q/K/V weights (wq/wk/wv: [C, C_local],
  * the output features of heads [r*n_head_local, (r+1)*n_head_local), C_local a multiple of 256) and the
- * full out_layer weight wo [n_ranks*C_local, C_out].  The projection and attention of its heads run
- * locally, the flash epilogue stores its heads into every rank's attn_full (bf16
+ * full out_layer weight wo [n_ranks*C_local, C_out]; n_head_local = C_local / d.  The projection and
+ * attention of its heads run locally, the flash epilogue stores its heads into every rank's attn_full (bf16
  * [n_ranks*C_local, L, N], contiguous, inside a kd_attn_symmetric_alloc buffer), and after the closing
  * barrier each rank applies out_layer to the gathered output: y [C_out, L, N] on every rank.
  * Collective (two barriers on the communicator). */
 kd_attn_status kd_attn_self_attention_block_sharded(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                                     const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                                    const float* q_gain, const float* k_gain, float eps,
-                                                    const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
-                                                    void* stream);
+                                                    int32_t n_head_local, const float* q_gain, const float* k_gain,
+                                                    float eps, const kd_rope3d* rope, kd_tensor* attn_full,
+                                                    kd_tensor* y, void* stream);
 
 /* The same for DiTCrossAttention::forward (crossdit.hpp:186-198): this rank's heads of the
  * visual queries against the text keys/values (column shards of k_in/v_in), no RoPE, the

@@ -61,7 +61,7 @@ inline bool kd_from_ggml(const ggml_tensor* t, kd_tensor* out) {
 }
 
 // Would kd_attn_attention accept ops::attention(q, k, v, n_head, mask, flash = true)?  q [C, Lq, N],
-// k/v [C_kv, Lk, N] f32 with head_dim 128, GQA ratio integral, f16 mask [Lk, >=Lq] or none -- or the
+// k/v [C_kv, Lk, N] f32 with head_dim 128 or 64, GQA ratio integral, f16 mask [Lk, >=Lq] or none -- or the
 // VAE mid block's single head of 512 channels (vae.hpp:89): packed rows, no mask.
 inline bool supports_attention(const ggml_tensor* q, const ggml_tensor* k, const ggml_tensor* v, int64_t n_head,
                                const ggml_tensor* mask) {
@@ -74,7 +74,8 @@ inline bool supports_attention(const ggml_tensor* q, const ggml_tensor* k, const
                 return false;
         return !mask && k->ne[1] == v->ne[1] && k->ne[2] == q->ne[2] && v->ne[2] == q->ne[2];
     }
-    if (d != 128 || k->ne[0] % d || v->ne[0] != k->ne[0] || q->ne[3] != 1 || k->ne[3] != 1 || v->ne[3] != 1)
+    if ((d != 128 && d != 64) || k->ne[0] % d || v->ne[0] != k->ne[0] || q->ne[3] != 1 || k->ne[3] != 1 ||
+        v->ne[3] != 1)
         return false;
     const int64_t n_kv = k->ne[0] / d;
     if (n_kv <= 0 || n_head % n_kv || k->ne[1] != v->ne[1] || k->ne[2] != q->ne[2] || v->ne[2] != q->ne[2]) return false;
@@ -103,7 +104,7 @@ inline void attention_node(ggml_tensor* dst, int ith, int /*nth*/, void* userdat
 }
 
 // Parameters of a fused DiT self-attention node (crossdit.hpp:132-150): RMSNorm gains of the q/k
-// norms (device, [128]) and the token grid of the 3D RoPE.
+// norms (device, [head_dim]) and the token grid of the 3D RoPE.
 struct DitAttentionParams {
     int32_t n_head = 32;
     const float* q_gain = nullptr;
@@ -153,13 +154,13 @@ inline bool linear_from_ggml(const ggml_tensor* w, const ggml_tensor* b, kd_line
 }
 
 // Would kd_attn_self_attention_block take DiTSelfAttention::forward(x) with these parameters?  x [C, L, N]
-// f32 with C = n_head * 128, the four Linears [C, C] (out_layer [C, C_out]) of types the GEMM expands,
-// C and C_out multiples of 256, a RoPE grid covering L.
+// f32 with C = n_head * d, d = 128 or 64, the four Linears [C, C] (out_layer [C, C_out]) of types the GEMM
+// expands, C and C_out multiples of 256, a RoPE grid covering L.
 inline bool supports_self_attention_block(const ggml_tensor* x, const ggml_tensor* const w[4],
                                           const ggml_tensor* const b[4], int64_t n_head, const kd_rope3d* rope) {
     if (!x || x->type != GGML_TYPE_F32 || x->nb[0] != 4 || x->ne[3] != 1 || n_head <= 0) return false;
     const int64_t C = x->ne[0];
-    if (C != n_head * 128 || C % 256) return false;
+    if ((C != n_head * 128 && C != n_head * 64) || C % 256) return false;
     for (int i = 0; i < 4; ++i) {
         kd_linear l{};
         if (!linear_from_ggml(w[i], b[i], &l) || l.ne[0] != C || l.ne[1] % 256 || (i < 3 && l.ne[1] != C)) return false;
@@ -182,8 +183,8 @@ inline void dit_block_node(ggml_tensor* dst, int ith, int /*nth*/, void* userdat
         s.last_status = KD_ATTN_ERR_INVALID_ARGUMENT;
         return;
     }
-    s.last_status = kd_attn_self_attention_block(s.ctx, &x, &w[0], &w[1], &w[2], &w[3], a->q_gain, a->k_gain, a->eps,
-                                                 a->use_rope ? &a->rope : nullptr, &y, s.stream);
+    s.last_status = kd_attn_self_attention_block(s.ctx, &x, &w[0], &w[1], &w[2], &w[3], a->n_head, a->q_gain,
+                                                 a->k_gain, a->eps, a->use_rope ? &a->rope : nullptr, &y, s.stream);
     if (s.last_status != KD_ATTN_OK)
         fprintf(stderr, "kd_bridge: kd_attn_self_attention_block failed (%d): %s\n", s.last_status,
                 kd_attn_last_error(s.ctx));

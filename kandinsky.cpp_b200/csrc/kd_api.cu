@@ -1268,20 +1268,34 @@ kd_attn_status linear_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear
 
 // DiTSelfAttention::forward (crossdit.hpp:117-154) from the hidden states: fused QKV projection, flash
 // attention, out-projection.  Scratch: [Q][K][V operands][attention output][GEMM work, shared by both GEMMs].
+// The head dim of a block whose projections map to C features over n_head heads (DiTSelfAttention's and
+// DiTCrossAttention's num_heads, crossdit.hpp): D = C / n_head, 128 or 64.
+kd_attn_status block_head_dim(kd_attn_ctx* ctx, const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
+                              const kd_linear* wo, int32_t n_head, int64_t* D) {
+    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    const int64_t C = wq->ne[1];
+    if (wk->ne[1] != C || wv->ne[1] != C || wo->ne[0] != C)
+        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the projections must map to C features and back");
+    *D = n_head > 0 ? C / n_head : 0;
+    if (n_head <= 0 || (*D != kHeadDim && *D != kHeadDim64) || (int64_t)n_head * *D != C)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "C = %lld over %d heads is not a head dim of 128 or 64", (long long)C,
+                    n_head);
+    return KD_ATTN_OK;
+}
+
 kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                          const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                         const float* q_gain, const float* k_gain, float eps, const kd_rope3d* rope,
-                                         kd_tensor* y, cudaStream_t st) {
+                                         int32_t n_head, const float* q_gain, const float* k_gain, float eps,
+                                         const kd_rope3d* rope, kd_tensor* y, cudaStream_t st) {
     kd_attn_status rc;
     GemmInput in;
     if ((rc = gemm_input(ctx, x, &in))) return rc;
-    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    int64_t D = 0;
+    if ((rc = block_head_dim(ctx, wq, wk, wv, wo, n_head, &D))) return rc;
     const int64_t C = wq->ne[1], L = in.L, N = in.N;
-    if (C % kHeadDim || wk->ne[1] != C || wv->ne[1] != C || wo->ne[0] != C)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the projections must map to n_head * 128 features and back");
-    const int32_t H = (int32_t)(C / kHeadDim);
+    const int32_t H = n_head;
     const int32_t op = KD_ATTN_TYPE_BF16;
-    const size_t opb = align256((size_t)N * H * L * kHeadDim * 2);
+    const size_t opb = align256((size_t)N * H * L * D * 2);
     const bool rot = rope != nullptr;
     GemmInput attn_in = in;  // the out-projection reads the attention output [C, L, N] bf16 in place
     attn_in.K = attn_in.Kp = C;
@@ -1289,10 +1303,10 @@ kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, c
     const size_t work = std::max(gemm_work_bytes(in, 3, C, rot), gemm_work_bytes(attn_in, 1, wo->ne[1], false));
     if ((rc = ensure_scratch(ctx, 4 * opb + work, st))) return rc;
     char* base = static_cast<char*>(ctx->scratch);
-    kd_tensor Qs = operand_view(base, op, L, H, N);
-    kd_tensor Ks = operand_view(base + opb, op, L, H, N);
-    kd_tensor Vs = operand_view(base + 2 * opb, op, L, H, N);
-    kd_tensor A{};  // attention output [C, L, N] bf16 = the flash dst [128, H, L, N]
+    kd_tensor Qs = operand_view(base, op, L, H, N, D);
+    kd_tensor Ks = operand_view(base + opb, op, L, H, N, D);
+    kd_tensor Vs = operand_view(base + 2 * opb, op, L, H, N, D);
+    kd_tensor A{};  // attention output [C, L, N] bf16 = the flash dst [D, H, L, N]
     A.data = base + 3 * opb;
     A.type = op;
     A.ne[0] = C;
@@ -1308,8 +1322,8 @@ kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, c
     kd_tensor* o3[3] = {&Qs, &Ks, &Vs};
     if ((rc = qkv_projection_core(ctx, x, w3, q_gain, k_gain, eps, rope, op, o3, st, gw))) return rc;
     kd_tensor ov;
-    if ((rc = out_view(ctx, &A, H, L, N, &ov))) return rc;
-    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)kHeadDim), nullptr, &ov, nullptr};
+    if ((rc = out_view(ctx, &A, H, L, N, &ov, D))) return rc;
+    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)D), nullptr, &ov, nullptr};
     if ((rc = flash_run(ctx, fa, st))) return rc;  // bf16 operands, no mask: no scratch of its own
     return linear_core(ctx, &A, wo, y, st, gw);
 }
@@ -1320,21 +1334,20 @@ kd_attn_status self_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x, c
 // core's mask-class scratch][Q][K][V operands][attention output][GEMM work shared by the three GEMMs].
 kd_attn_status cross_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
                                           const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
-                                          const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
-                                          const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
-                                          cudaStream_t st) {
+                                          const kd_linear* wo, int32_t n_head, const float* q_gain,
+                                          const float* k_gain, float eps, const kd_tensor* mask,
+                                          const int32_t* kv_len, kd_tensor* y, cudaStream_t st) {
     kd_attn_status rc;
     GemmInput iq, ikv;
     if ((rc = gemm_input(ctx, x_query, &iq)) || (rc = gemm_input(ctx, x_kv, &ikv))) return rc;
-    if (!wq || !wk || !wv || !wo) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "all four weights are required");
+    int64_t D = 0;
+    if ((rc = block_head_dim(ctx, wq, wk, wv, wo, n_head, &D))) return rc;
     const int64_t C = wq->ne[1], Lq = iq.L, Lk = ikv.L, N = iq.N;
     if (ikv.N != N) return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "x_query and x_kv disagree on the batch");
-    if (C % kHeadDim || wk->ne[1] != C || wv->ne[1] != C || wo->ne[0] != C)
-        return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "the projections must map to n_head * 128 features and back");
-    const int32_t H = (int32_t)(C / kHeadDim);
+    const int32_t H = n_head;
     const int32_t op = KD_ATTN_TYPE_BF16;
-    const size_t qb = align256((size_t)N * H * Lq * kHeadDim * 2);
-    const size_t kb = align256((size_t)N * H * Lk * kHeadDim * 2);
+    const size_t qb = align256((size_t)N * H * Lq * D * 2);
+    const size_t kb = align256((size_t)N * H * Lk * D * 2);
     const size_t flash_extra =
         mask ? align256((size_t)mask->ne[2] * mask->ne[3] * ((Lq + 63) / 64) * ((Lk + 63) / 64)) : 0;
     GemmInput attn_in = iq;  // the out-projection reads the attention output [C, Lq, N] bf16 in place
@@ -1344,10 +1357,10 @@ kd_attn_status cross_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x_q
                                   gemm_work_bytes(attn_in, 1, wo->ne[1], false)});
     if ((rc = ensure_scratch(ctx, flash_extra + 2 * qb + 2 * kb + work, st))) return rc;
     char* base = static_cast<char*>(ctx->scratch) + flash_extra;
-    kd_tensor Qs = operand_view(base, op, Lq, H, N);
-    kd_tensor Ks = operand_view(base + qb, op, Lk, H, N);
-    kd_tensor Vs = operand_view(base + qb + kb, op, Lk, H, N);
-    kd_tensor A{};  // attention output [C, Lq, N] bf16 = the flash dst [128, H, Lq, N]
+    kd_tensor Qs = operand_view(base, op, Lq, H, N, D);
+    kd_tensor Ks = operand_view(base + qb, op, Lk, H, N, D);
+    kd_tensor Vs = operand_view(base + qb + kb, op, Lk, H, N, D);
+    kd_tensor A{};  // attention output [C, Lq, N] bf16 = the flash dst [D, H, Lq, N]
     A.data = base + qb + 2 * kb;
     A.type = op;
     A.ne[0] = C;
@@ -1366,8 +1379,8 @@ kd_attn_status cross_attention_block_core(kd_attn_ctx* ctx, const kd_tensor* x_q
     kd_tensor* okv3[3] = {nullptr, &Ks, &Vs};
     if ((rc = qkv_projection_core(ctx, x_kv, wkv3, nullptr, k_gain, eps, nullptr, op, okv3, st, gw))) return rc;
     kd_tensor ov;
-    if ((rc = out_view(ctx, &A, H, Lq, N, &ov))) return rc;
-    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)kHeadDim), kv_len, &ov, nullptr};
+    if ((rc = out_view(ctx, &A, H, Lq, N, &ov, D))) return rc;
+    FlashArgs fa{&Qs, &Ks, &Vs, mask, 1.0f / std::sqrt((float)D), kv_len, &ov, nullptr};
     if ((rc = flash_run(ctx, fa, st))) return rc;
     return linear_core(ctx, &A, wo, y, st, gw);
 }
@@ -1582,23 +1595,23 @@ kd_attn_status kd_attn_linear(kd_attn_ctx* ctx, const kd_tensor* x, const kd_lin
 
 kd_attn_status kd_attn_self_attention_block(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                             const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                            const float* q_gain, const float* k_gain, float eps,
+                                            int32_t n_head, const float* q_gain, const float* k_gain, float eps,
                                             const kd_rope3d* rope, kd_tensor* y, void* stream) {
     if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
     DeviceGuard g(ctx->device);
-    return self_attention_block_core(ctx, x, wq, wk, wv, wo, q_gain, k_gain, eps, rope, y,
+    return self_attention_block_core(ctx, x, wq, wk, wv, wo, n_head, q_gain, k_gain, eps, rope, y,
                                      static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_cross_attention_block(kd_attn_ctx* ctx, const kd_tensor* x_query, const kd_tensor* x_kv,
                                              const kd_linear* wq, const kd_linear* wk, const kd_linear* wv,
-                                             const kd_linear* wo, const float* q_gain, const float* k_gain, float eps,
-                                             const kd_tensor* mask, const int32_t* kv_len, kd_tensor* y,
-                                             void* stream) {
+                                             const kd_linear* wo, int32_t n_head, const float* q_gain,
+                                             const float* k_gain, float eps, const kd_tensor* mask,
+                                             const int32_t* kv_len, kd_tensor* y, void* stream) {
     if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
     DeviceGuard g(ctx->device);
-    return cross_attention_block_core(ctx, x_query, x_kv, wq, wk, wv, wo, q_gain, k_gain, eps, mask, kv_len, y,
-                                      static_cast<cudaStream_t>(stream));
+    return cross_attention_block_core(ctx, x_query, x_kv, wq, wk, wv, wo, n_head, q_gain, k_gain, eps, mask, kv_len,
+                                      y, static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_flash_ext(kd_attn_ctx* ctx, const kd_tensor* q, const kd_tensor* k, const kd_tensor* v,
@@ -1776,9 +1789,9 @@ kd_attn_status sharded_core(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_te
 // out_layer order of crossdit.hpp:150-153.  Scratch: [Q][K][V operands][GEMM work].
 kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                                  const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                                 const float* q_gain, const float* k_gain, float eps,
-                                                 const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
-                                                 cudaStream_t st) {
+                                                 int32_t n_head_local, const float* q_gain, const float* k_gain,
+                                                 float eps, const kd_rope3d* rope, kd_tensor* attn_full,
+                                                 kd_tensor* y, cudaStream_t st) {
     kd_attn_status rc;
     GemmInput in;
     if ((rc = gemm_input(ctx, x, &in))) return rc;
@@ -1786,16 +1799,20 @@ kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tens
     if ((rc = check_tensor(ctx, attn_full, "attn_full"))) return rc;
     const int R = ctx->n_ranks;
     const int64_t Cl = wq->ne[1], C = Cl * R, L = in.L, N = in.N;
-    if (Cl % kHeadDim || wk->ne[1] != Cl || wv->ne[1] != Cl || wo->ne[0] != C)
+    if (wk->ne[1] != Cl || wv->ne[1] != Cl || wo->ne[0] != C)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT,
-                    "wq/wk/wv must be this rank's n_head_local * 128 output features and wo take all n_ranks of them");
+                    "wq/wk/wv must be this rank's n_head_local * D output features and wo take all n_ranks of them");
+    const int64_t D = n_head_local > 0 ? Cl / n_head_local : 0;
+    if (n_head_local <= 0 || (D != kHeadDim && D != kHeadDim64) || (int64_t)n_head_local * D != Cl)
+        return fail(ctx, KD_ATTN_ERR_UNSUPPORTED, "C_local = %lld over %d heads is not a head dim of 128 or 64",
+                    (long long)Cl, n_head_local);
     if (attn_full->type != KD_ATTN_TYPE_BF16 || attn_full->ne[0] != C || attn_full->ne[1] != L ||
         attn_full->ne[2] != N || attn_full->ne[3] != 1 || attn_full->nb[0] != 2 ||
         attn_full->nb[1] != 2 * (size_t)C || attn_full->nb[2] != attn_full->nb[1] * (size_t)L)
         return fail(ctx, KD_ATTN_ERR_INVALID_ARGUMENT, "attn_full must be a contiguous bf16 [n_ranks * C_local, L, N]");
-    const int32_t Hl = (int32_t)(Cl / kHeadDim);
+    const int32_t Hl = n_head_local;
     const int32_t op = KD_ATTN_TYPE_BF16;
-    const size_t opb = align256((size_t)N * Hl * L * kHeadDim * 2);
+    const size_t opb = align256((size_t)N * Hl * L * D * 2);
     const bool rot = rope != nullptr;
     GemmInput attn_in = in;  // the out-projection reads attn_full in place
     attn_in.x = attn_full;
@@ -1804,9 +1821,9 @@ kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tens
     const size_t work = std::max(gemm_work_bytes(in, 3, Cl, rot), gemm_work_bytes(attn_in, 1, wo->ne[1], false));
     if ((rc = ensure_scratch(ctx, 3 * opb + work, st))) return rc;
     char* base = static_cast<char*>(ctx->scratch);
-    kd_tensor Qs = operand_view(base, op, L, Hl, N);
-    kd_tensor Ks = operand_view(base + opb, op, L, Hl, N);
-    kd_tensor Vs = operand_view(base + 2 * opb, op, L, Hl, N);
+    kd_tensor Qs = operand_view(base, op, L, Hl, N, D);
+    kd_tensor Ks = operand_view(base + opb, op, L, Hl, N, D);
+    kd_tensor Vs = operand_view(base + 2 * opb, op, L, Hl, N, D);
     char* gw = base + 3 * opb;
     const kd_linear* w3[3] = {wq, wk, wv};
     kd_tensor* o3[3] = {&Qs, &Ks, &Vs};
@@ -1826,9 +1843,9 @@ kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tens
     cols.data = static_cast<char*>(attn_full->data) + (size_t)ctx->rank * Cl * 2;
     cols.ne[0] = Cl;
     kd_tensor ov;
-    if ((rc = out_view(ctx, &cols, Hl, L, N, &ov))) return rc;
+    if ((rc = out_view(ctx, &cols, Hl, L, N, &ov, D))) return rc;
     if ((rc = rank_barrier(ctx, st))) return rc;  // nobody still reads the previous contents of its copy
-    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)kHeadDim), nullptr, &ov, nullptr};
+    FlashArgs fa{&Qs, &Ks, &Vs, nullptr, 1.0f / std::sqrt((float)D), nullptr, &ov, nullptr};
     fa.out_base = sbase;
     fa.peer_base = peers;
     fa.n_peers = np;
@@ -1843,13 +1860,13 @@ extern "C" {
 
 kd_attn_status kd_attn_self_attention_block_sharded(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                                     const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
-                                                    const float* q_gain, const float* k_gain, float eps,
-                                                    const kd_rope3d* rope, kd_tensor* attn_full, kd_tensor* y,
-                                                    void* stream) {
+                                                    int32_t n_head_local, const float* q_gain, const float* k_gain,
+                                                    float eps, const kd_rope3d* rope, kd_tensor* attn_full,
+                                                    kd_tensor* y, void* stream) {
     if (!ctx) return KD_ATTN_ERR_INVALID_ARGUMENT;
     DeviceGuard g(ctx->device);
-    return self_attention_block_sharded_core(ctx, x, wq, wk, wv, wo, q_gain, k_gain, eps, rope, attn_full, y,
-                                             static_cast<cudaStream_t>(stream));
+    return self_attention_block_sharded_core(ctx, x, wq, wk, wv, wo, n_head_local, q_gain, k_gain, eps, rope,
+                                             attn_full, y, static_cast<cudaStream_t>(stream));
 }
 
 kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor* q_in, const kd_tensor* k_in,

@@ -14,12 +14,12 @@
 //   kd::dit_self_attention        src/models/crossdit.hpp:132-150 (DiTSelfAttention::forward
 //                                 between the Q/K/V Linears and out_layer)
 //   kd::dit_cross_attention       src/models/crossdit.hpp:186-198 (DiTCrossAttention::forward)
-//   kd::CrossDiTAttentionConfig   src/models/crossdit.hpp:67-75 (pro_video constants used here)
+//   kd::CrossDiTAttentionConfig   src/models/crossdit.hpp:48-56,67-75 (lite_video / pro_video constants used here)
 //
 // Errors: like ops::attention (which logs LOG_ERROR and returns nullptr on an invalid GQA
 // ratio, ops.hpp:136-139) these return false and report through the library's log callback;
 // kd::Context::last_error() holds the text.  There is no fallback: a shape the kernels do not
-// cover (head_dim != 128, the causal / non-flash branch) returns false with the reason.
+// cover (head_dim other than 128 or 64, the causal / non-flash branch) returns false with the reason.
 //
 // Header-only; link libkd_attn.so.  No CUDA headers are needed: streams are passed as void*.
 #pragma once
@@ -71,8 +71,9 @@ struct Tensor {
     }
 };
 
-// The constants of CrossDiTConfig::pro_video that this path reads (crossdit.hpp:67-75,
-// rope.hpp:60): head_dim 128 = 32 + 48 + 48 rotary dims, theta 1e4, RMSNorm eps 1e-6.
+// The constants of a CrossDiTConfig that this path reads (crossdit.hpp:48-56,67-75, rope.hpp:60):
+// pro_video (and lite_image) head_dim 128 = 32 + 48 + 48 rotary dims; lite_video head_dim 64 =
+// 16 + 24 + 24; scale_factor {1, 2, 2}, theta 1e4, RMSNorm eps 1e-6.
 struct CrossDiTAttentionConfig {
     int32_t head_dim = 128;
     int32_t axes_dims[3] = {32, 48, 48};
@@ -82,6 +83,15 @@ struct CrossDiTAttentionConfig {
     int32_t op_type = KD_ATTN_TYPE_BF16;  // operand type of the flash kernel (ggml: f16)
 
     static CrossDiTAttentionConfig pro_video() { return CrossDiTAttentionConfig{}; }
+    static CrossDiTAttentionConfig lite_video() {
+        CrossDiTAttentionConfig c;
+        c.head_dim = 64;
+        c.axes_dims[0] = 16;
+        c.axes_dims[1] = 24;
+        c.axes_dims[2] = 24;
+        return c;
+    }
+    bool supported() const { return head_dim == 128 || head_dim == 64; }
 };
 
 // A Linear layer's parameters as Linear::init_params allocates them (module.hpp:97-103): the weight, ggml
@@ -175,7 +185,7 @@ inline bool dit_self_attention_block(Context& ctx, const Tensor& x, const Linear
                                      const Linear& to_value, const Linear& out_layer, const float* query_norm_w,
                                      const float* key_norm_w, const int32_t grid[3],
                                      const CrossDiTAttentionConfig& cfg, Tensor& y, void* stream = nullptr) {
-    if (!ctx.ok() || cfg.head_dim != 128) return false;
+    if (!ctx.ok() || !cfg.supported() || to_query.out_features % cfg.head_dim) return false;
     kd_rope3d rope{};
     for (int a = 0; a < 3; ++a) {
         rope.axes_dim[a] = cfg.axes_dims[a];
@@ -186,8 +196,9 @@ inline bool dit_self_attention_block(Context& ctx, const Tensor& x, const Linear
     const kd_tensor tx = x.view();
     const kd_linear wq = to_query.view(), wk = to_key.view(), wv = to_value.view(), wo = out_layer.view();
     kd_tensor ty = y.view();
-    return kd_attn_self_attention_block(ctx.get(), &tx, &wq, &wk, &wv, &wo, query_norm_w, key_norm_w, cfg.norm_eps,
-                                        &rope, &ty, stream) == KD_ATTN_OK;
+    const int32_t n_head = (int32_t)(to_query.out_features / cfg.head_dim);
+    return kd_attn_self_attention_block(ctx.get(), &tx, &wq, &wk, &wv, &wo, n_head, query_norm_w, key_norm_w,
+                                        cfg.norm_eps, &rope, &ty, stream) == KD_ATTN_OK;
 }
 
 // DiTCrossAttention::forward (crossdit.hpp:174-200) whole: x_query [C, Lq, N] visual and x_kv [C, Lk, N]
@@ -198,24 +209,25 @@ inline bool dit_cross_attention_block(Context& ctx, const Tensor& x_query, const
                                       const float* query_norm_w, const float* key_norm_w, const int32_t* kv_len,
                                       const Tensor* mask, const CrossDiTAttentionConfig& cfg, Tensor& y,
                                       void* stream = nullptr) {
-    if (!ctx.ok() || cfg.head_dim != 128) return false;
+    if (!ctx.ok() || !cfg.supported() || to_query.out_features % cfg.head_dim) return false;
     const kd_tensor tq = x_query.view(), tkv = x_kv.view();
     const kd_linear wq = to_query.view(), wk = to_key.view(), wv = to_value.view(), wo = out_layer.view();
     kd_tensor tm{};
     if (mask) tm = mask->view();
     kd_tensor ty = y.view();
-    return kd_attn_cross_attention_block(ctx.get(), &tq, &tkv, &wq, &wk, &wv, &wo, query_norm_w, key_norm_w,
+    const int32_t n_head = (int32_t)(to_query.out_features / cfg.head_dim);
+    return kd_attn_cross_attention_block(ctx.get(), &tq, &tkv, &wq, &wk, &wv, &wo, n_head, query_norm_w, key_norm_w,
                                          cfg.norm_eps, mask ? &tm : nullptr, kv_len, &ty, stream) == KD_ATTN_OK;
 }
 
 // DiTSelfAttention::forward from the Q/K/V projections to the input of out_layer
 // (crossdit.hpp:132-150): per-head RMSNorm of Q and K with the query_norm / key_norm weights
-// (device f32 [128], or nullptr for unit gain), 3D RoPE over the (frames, height, width) token
+// (device f32 [head_dim], or nullptr for unit gain), 3D RoPE over the (frames, height, width) token
 // grid with the config's axes and scale factors, flash attention.  q, k, v, out: [C, L, N].
 inline bool dit_self_attention(Context& ctx, const Tensor& q, const Tensor& k, const Tensor& v, int64_t n_head,
                                const float* query_norm_w, const float* key_norm_w, const int32_t grid[3],
                                const CrossDiTAttentionConfig& cfg, Tensor& out, void* stream = nullptr) {
-    if (!ctx.ok() || cfg.head_dim != 128 || n_head <= 0 || n_head > INT32_MAX) return false;
+    if (!ctx.ok() || !cfg.supported() || n_head <= 0 || n_head > INT32_MAX) return false;
     kd_rope3d rope{};
     for (int a = 0; a < 3; ++a) {
         rope.axes_dim[a] = cfg.axes_dims[a];
@@ -236,7 +248,7 @@ inline bool dit_cross_attention(Context& ctx, const Tensor& q, const Tensor& k, 
                                 const float* query_norm_w, const float* key_norm_w, const int32_t* kv_len,
                                 const Tensor* mask, const CrossDiTAttentionConfig& cfg, Tensor& out,
                                 void* stream = nullptr) {
-    if (!ctx.ok() || cfg.head_dim != 128 || n_head <= 0 || n_head > INT32_MAX) return false;
+    if (!ctx.ok() || !cfg.supported() || n_head <= 0 || n_head > INT32_MAX) return false;
     const kd_tensor tq = q.view(), tk = k.view(), tv = v.view();
     kd_tensor to = out.view();
     kd_tensor tm{};

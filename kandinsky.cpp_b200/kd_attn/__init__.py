@@ -159,12 +159,13 @@ def _load():
     L.kd_attn_qkv_projection.restype = st
     L.kd_attn_linear.argtypes = [P, T, W, T, P]
     L.kd_attn_linear.restype = st
-    L.kd_attn_self_attention_block.argtypes = [P, T, W, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D), T, P]
+    L.kd_attn_self_attention_block.argtypes = [P, T, W, W, W, W, ctypes.c_int32, P, P, ctypes.c_float,
+                                               ctypes.POINTER(Rope3D), T, P]
     L.kd_attn_self_attention_block.restype = st
-    L.kd_attn_cross_attention_block.argtypes = [P, T, T, W, W, W, W, P, P, ctypes.c_float, T, P, T, P]
+    L.kd_attn_cross_attention_block.argtypes = [P, T, T, W, W, W, W, ctypes.c_int32, P, P, ctypes.c_float, T, P, T, P]
     L.kd_attn_cross_attention_block.restype = st
-    L.kd_attn_self_attention_block_sharded.argtypes = [P, T, W, W, W, W, P, P, ctypes.c_float, ctypes.POINTER(Rope3D),
-                                                       T, T, P]
+    L.kd_attn_self_attention_block_sharded.argtypes = [P, T, W, W, W, W, ctypes.c_int32, P, P, ctypes.c_float,
+                                                       ctypes.POINTER(Rope3D), T, T, P]
     L.kd_attn_self_attention_block_sharded.restype = st
     L.kd_attn_flash_ext.argtypes = [P, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, T, P, P]
     L.kd_attn_flash_ext.restype = st
@@ -367,22 +368,24 @@ class Context:
         self.check(lib.kd_attn_linear(self.handle, _ref(x), ctypes.byref(w), _ref(y), _stream_ptr(stream)))
         return y
 
-    def self_attention_block(self, x, wq, wk, wv, wo, y, q_gain=None, k_gain=None, eps=1e-6, rope=None,
+    def self_attention_block(self, x, wq, wk, wv, wo, n_head, y, q_gain=None, k_gain=None, eps=1e-6, rope=None,
                              stream=None):
-        """DiTSelfAttention::forward from the hidden states x (N, L, C) f32 to y (N, L, C_out)."""
+        """DiTSelfAttention::forward from the hidden states x (N, L, C) f32 to y (N, L, C_out); n_head heads of
+        C / n_head = 128 or 64."""
         self.check(lib.kd_attn_self_attention_block(self.handle, _ref(x), ctypes.byref(wq), ctypes.byref(wk),
-                                                    ctypes.byref(wv), ctypes.byref(wo), _ptr(q_gain), _ptr(k_gain),
+                                                    ctypes.byref(wv), ctypes.byref(wo), int(n_head), _ptr(q_gain),
+                                                    _ptr(k_gain),
                                                     float(eps), None if rope is None else ctypes.byref(rope), _ref(y),
                                                     _stream_ptr(stream)))
         return y
 
-    def cross_attention_block(self, x_query, x_kv, wq, wk, wv, wo, y, q_gain=None, k_gain=None, eps=1e-6,
+    def cross_attention_block(self, x_query, x_kv, wq, wk, wv, wo, n_head, y, q_gain=None, k_gain=None, eps=1e-6,
                               mask=None, kv_len=None, stream=None):
         """DiTCrossAttention::forward: x_query (N, Lq, C) f32 visual, x_kv (N, Lk, C) f32 text -> y (N, Lq, C_out);
         kv_len: device int32 (N,) valid text lengths, mask: f16 (mn, mh, >=Lq, >=Lk), either may be None."""
         self.check(lib.kd_attn_cross_attention_block(self.handle, _ref(x_query), _ref(x_kv), ctypes.byref(wq),
                                                      ctypes.byref(wk), ctypes.byref(wv), ctypes.byref(wo),
-                                                     _ptr(q_gain), _ptr(k_gain), float(eps), _ref(mask),
+                                                     int(n_head), _ptr(q_gain), _ptr(k_gain), float(eps), _ref(mask),
                                                      _ptr(kv_len), _ref(y), _stream_ptr(stream)))
         return y
 
@@ -471,12 +474,14 @@ class Context:
                                                       _ref(out_full), _stream_ptr(stream)))
         return out_full
 
-    def self_attention_block_sharded(self, x, wq, wk, wv, wo, attn_full, y, q_gain=None, k_gain=None, eps=1e-6,
-                                     rope=None, stream=None):
+    def self_attention_block_sharded(self, x, wq, wk, wv, wo, n_head_local, attn_full, y, q_gain=None, k_gain=None,
+                                     eps=1e-6, rope=None, stream=None):
         """Heads sharded over the group: x (N, L, C) f32 replicated, this rank's Q/K/V weight shards (KdLinear,
-        C_local outputs), the full wo; attn_full a symmetric bf16 (N, L, n_ranks*C_local); y (N, L, C_out)."""
+        C_local = n_head_local * d outputs), the full wo; attn_full a symmetric bf16 (N, L, n_ranks*C_local);
+        y (N, L, C_out)."""
         self.check(lib.kd_attn_self_attention_block_sharded(self.handle, _ref(x), ctypes.byref(wq), ctypes.byref(wk),
-                                                            ctypes.byref(wv), ctypes.byref(wo), _ptr(q_gain),
+                                                            ctypes.byref(wv), ctypes.byref(wo), int(n_head_local),
+                                                            _ptr(q_gain),
                                                             _ptr(k_gain), float(eps),
                                                             None if rope is None else ctypes.byref(rope),
                                                             _ref(attn_full), _ref(y), _stream_ptr(stream)))

@@ -80,10 +80,10 @@ kd_attn_status kd_attn_self_attention(kd_attn_ctx*, const kd_tensor* q, const kd
 static kd_linear g_block_w[4];
 static kd_tensor g_block_x, g_block_y;
 kd_attn_status kd_attn_self_attention_block(kd_attn_ctx*, const kd_tensor* x, const kd_linear* wq, const kd_linear* wk,
-                                            const kd_linear* wv, const kd_linear* wo, const float* qg, const float* kg,
-                                            float, const kd_rope3d* rope, kd_tensor* y, void*) {
+                                            const kd_linear* wv, const kd_linear* wo, int32_t n_head, const float* qg,
+                                            const float* kg, float, const kd_rope3d* rope, kd_tensor* y, void*) {
     Call c;
-    c.fn = "self_attention_block"; c.qg = qg; c.kg = kg; c.rope = rope;
+    c.fn = "self_attention_block"; c.n_head = n_head; c.qg = qg; c.kg = kg; c.rope = rope;
     g_block_x = *x; g_block_y = *y;
     g_block_w[0] = *wq; g_block_w[1] = *wk; g_block_w[2] = *wv; g_block_w[3] = *wo;
     g_calls.push_back(c);
@@ -140,7 +140,8 @@ int main() {
 
     // 2. build-time support test
     CHECK(kd_bridge::supports_attention(&q, &k, &v, H, nullptr));
-    CHECK(!kd_bridge::supports_attention(&q, &k, &v, 64, nullptr));       // head_dim 64
+    CHECK(kd_bridge::supports_attention(&q, &k, &v, 64, nullptr));        // head_dim 64 (the lite video model)
+    CHECK(!kd_bridge::supports_attention(&q, &k, &v, 16, nullptr));       // head_dim 256
     ggml_tensor kg = make(GGML_TYPE_F32, 1024, L, N, 0x200000), vg = make(GGML_TYPE_F32, 1024, L, N, 0x300000);
     CHECK(kd_bridge::supports_attention(&q, &kg, &vg, H, nullptr));       // GQA 32 : 8
     ggml_tensor qh = make(GGML_TYPE_F16, C, L, N, 0x100000);
@@ -160,7 +161,7 @@ int main() {
     kd_bridge::state().ctx = fake_ctx;
     CHECK(ops_kd::attention(&gctx, nullptr, &q, &k, &v, H, nullptr, false) == &g_reference_result);
     CHECK(ops_kd::attention(&gctx, nullptr, &q, &k, &v, H, nullptr, true, true) == &g_reference_result);
-    CHECK(ops_kd::attention(&gctx, nullptr, &q, &k, &v, 64, nullptr, true) == &g_reference_result);
+    CHECK(ops_kd::attention(&gctx, nullptr, &q, &k, &v, 16, nullptr, true) == &g_reference_result);
     CHECK(g_reference_calls == 4 && g_nodes.empty());
 
     // 4. supported flash call: one custom node; its callback calls kd_attn_attention on the mapping
@@ -226,7 +227,7 @@ int main() {
         CHECK(g_block_w[0].type == KD_ATTN_TYPE_Q8_0 && g_block_w[3].type == KD_ATTN_TYPE_Q4_0);
         CHECK(g_block_w[1].data == w[1].data && g_block_w[1].nb1 == w[1].nb[1] && g_block_w[1].ne[0] == C);
         CHECK(g_block_w[0].bias == b[0].data && g_block_w[2].bias == nullptr);
-        CHECK(g_calls[0].qg == gains[0] && g_calls[0].rope == &prm.rope);
+        CHECK(g_calls[0].qg == gains[0] && g_calls[0].rope == &prm.rope && g_calls[0].n_head == prm.n_head);
         ggml_tensor bad = w[1];
         bad.type = (enum ggml_type)3;  // q4_1: not a type the GEMM expands
         ggml_tensor* wbad[4] = {&w[0], &bad, &w[2], &w[3]};

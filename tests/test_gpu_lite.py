@@ -242,3 +242,59 @@ def test_lite_projection_feeds_flash(ctx, kd):
     exact = oracle.flash_attn_ext(q, oracle.to_type(k, oracle.BF16), oracle.to_type(v, oracle.BF16),
                                   mode=oracle.EXACT)
     assert_gates(out.cpu().numpy(), exact, label="lite projection -> flash")
+
+
+# ------------------------------------------------------------------ whole lite attention modules
+def test_lite_self_attention_block_matches_oracle(ctx, kd):
+    """DiTSelfAttention::forward of the lite video model (crossdit.hpp:117-154 with num_heads 28 of 64):
+    q8_0 Q/K/V weights with biases, RMSNorm gains over 64-wide heads, the {16, 24, 24} RoPE, q4_0
+    out-projection; against the oracle's linear -> RMSNorm -> RoPE -> flash_attn_ext -> linear chain.  The
+    same hidden states with n_head 14 (head dim 128) are rejected by the RoPE's width."""
+    from test_gpu_projection import make_weight
+    from test_gpu_projection import dev as pdev
+    N, grid, H = 1, (2, 8, 16), 28
+    C, L = H * D, int(np.prod(grid))
+    x = seeded((N, L, C), 171, 0)
+    lin = [make_weight(kd, 172, 10 * i, C, C, kd.Q8_0) for i in range(3)]
+    lo, keep_o, deq_o, b_o = make_weight(kd, 173, 0, C, C, kd.Q4_0)
+    q_gain = (1.0 + 0.1 * seeded((D,), 174, 0)).astype(np.float32)
+    k_gain = (1.0 + 0.1 * seeded((D,), 174, 1)).astype(np.float32)
+    rope = kd.Rope3D.make(grid, axes=LITE_AXES, scale=LITE_SCALE)
+    y = torch.full((N, L, C), float("nan"), device="cuda")
+    ctx.self_attention_block(pdev(x), lin[0][0], lin[1][0], lin[2][0], lo, H, y, q_gain=pdev(q_gain),
+                             k_gain=pdev(k_gain), rope=rope)
+    ctx.device_status()
+    proj = [oracle.linear(x, l[2], l[3]).astype(np.float32) for l in lin]
+    attn = oracle.self_attention(*proj, H, q_gain=q_gain, k_gain=k_gain,
+                                 rope_table=oracle.visual_rope_table(grid, axes=LITE_AXES, scale=LITE_SCALE),
+                                 kv_type=oracle.BF16, q_type=oracle.BF16, mode=oracle.EXACT)
+    ref = oracle.linear(attn, deq_o, b_o)
+    m = oracle.parity_metrics(y.cpu().numpy(), ref)
+    assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m
+    with pytest.raises(kd.KdAttnError) as e:
+        ctx.self_attention_block(pdev(x), lin[0][0], lin[1][0], lin[2][0], lo, H // 2, y, rope=rope)
+    assert e.value.status == kd.ERR_INVALID_ARGUMENT
+    ctx.device_status()
+
+
+def test_lite_cross_attention_block_matches_oracle(ctx, kd):
+    """DiTCrossAttention::forward of the lite video model: visual queries against text states with valid
+    lengths, q4_0 weights, 28 heads of 64, RMSNorm on Q and K, no RoPE."""
+    from test_gpu_projection import make_weight
+    from test_gpu_projection import dev as pdev
+    N, Lq, Lt, H = 2, 256, 77, 28
+    C = H * D
+    xq, xt = seeded((N, Lq, C), 181, 0), seeded((N, Lt, C), 181, 1)
+    lin = [make_weight(kd, 182, 10 * i, C, C, kd.Q4_0) for i in range(3)]
+    lo, keep_o, deq_o, b_o = make_weight(kd, 183, 0, C, C, kd.F16)
+    kv_len = np.array([77, 40], np.int32)
+    y = torch.full((N, Lq, C), float("nan"), device="cuda")
+    ctx.cross_attention_block(pdev(xq), pdev(xt), lin[0][0], lin[1][0], lin[2][0], lo, H, y, kv_len=pdev(kv_len))
+    ctx.device_status()
+    q = oracle.linear(xq, lin[0][2], lin[0][3]).astype(np.float32)
+    k = oracle.linear(xt, lin[1][2], lin[1][3]).astype(np.float32)
+    v = oracle.linear(xt, lin[2][2], lin[2][3]).astype(np.float32)
+    attn = oracle.self_attention(q, k, v, H, kv_type=oracle.BF16, q_type=oracle.BF16, kv_len=kv_len,
+                                 mode=oracle.EXACT)
+    m = oracle.parity_metrics(y.cpu().numpy(), oracle.linear(attn, deq_o, b_o))
+    assert m["cos"] >= 0.9999 and m["maxabs_over_rms"] <= 5e-2, m

@@ -194,12 +194,13 @@ def _rank_main_block(rank, world, port, out_dir):
         torch.cuda.synchronize()
         dist.barrier(device_ids=[rank])
         for _ in range(2):    # the second call overwrites the first in place
-            ctx.self_attention_block_sharded(x, *shard, wo, attn_full, y, q_gain=gains[0], k_gain=gains[1], rope=rope)
+            ctx.self_attention_block_sharded(x, *shard, wo, Cl // 128, attn_full, y, q_gain=gains[0], k_gain=gains[1],
+                                             rope=rope)
         ctx.device_status()
         with kd_attn.Context(device=rank) as single:
             full = [kd_attn.KdLinear.of(ws[i], kd_attn.F16, C, C, bs[i]) for i in range(4)]
             ref = torch.empty(N, L, C, device="cuda")
-            single.self_attention_block(x, *full, ref, q_gain=gains[0], k_gain=gains[1], rope=rope)
+            single.self_attention_block(x, *full, C // 128, ref, q_gain=gains[0], k_gain=gains[1], rope=rope)
             single.device_status()
         res["y"] = (y.cpu(), ref.cpu())
         ctx.symmetric_free(attn_full)

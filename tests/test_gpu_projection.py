@@ -221,7 +221,7 @@ def test_self_attention_block_matches_oracle(ctx, kd):
     q_gain = (1.0 + 0.1 * seeded((128,), 134, 0)).astype(np.float32)
     k_gain = (1.0 + 0.1 * seeded((128,), 134, 1)).astype(np.float32)
     y = torch.full((N, L, C), float("nan"), device="cuda")
-    ctx.self_attention_block(dev(x), lin[0][0], lin[1][0], lin[2][0], lo, y, q_gain=dev(q_gain),
+    ctx.self_attention_block(dev(x), lin[0][0], lin[1][0], lin[2][0], lo, H, y, q_gain=dev(q_gain),
                              k_gain=dev(k_gain), rope=kd.Rope3D.make(grid))
     ctx.device_status()
     proj = [oracle.linear(x, l[2], l[3]).astype(np.float32) for l in lin]
@@ -264,12 +264,12 @@ def test_cross_attention_block_matches_oracle(ctx, kd):
     k_gain = (1.0 + 0.1 * seeded((128,), 154, 1)).astype(np.float32)
     kv_len = np.array([77, 40], np.int32)
     y = torch.full((N, Lq, C), float("nan"), device="cuda")
-    ctx.cross_attention_block(dev(xq), dev(xt), lin[0][0], lin[1][0], lin[2][0], lo, y, q_gain=dev(q_gain),
+    ctx.cross_attention_block(dev(xq), dev(xt), lin[0][0], lin[1][0], lin[2][0], lo, H, y, q_gain=dev(q_gain),
                               k_gain=dev(k_gain), kv_len=dev(kv_len))
     mask = np.zeros((N, 1, Lq, Lt), np.float16)
     mask[1, :, :, 40:] = -np.inf
     y2 = torch.full((N, Lq, C), float("nan"), device="cuda")
-    ctx.cross_attention_block(dev(xq), dev(xt), lin[0][0], lin[1][0], lin[2][0], lo, y2, q_gain=dev(q_gain),
+    ctx.cross_attention_block(dev(xq), dev(xt), lin[0][0], lin[1][0], lin[2][0], lo, H, y2, q_gain=dev(q_gain),
                               k_gain=dev(k_gain), mask=dev(mask))
     ctx.device_status()
     q = oracle.linear(xq, lin[0][2], lin[0][3]).astype(np.float32)
@@ -294,11 +294,11 @@ def test_sharded_block_single_rank_equals_block(ctx, kd):
     lin = [make_weight(kd, 162, 10 * i, C, C, kd.Q8_0) for i in range(4)]
     rope = kd.Rope3D.make(grid)
     y = torch.empty((N, L, C), device="cuda")
-    ctx.self_attention_block(dev(x), *(l[0] for l in lin), y, rope=rope)
+    ctx.self_attention_block(dev(x), *(l[0] for l in lin), C // 128, y, rope=rope)
     attn_full = torch.empty((N, L, C), device="cuda", dtype=torch.bfloat16)
     y1 = torch.full((N, L, C), float("nan"), device="cuda")
-    ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), attn_full, y1, rope=rope)
+    ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), C // 128, attn_full, y1, rope=rope)
     ctx.device_status()
     assert torch.equal(y, y1)
     with pytest.raises(kd.KdAttnError):  # attn_full must be bf16
-        ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), attn_full.float(), y1, rope=rope)
+        ctx.self_attention_block_sharded(dev(x), *(l[0] for l in lin), C // 128, attn_full.float(), y1, rope=rope)
