@@ -455,11 +455,25 @@ def lite_video(args, ctx, kd_attn, torch, q, k, v, rope, dev, stream):
     ctx.qk_prologue(ql, kl, vl, qs, ks, vs, rope=rope_l, stream=stream)
     o4 = out.view(N, L, H, d)
     fa_ms = _timed(torch, stream, lambda: ctx.flash_attn_ext(qs, ks, vs, o4, stream=stream), args.steps, args.warmup)
+    del qs, ks, vs
+    # the whole module (DiTSelfAttention::forward of the lite model): q8_0 Q/K/V/out weights [1792, 1792]
+    # with biases, the first 1792 channels of config 1's projections as the hidden states
+    C = H * d
+    ws = [_q8_0_weight(torch, C, C, 20 + i, dev) for i in range(4)]
+    lin = [kd_attn.KdLinear.of(ws[i], kd_attn.Q8_0, C, C, torch.randn(C, device=dev) * 0.1) for i in range(4)]
+    y = torch.empty(N, L, C, device=dev)
+    block_ms = _timed(torch, stream, lambda: ctx.self_attention_block(ql, *lin, H, y, rope=rope_l, stream=stream),
+                      args.steps, args.warmup)
     ctx.device_status()
     flop = 4.0 * N * H * L * L * d
+    gemm_flop = 4 * 2.0 * N * L * C * C
     return {"workload": f"lite video self-attn B{N} L{L} H{H} d{d} bf16", "call_ms": call_ms,
             "call_tflops": flop / (call_ms * 1e-3) / 1e12, "flash_kernel_ms": fa_ms,
-            "flash_kernel_tflops": flop / (fa_ms * 1e-3) / 1e12}
+            "flash_kernel_tflops": flop / (fa_ms * 1e-3) / 1e12,
+            "self_attention_block_ms": block_ms,
+            "self_attention_block": "kd_attn_self_attention_block, n_head 28: x f32 [1792, L, N] -> q8_0 QKV "
+                                    "projection -> flash -> q8_0 out-projection -> y f32",
+            "self_attention_block_tflops": (flop + gemm_flop) / (block_ms * 1e-3) / 1e12}
 
 
 def _q8_0_weight(torch, rows, cols, seed, dev):
