@@ -415,8 +415,10 @@ kd_attn_status kd_attn_self_attention_sharded(kd_attn_ctx* ctx, const kd_tensor*
  * full out_layer weight wo [n_ranks*C_local, C_out]; n_head_local = C_local / d.  The projection and
  * attention of its heads run locally, the flash epilogue stores its heads into every rank's attn_full (bf16
  * [n_ranks*C_local, L, N], contiguous, inside a kd_attn_symmetric_alloc buffer), and after the closing
- * barrier each rank applies out_layer to the gathered output: y [C_out, L, N] on every rank.
- * Collective (two barriers on the communicator). */
+ * barrier out_layer runs on the gathered output: y [C_out, L, N] on every rank.  When y is contiguous
+ * and inside a kd_attn_symmetric_alloc buffer, rank r computes token rows [r*M/n, (r+1)*M/n) of y
+ * (M = L*N) and copies them into every other rank's y (a third barrier closes the call); otherwise
+ * every rank computes all rows.  Collective (two or three barriers on the communicator). */
 kd_attn_status kd_attn_self_attention_block_sharded(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* wq,
                                                     const kd_linear* wk, const kd_linear* wv, const kd_linear* wo,
                                                     int32_t n_head_local, const float* q_gain, const float* k_gain,

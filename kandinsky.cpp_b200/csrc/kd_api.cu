@@ -1231,6 +1231,7 @@ kd_attn_status qkv_projection_core(kd_attn_ctx* ctx, const kd_tensor* x, const k
 
 // ops::linear (ops.hpp:27-42): y = x W^T + b.  x [K, L, N] f32 or bf16, y [C, L, N] f32 / bf16 / f16 with
 // contiguous, 16-byte-aligned rows.  `work` = NULL: the context's scratch.
+// ops::linear on the projection GEMM.
 kd_attn_status linear_core(kd_attn_ctx* ctx, const kd_tensor* x, const kd_linear* w, kd_tensor* y, cudaStream_t st,
                            char* work = nullptr) {
     kd_attn_status rc;
@@ -1851,7 +1852,36 @@ kd_attn_status self_attention_block_sharded_core(kd_attn_ctx* ctx, const kd_tens
     fa.n_peers = np;
     if ((rc = flash_run(ctx, fa, st))) return rc;
     if ((rc = rank_barrier(ctx, st))) return rc;  // every rank's heads have landed in every copy
-    return linear_core(ctx, attn_full, wo, y, st, gw);
+    // The out-projection.  y in a symmetric buffer (contiguous rows): rank r computes token rows
+    // [r*M/R, (r+1)*M/R) of y = out_layer(attn_full), the copy engines put that block into every other
+    // rank's copy, and a barrier closes the call; otherwise every rank computes all rows.  (Storing the
+    // rows to the peers from the GEMM epilogue -- 16 bytes per lane to 32 rows per instruction -- made the
+    // 2-GPU block slower than computing every row on every rank: 20.3 vs 19.2 ms.)
+    if ((rc = check_tensor(ctx, y, "y"))) return rc;
+    const size_t ye = elt_size(y->type);
+    const int64_t Co = wo->ne[1], M = L * N;
+    kd_attn_ctx::SymBuf* yb = nullptr;
+    if (R > 1 && y->ne[0] == Co && y->ne[1] == L && y->ne[2] == N && y->ne[3] == 1 && y->nb[0] == ye &&
+        y->nb[1] == (size_t)Co * ye && y->nb[2] == y->nb[1] * (size_t)L && M > 0)
+        yb = find_sym(ctx, y->data, y->nb[1] * (size_t)M);
+    if (!yb) return linear_core(ctx, attn_full, wo, y, st, gw);
+    const int64_t m0 = M * ctx->rank / R, m1 = M * (ctx->rank + 1) / R;
+    kd_tensor xs = *attn_full, ys = *y;  // [C, M, 1] and [C_out, M, 1] views, rows [m0, m1)
+    xs.data = static_cast<char*>(attn_full->data) + (size_t)m0 * attn_full->nb[1];
+    ys.data = static_cast<char*>(y->data) + (size_t)m0 * y->nb[1];
+    xs.ne[1] = ys.ne[1] = m1 - m0;
+    xs.ne[2] = ys.ne[2] = 1;
+    xs.nb[2] = xs.nb[3] = attn_full->nb[1] * (size_t)(m1 - m0);
+    ys.nb[2] = ys.nb[3] = y->nb[1] * (size_t)(m1 - m0);
+    if (m1 > m0) {
+        if ((rc = linear_core(ctx, &xs, wo, &ys, st, gw))) return rc;
+        // this rank's rows, one contiguous block, into every other rank's copy by the copy engines
+        const size_t off = static_cast<char*>(ys.data) - yb->local, bytes = y->nb[1] * (size_t)(m1 - m0);
+        for (int i = 0; i < R; ++i)
+            if (i != ctx->rank)
+                KD_CUDA(ctx, cudaMemcpyAsync(yb->peer[i] + off, ys.data, bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    return rank_barrier(ctx, st);  // every rank's rows of y have landed in every copy
 }
 
 }  // namespace

@@ -197,12 +197,24 @@ def _rank_main_block(rank, world, port, out_dir):
             ctx.self_attention_block_sharded(x, *shard, wo, Cl // 128, attn_full, y, q_gain=gains[0], k_gain=gains[1],
                                              rope=rope)
         ctx.device_status()
+        # y in a symmetric buffer: each rank computes its half of the token rows of the out-projection and
+        # stores them into both copies of y
+        ys = ctx.symmetric_tensor((N, L, C), torch.float32)
+        ys.fill_(float("nan"))
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+        for _ in range(2):
+            ctx.self_attention_block_sharded(x, *shard, wo, Cl // 128, attn_full, ys, q_gain=gains[0],
+                                             k_gain=gains[1], rope=rope)
+        ctx.device_status()
         with kd_attn.Context(device=rank) as single:
             full = [kd_attn.KdLinear.of(ws[i], kd_attn.F16, C, C, bs[i]) for i in range(4)]
             ref = torch.empty(N, L, C, device="cuda")
             single.self_attention_block(x, *full, C // 128, ref, q_gain=gains[0], k_gain=gains[1], rope=rope)
             single.device_status()
         res["y"] = (y.cpu(), ref.cpu())
+        res["y_row_sharded"] = ys.cpu()
+        ctx.symmetric_free(ys)
         ctx.symmetric_free(attn_full)
     torch.save(res, os.path.join(out_dir, f"block_r{rank}.pt"))
     dist.barrier(device_ids=[rank])
@@ -211,8 +223,9 @@ def _rank_main_block(rank, world, port, out_dir):
 
 def test_two_gpu_sharded_block_matches_single_gpu(tmp_path):
     """kd_attn_self_attention_block_sharded: each rank projects and attends its heads from its weight
-    shards, the exchange fills every rank's attn_full, every rank applies out_layer; each rank's y must
-    equal the single-GPU kd_attn_self_attention_block bit for bit."""
+    shards, the exchange fills every rank's attn_full, and out_layer runs either on every rank (y a plain
+    buffer) or on each rank's half of the token rows with the rows stored into both copies (y symmetric);
+    each rank's y must equal the single-GPU kd_attn_self_attention_block bit for bit both ways."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -220,6 +233,8 @@ def test_two_gpu_sharded_block_matches_single_gpu(tmp_path):
     mp.start_processes(_rank_main_block, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")
     for r in range(2):
-        got, ref = torch.load(os.path.join(str(tmp_path), f"block_r{r}.pt"))["y"]
+        saved = torch.load(os.path.join(str(tmp_path), f"block_r{r}.pt"))
+        got, ref = saved["y"]
         assert torch.isfinite(got).all()
         assert torch.equal(got, ref)
+        assert torch.equal(saved["y_row_sharded"], ref)
