@@ -22,10 +22,9 @@ def _sample_rows(L, n, seed):
 
 
 def _oracle_head_rows(q_in, k_in, v_in, n, h, rows, table, kv_type, mask_row=None, kv_len=None, table_q=None,
-                      table_k=None):
+                      table_k=None, d=128):
     """fp64 oracle for query rows `rows` of head h, sequence n (prologue + flash, like the GPU call).
     table_q / table_k: RoPE rows for the given q rows and all keys, when q_in holds only those rows."""
-    d = 128
     qs = q_in[n:n + 1, rows, h * d:(h + 1) * d]
     ks = k_in[n:n + 1, :, h * d:(h + 1) * d]
     vs = v_in[n:n + 1, :, h * d:(h + 1) * d]
@@ -193,3 +192,27 @@ def test_config2_full_size_cross_attention(ctx, kd, use_mask):
         ref, lref = _oracle_head_rows(q, k, v, n, h, rows, None, oracle.BF16, kv_len=int(kv_len[n]))
         got = o[n, rows, h * d:(h + 1) * d]
         assert_gates(got, ref, lse=ls[n, h, rows], lse_ref=lref, label=f"cfg2 n{n} h{h} mask={use_mask}", out_type="bf16")
+
+
+def test_lite_video_full_size_self_attention(ctx, kd):
+    """The lite video model at config 1's tokens: B2 x 31,744 tokens (31x32x32) x 28 heads x d64 (RoPE axes
+    {16, 24, 24}, scale {1, 2, 2}), bf16 operands -- the head_dim-64 long-key kernel over 248 K/V tiles per
+    plane; sampled rows of four planes, the last one (1, 27) included, against the fp64 oracle."""
+    N, L, H, d = 2, 31744, 28, 64
+    C = H * d
+    grid, axes, scale = (31, 32, 32), (16, 24, 24), (1, 2, 2)
+    q, k, v = _device_projections(ctx, N, L, C, seed=37)
+    out = torch.empty(N, L, C, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(N, H, L, device="cuda")
+    ctx.self_attention(q, k, v, H, out, rope=kd.Rope3D.make(grid, axes=axes, scale=scale), op_type=kd.BF16, lse=lse)
+    ctx.device_status()
+    assert bool(torch.isfinite(out).all()) and bool(torch.isfinite(lse).all())
+    table = oracle.visual_rope_table(grid, axes=axes, scale=scale)
+    for n, h in [(0, 0), (1, 27), (0, 13), (1, 6)]:
+        rows = _sample_rows(L, 64, seed=700 + n * 100 + h)
+        qh, kh, vh = _head_slice(q, n, h, rows, d), _head_slice(k, n, h, d=d), _head_slice(v, n, h, d=d)
+        ref, lref = _oracle_head_rows(qh, kh, vh, 0, 0, np.arange(len(rows)), None, oracle.BF16,
+                                      table_q=table[rows], table_k=table, d=d)
+        got = out[n, torch.as_tensor(rows, device="cuda"), h * d:(h + 1) * d].float().cpu().numpy()
+        assert_gates(got, ref, lse=lse[n, h].cpu().numpy()[rows], lse_ref=lref, label=f"lite n{n} h{h}",
+                     out_type="bf16")
